@@ -1,0 +1,125 @@
+/*
+ * localmoe_b200.h -- C ABI of the B200 (sm_100a) INT8 group-128 MoE matmul path.
+ *
+ * Conventions shared by every entry point:
+ *  - all tensor arguments are DEVICE pointers to contiguous row-major memory;
+ *  - weights use the converted-checkpoint layout: int8 q[.., N, K] (K fastest)
+ *    and float32 scale[.., N, K/128], one scale per 128-wide K group;
+ *    expert banks are stacked [E, N, K]; gate_up rows [0, I) are gate and
+ *    [I, 2I) are up;
+ *  - activations are bf16 (dtype LMOE_BF16) or fp16 (LMOE_F16);
+ *  - `stream` is a cudaStream_t passed as void*; work is enqueued on it with
+ *    no host synchronisation, so every call can be captured in a CUDA graph;
+ *  - no entry point allocates device memory: scratch ("workspace") buffers are
+ *    passed in by the caller, sized by the *_workspace_size functions;
+ *  - the return value is LMOE_OK or a negative LMOE_ERR_* code (invalid
+ *    geometry or a CUDA launch error); nothing aborts or traps.  Device-side
+ *    bounded waits that give up set LMOE_DEVERR_* bits in the caller's
+ *    int32 error word (`err`), which the caller may read after the stream.
+ *
+ * Each declaration names the reference interface it replaces
+ * (heliosz616/LocalMoe35Ba3b, file:line).
+ */
+#ifndef LOCALMOE_B200_H
+#define LOCALMOE_B200_H
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LMOE_API __attribute__((visibility("default")))
+#else
+#define LMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LMOE_OK 0
+#define LMOE_ERR_INVALID (-1)
+#define LMOE_ERR_CUDA (-2)
+#define LMOE_ERR_UNSUPPORTED (-3)
+
+#define LMOE_DEVERR_TIMEOUT 1
+#define LMOE_ERR_TIMEOUT LMOE_DEVERR_TIMEOUT
+
+#define LMOE_BF16 0
+#define LMOE_F16 1
+
+/* Library ABI version (increments on any signature change). */
+LMOE_API int lmoe_abi_version(void);
+
+/* Replaces w8a8.quantize / w8a8._quant (qwen35_deploy/operators/w8a8.py:8-22).
+ * Per (row, 128-group): s = max(absmax, 1e-10) * fp32(1/127), q = rint(x / s). */
+LMOE_API int lmoe_quantize_rows(const void* x, int8_t* q, float* s, int64_t rows, int64_t k, int dtype, void* stream);
+
+/* Replaces int8.linear / int8._linear (qwen35_deploy/operators/int8.py:9-37).
+ * y[m, n] = sum_k x[m, k] * round_dtype(q[n, k] * scale[n, k/128]), fp32 accumulation.
+ * Small m runs an HBM-streaming GEMV; large m a tcgen05 tensor-core GEMM. */
+LMOE_API int lmoe_linear_w8a16(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n,
+                      int64_t k, int dtype, int* err, void* stream);
+
+/* Replaces int8.grouped_linear / int8._grouped_linear (qwen35_deploy/operators/int8.py:213-237).
+ * table is a device int64 [experts, 5] of (gate_up.q, gate_up.scale, down.q, down.scale, slot);
+ * field 0 selects the gate_up pair, field 2 the down pair.  Row e uses x row 0 when
+ * shared != 0, else x row e.  y is [experts, n]. */
+LMOE_API int lmoe_grouped_linear_w8a16(const void* x, const int64_t* table, void* y, int64_t experts, int64_t n, int64_t k,
+                              int field, int shared, int dtype, void* stream);
+
+/* Replaces w8a8.grouped_linear / w8a8._linear (qwen35_deploy/operators/w8a8.py:25-48):
+ * per-(row,128) int8 activation quantisation (into xq/xs, [rows, k] and [rows, k/128])
+ * followed by per-group int32 dots, acc = acc + (float(dot) * xs) * ws in group order. */
+LMOE_API int lmoe_grouped_linear_w8a8(const void* x, const int64_t* table, void* y, int64_t experts, int64_t n, int64_t k,
+                             int field, int shared, int dtype, int8_t* xq, float* xs, void* stream);
+
+/* Replaces int8._ordered_reduce (qwen35_deploy/operators/int8.py:240-250):
+ * y[n] = ordered sum over table rows e of round(values[e, n] * weights[table[e, 4]]). */
+LMOE_API int lmoe_ordered_reduce(const void* values, const int64_t* table, const float* weights, void* y, int64_t n,
+                        int64_t experts, int dtype, void* stream);
+
+/* Replaces gpu_routes.plan / gpu_routes._table (qwen35_deploy/runtime/gpu_routes.py:17-63).
+ * Outputs (int64): pos [tokens*top], table [ceil(tokens*top/bm)+experts, 3],
+ * ordered [tokens, top], slots [tokens, top]. ws: lmoe_plan_workspace_size bytes. */
+LMOE_API int64_t lmoe_plan_workspace_size(int64_t tokens, int64_t top, int64_t experts);
+LMOE_API int lmoe_plan(const int64_t* ids, int64_t tokens, int64_t top, int64_t experts, int64_t bm, int64_t* pos,
+              int64_t* table, int64_t* ordered, int64_t* slots, void* ws, void* stream);
+
+/* Routing metadata for the fused prefill path (replaces the torch sort/searchsorted/
+ * argsort/scatter of gpu_routes.py:51-62 plus _table with this build's 256-route tiles).
+ * meta: lmoe_route_meta_size bytes.  with_shared != 0 appends a segment of `tokens`
+ * identity routes for the shared expert. */
+LMOE_API int64_t lmoe_route_meta_size(int64_t tokens, int64_t top, int64_t experts);
+LMOE_API int lmoe_route_meta(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
+                    int with_shared, void* meta, void* stream);
+
+/* Replaces prefill._routed via gpu_routes._nonempty (qwen35_deploy/runtime/prefill.py:12-34,
+ * gpu_routes.py:39-44): for every route r of expert e, y[r] = x[gather ? pos[r] : r] . W_e^T.
+ * meta comes from lmoe_route_meta (its expert segments and tiles). */
+LMOE_API int lmoe_routed_linear(const void* x, const int8_t* q, const float* scale, int64_t experts, int64_t n,
+                       int64_t k, const void* meta, int64_t tokens, int64_t top, int gather, void* y,
+                       int dtype, int* err, void* stream);
+
+/* Replaces prefill._reduce (qwen35_deploy/runtime/prefill.py:37-49): per token, ordered
+ * combine of its routes (ordered/slots as returned by lmoe_plan; weights fp32 [tokens, top]). */
+LMOE_API int lmoe_routed_reduce(const void* down, const int64_t* ordered, const int64_t* slots, const float* weights,
+                       void* y, int64_t tokens, int64_t n, int64_t top, int dtype, void* stream);
+
+/* Replaces gpu_routes.routed_moe (qwen35_deploy/runtime/gpu_routes.py:66-82) -- and, when
+ * the shared-expert arguments are non-null, the whole Qwen3_5MoeSparseMoeBlock expert part
+ * (transformers qwen3_5_moe/modeling_qwen3_5_moe.py:781-792):
+ *   out = routed(x) [+ round(sigmoid(round(x . shared_gate_w)) * shared_expert(x))]
+ *   [+ residual]
+ * Launches: route metadata, gate_up GEMM with fused SwiGLU, down GEMM with fused routing
+ * weight, ordered combine.  ws: lmoe_moe_workspace_size bytes.  stage_events (nullable)
+ * is an array of 5 cudaEvent_t recorded before/between/after the four launches. */
+LMOE_API int64_t lmoe_moe_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t hidden, int64_t inter);
+LMOE_API int lmoe_routed_moe(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
+                    const int8_t* qg, const float* sg, const int8_t* qd, const float* sd, int64_t experts,
+                    int64_t hidden, int64_t inter, const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu,
+                    const float* sh_su, const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w,
+                    const void* residual, void* out, int dtype, void* ws, int* err, void** stage_events,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LOCALMOE_B200_H */

@@ -1,0 +1,38 @@
+// Host-side launch description of the tcgen05 grouped GEMM (grouped_gemm.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "routes.cuh"
+
+namespace lmoe {
+
+enum GemmMode { kPlain = 0, kSwiGLU = 1, kWeighted = 2 };
+
+struct GemmLaunch {
+  const void* x;          // activations [rows, K]
+  int64_t K;
+  const int32_t* pos;     // gather index per route row (nullptr: the row itself)
+  const Tile* tiles;      // nullptr: dense mode over dense_rows rows
+  const int32_t* hdr;     // tiles mode: metadata header (tile count)
+  int64_t grid_tiles;     // grid.y: max tiles (tiles mode) or ceil(M/256) (dense)
+  int64_t dense_rows;
+  const int8_t* q_bank;   // routed bank [experts*N, K]
+  const float* s_bank;
+  int64_t experts, N, inter;
+  const int8_t* q_lo;     // shared expert: gate (SwiGLU) or whole matrix (plain/weighted)
+  const float* s_lo;
+  const int8_t* q_hi;     // shared expert: up (SwiGLU)
+  const float* s_hi;
+  int64_t rows_lo, rows_hi;
+  void* y;
+  int64_t ldy;
+  const float* rweight;   // weighted mode: per-route weight
+  int mode;
+  int dtype;
+  int* err;
+};
+
+int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st);
+
+}  // namespace lmoe

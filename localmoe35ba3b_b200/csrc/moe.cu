@@ -1,0 +1,211 @@
+// Prefill MoE expert block: routing metadata -> gate_up GEMM (+SwiGLU) ->
+// down GEMM (+routing weight) -> ordered combine (+ gated shared expert,
+// + optional residual).
+//
+// Replaces gpu_routes.routed_moe (qwen35_deploy/runtime/gpu_routes.py:66-82)
+// and, with the shared-expert arguments, the expert part of the HF
+// Qwen3_5MoeSparseMoeBlock.forward (transformers qwen3_5_moe/
+// modeling_qwen3_5_moe.py:781-792).  Rounding sequence kept from the
+// reference: per route v = round(round(acc) * w) (prefill.py:45), per token
+// acc = round(acc + v) over routes in ascending expert order (prefill.py:46),
+// then round(acc + round(round(sigmoid(round(x . g))) * shared)) (HF :787-790).
+#include "common.cuh"
+#include "gemm.cuh"
+#include "routes.cuh"
+
+namespace lmoe {
+
+
+
+constexpr int kCombineThreads = 256;
+
+template <int DT>
+__global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(
+    const typename Act<DT>::T* __restrict__ down, const int32_t* __restrict__ ordered, int top, int64_t H, int64_t R,
+    const typename Act<DT>::T* __restrict__ x, const typename Act<DT>::T* __restrict__ gate_w, int with_shared,
+    const typename Act<DT>::T* __restrict__ residual, typename Act<DT>::T* __restrict__ out) {
+  using A = Act<DT>;
+  __shared__ float red[kCombineThreads / 32];
+  const int64_t t = blockIdx.x;
+  float sig = 1.f;
+  if (with_shared && gate_w != nullptr) {
+    float part = 0.f;
+    for (int64_t c = threadIdx.x * 8; c < H; c += kCombineThreads * 8) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(x + t * H + c);
+      const uint4 gv = *reinterpret_cast<const uint4*>(gate_w + c);
+      const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, ga[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        part = fmaf(A::lo_f(xa[j]), A::lo_f(ga[j]), part);
+        part = fmaf(A::hi_f(xa[j]), A::hi_f(ga[j]), part);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane_id() == 0) red[warp_id()] = part;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombineThreads / 32; ++w) tot += red[w];
+    const float logit = A::round(tot);
+    sig = A::round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-logit))));
+  }
+  for (int64_t c = threadIdx.x * 8; c < H; c += kCombineThreads * 8) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int i = 0; i < top; ++i) {
+      const int64_t r = ordered[t * top + i];
+      const uint4 v = *reinterpret_cast<const uint4*>(down + r * H + c);
+      const uint32_t va[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = A::round(__fadd_rn(acc[2 * j], A::lo_f(va[j])));
+        acc[2 * j + 1] = A::round(__fadd_rn(acc[2 * j + 1], A::hi_f(va[j])));
+      }
+    }
+    if (with_shared) {
+      const uint4 v = *reinterpret_cast<const uint4*>(down + (R + t) * H + c);
+      const uint32_t va[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float s0 = gate_w ? A::round(__fmul_rn(sig, A::lo_f(va[j]))) : A::lo_f(va[j]);
+        const float s1 = gate_w ? A::round(__fmul_rn(sig, A::hi_f(va[j]))) : A::hi_f(va[j]);
+        acc[2 * j] = A::round(__fadd_rn(acc[2 * j], s0));
+        acc[2 * j + 1] = A::round(__fadd_rn(acc[2 * j + 1], s1));
+      }
+    }
+    if (residual != nullptr) {
+      const uint4 v = *reinterpret_cast<const uint4*>(residual + t * H + c);
+      const uint32_t va[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = A::round(__fadd_rn(A::lo_f(va[j]), acc[2 * j]));
+        acc[2 * j + 1] = A::round(__fadd_rn(A::hi_f(va[j]), acc[2 * j + 1]));
+      }
+    }
+    uint4 o;
+    o.x = A::pack(acc[0], acc[1]);
+    o.y = A::pack(acc[2], acc[3]);
+    o.z = A::pack(acc[4], acc[5]);
+    o.w = A::pack(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + t * H + c) = o;
+  }
+}
+
+struct MoeWs {
+  int64_t off_meta, off_hidden, off_down, bytes;
+  MoeWs(int64_t T, int64_t top, int64_t E, int64_t H, int64_t I) {
+    const int64_t R = T * top;
+    const MetaLayout L(T, top, E);
+    off_meta = 0;
+    off_hidden = MetaLayout::align(L.bytes);
+    off_down = MetaLayout::align(off_hidden + (R + T) * I * 2);
+    bytes = MetaLayout::align(off_down + (R + T) * H * 2);
+  }
+};
+
+}  // namespace lmoe
+
+using namespace lmoe;
+
+int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
+                         int with_shared, void* meta, int* err, cudaStream_t st);
+
+extern "C" int64_t lmoe_moe_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t hidden,
+                                           int64_t inter) {
+  return MoeWs(tokens, top, experts, hidden, inter).bytes;
+}
+
+extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
+                               const int8_t* qg, const float* sg, const int8_t* qd, const float* sd, int64_t experts,
+                               int64_t hidden, int64_t inter, const int8_t* sh_qg, const float* sh_sg,
+                               const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd, const float* sh_sd,
+                               const void* sh_gate_w, const void* residual, void* out, int dtype, void* ws, int* err,
+                               void** stage_events, void* stream) {
+  if (!x || !weights || !ids || !qg || !sg || !qd || !sd || !out || !ws) return LMOE_ERR_INVALID;
+  if (tokens <= 0 || top <= 0 || experts <= 0 || hidden <= 0 || inter <= 0) return LMOE_ERR_INVALID;
+  if (hidden % kGroup || inter % kGroup || hidden % 8) return LMOE_ERR_INVALID;
+  if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_ERR_INVALID;
+  const bool with_shared = sh_qg != nullptr;
+  if (with_shared && (!sh_sg || !sh_qu || !sh_su || !sh_qd || !sh_sd)) return LMOE_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  const MoeWs W(tokens, top, experts, hidden, inter);
+  const MetaLayout ML(tokens, top, experts);
+  char* w = (char*)ws;
+  char* meta = w + W.off_meta;
+  void* hid = w + W.off_hidden;
+  void* dn = w + W.off_down;
+  const int64_t R = tokens * top;
+
+  // optional stage timing: events[0..4] bracket metadata, gate_up, down, combine
+  auto mark = [&](int i) -> int {
+    if (stage_events && stage_events[i]) LMOE_CUDA_CHECK(cudaEventRecord((cudaEvent_t)stage_events[i], st));
+    return LMOE_OK;
+  };
+  int rc = mark(0);
+  if (rc) return rc;
+  if ((rc = lmoe_route_meta_impl(ids, weights, tokens, top, experts, with_shared ? 1 : 0, meta, err, st))) return rc;
+  if ((rc = mark(1))) return rc;
+
+  GemmLaunch g = {};
+  g.x = x;
+  g.K = hidden;
+  g.pos = (const int32_t*)(meta + ML.off_pos);
+  g.tiles = (const Tile*)(meta + ML.off_tiles);
+  g.hdr = (const int32_t*)(meta + ML.off_hdr);
+  g.grid_tiles = ML.max_tiles;
+  g.q_bank = qg;
+  g.s_bank = sg;
+  g.experts = experts;
+  g.N = 2 * inter;
+  g.inter = inter;
+  if (with_shared) {
+    g.q_lo = sh_qg;
+    g.s_lo = sh_sg;
+    g.q_hi = sh_qu;
+    g.s_hi = sh_su;
+    g.rows_lo = inter;
+    g.rows_hi = inter;
+  }
+  g.y = hid;
+  g.ldy = inter;
+  g.mode = kSwiGLU;
+  g.dtype = dtype;
+  g.err = err;
+  if ((rc = launch_grouped_gemm(g, st))) return rc;
+  if ((rc = mark(2))) return rc;
+
+  GemmLaunch d = g;
+  d.x = hid;
+  d.K = inter;
+  d.pos = nullptr;
+  d.q_bank = qd;
+  d.s_bank = sd;
+  d.N = hidden;
+  d.inter = 0;
+  d.q_lo = with_shared ? sh_qd : nullptr;
+  d.s_lo = with_shared ? sh_sd : nullptr;
+  d.q_hi = nullptr;
+  d.s_hi = nullptr;
+  d.rows_lo = with_shared ? hidden : 0;
+  d.rows_hi = 0;
+  d.y = dn;
+  d.ldy = hidden;
+  d.rweight = (const float*)(meta + ML.off_rweight);
+  d.mode = kWeighted;
+  if ((rc = launch_grouped_gemm(d, st))) return rc;
+  if ((rc = mark(3))) return rc;
+
+  const int32_t* ordered = (const int32_t*)(meta + ML.off_ordered);
+  if (dtype == LMOE_BF16)
+    moe_combine_kernel<LMOE_BF16><<<(unsigned)tokens, kCombineThreads, 0, st>>>(
+        (const __nv_bfloat16*)dn, ordered, (int)top, hidden, R, (const __nv_bfloat16*)x,
+        (const __nv_bfloat16*)sh_gate_w, with_shared ? 1 : 0, (const __nv_bfloat16*)residual, (__nv_bfloat16*)out);
+  else
+    moe_combine_kernel<LMOE_F16><<<(unsigned)tokens, kCombineThreads, 0, st>>>(
+        (const __half*)dn, ordered, (int)top, hidden, R, (const __half*)x, (const __half*)sh_gate_w,
+        with_shared ? 1 : 0, (const __half*)residual, (__half*)out);
+  LMOE_CUDA_CHECK(cudaGetLastError());
+  return mark(4);
+}

@@ -1,0 +1,323 @@
+// GPU routing metadata: one single-CTA kernel replaces the torch stable sort,
+// searchsorted, cumsum, argsort and scatter of gpu_routes.plan and the
+// reference's _table kernel (qwen35_deploy/runtime/gpu_routes.py:17-63).
+//
+// Algorithm: a stable counting sort of the flat route ids.  The flat array is
+// cut into 32 contiguous segments, one per warp.  Pass 1 counts ids per
+// (warp, expert) in shared memory; a scan over experts, then over warps,
+// gives every (warp, expert) its first sorted slot; pass 2 walks each
+// segment in order, 32 routes at a time, ranking equal ids inside the warp
+// with __match_any_sync -- so routes of one expert keep their flat order, as
+// torch.sort(stable=True) does.  The per-token ascending-expert order
+// (argsort(dim=1, stable=True)) is an insertion sort of each token's top-k.
+#include "common.cuh"
+#include "routes.cuh"
+
+namespace lmoe {
+
+constexpr int kRouteThreads = 1024;
+constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kMaxTop = 32;
+
+// inclusive block scan over kRouteThreads values (one per thread)
+__device__ int block_incl_scan(int v, int* warp_tot) {
+  const int lane = lane_id(), warp = warp_id();
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  if (lane == 31) warp_tot[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int t = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += u;
+    }
+    warp_tot[lane] = t;
+  }
+  __syncthreads();
+  const int r = v + (warp > 0 ? warp_tot[warp - 1] : 0);
+  __syncthreads();
+  return r;
+}
+
+struct RouteArgs {
+  const int64_t* ids;
+  const float* weights;  // nullable: [T, top] fp32 routing weights
+  int T, top, E, with_shared;
+  // fused-path outputs (nullable block: hdr == nullptr)
+  int32_t* hdr;
+  int32_t* offsets;
+  Tile* tiles;
+  int32_t* pos32;
+  float* rweight;
+  int32_t* ordered32;
+  int32_t* inverse;  // scratch [R], required
+  // reference-format outputs (nullable)
+  int64_t* pos64;
+  int64_t* table64;
+  int64_t* ordered64;
+  int64_t* slots64;
+  int bm;
+  int max_tiles_ref;
+  int* err;
+};
+
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
+  extern __shared__ int cw[];  // [kRouteWarps][E+1] counts, then first slots
+  __shared__ int warp_tot[32];
+  __shared__ int s_total_tiles;
+  const int R = a.T * a.top;
+  const int E = a.E;
+  const int Es = E + (a.with_shared ? 1 : 0);  // ranked experts incl. shared
+  const int lane = lane_id(), warp = warp_id();
+  const int L = (R + kRouteWarps - 1) / kRouteWarps;
+  const int seg_lo = warp * L;
+  const int seg_hi = min(R, seg_lo + L);
+
+  for (int i = threadIdx.x; i < kRouteWarps * (E + 1); i += blockDim.x) cw[i] = 0;
+  __syncthreads();
+  // pass 1: per-warp counts (out-of-range ids are counted in bucket E and flagged)
+  for (int f = seg_lo + lane; f < seg_hi; f += 32) {
+    int64_t id = a.ids[f];
+    if (id < 0 || id >= E) {
+      raise_error(a.err, 2);
+      id = E;
+    }
+    atomicAdd(&cw[warp * (E + 1) + (int)id], 1);
+  }
+  __syncthreads();
+  // per expert: exclusive over warps, then exclusive over experts
+  int count = 0;
+  const int e = threadIdx.x;
+  if (e <= E) {
+    for (int w = 0; w < kRouteWarps; ++w) {
+      const int c = cw[w * (E + 1) + e];
+      cw[w * (E + 1) + e] = count;
+      count += c;
+    }
+  }
+  // E + 1 <= kRouteThreads is checked on the host
+  const int incl = block_incl_scan(e <= E ? count : 0, warp_tot);
+  const int first = incl - (e <= E ? count : 0);
+  if (e <= E) {
+    for (int w = 0; w < kRouteWarps; ++w) cw[w * (E + 1) + e] += first;
+    if (a.offsets != nullptr && e < E) a.offsets[e] = first;
+  }
+  if (a.offsets != nullptr && e == 0) {
+    a.offsets[E] = R;
+    a.offsets[E + 1] = R + (a.with_shared ? a.T : 0);
+  }
+  __syncthreads();
+
+  // pass 2: stable placement
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = seg_lo; base < seg_hi; base += 32) {
+    const int f = base + lane;
+    const bool valid = f < seg_hi;
+    int id = -1;
+    if (valid) {
+      const int64_t v = a.ids[f];
+      id = (v < 0 || v >= E) ? E : (int)v;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, id);
+    int dst = 0;
+    if (valid) dst = cw[warp * (E + 1) + id] + __popc(peers & lt);
+    __syncwarp();
+    if (valid) {
+      a.inverse[f] = dst;
+      const int tok = f / a.top;
+      if (a.pos32) a.pos32[dst] = tok;
+      if (a.pos64) a.pos64[dst] = tok;
+      if (a.rweight) a.rweight[dst] = a.weights ? a.weights[f] : 1.0f;
+      if (lane == 31 - __clz(peers)) cw[warp * (E + 1) + id] += __popc(peers);
+    }
+    __syncwarp();
+  }
+  if (a.pos32 && a.with_shared)
+    for (int t = threadIdx.x; t < a.T; t += blockDim.x) a.pos32[R + t] = t;
+  __syncthreads();
+
+  // per token: slots by ascending expert (stable), ordered = inverse[t*top + slot]
+  for (int t = threadIdx.x; t < a.T; t += blockDim.x) {
+    int sid[kMaxTop], sl[kMaxTop];
+    for (int i = 0; i < a.top; ++i) {
+      const int64_t v = a.ids[(int64_t)t * a.top + i];
+      const int id = (int)v;
+      int j = i;
+      while (j > 0 && sid[j - 1] > id) {  // strict: equal ids keep slot order
+        sid[j] = sid[j - 1];
+        sl[j] = sl[j - 1];
+        --j;
+      }
+      sid[j] = id;
+      sl[j] = i;
+    }
+    for (int i = 0; i < a.top; ++i) {
+      const int64_t o = (int64_t)t * a.top + i;
+      const int route = a.inverse[(int64_t)t * a.top + sl[i]];
+      if (a.ordered32) a.ordered32[o] = route;
+      if (a.ordered64) a.ordered64[o] = route;
+      if (a.slots64) a.slots64[o] = sl[i];
+    }
+  }
+
+  // counts again, per expert (from offsets held in cw row 0 + totals)
+  // cw[0][e] was advanced by warp 0's routes; recompute counts from the scan
+  // values instead: count(e) = first(e+1) - first(e).
+  __shared__ int s_first[1025];
+  if (e <= E) s_first[e] = first;
+  if (e == 0) s_first[E + 1] = R;
+  __syncthreads();
+
+  // fused-path tiles, experts ordered by descending count (ties: lower id first)
+  if (a.tiles != nullptr) {
+    int cnt = 0, ntl = 0, rank = 0;
+    if (e < Es) {
+      cnt = (e < E) ? (s_first[e + 1] - s_first[e]) : a.T;
+      ntl = (cnt + kTileRoutes - 1) / kTileRoutes;
+      for (int o = 0; o < Es; ++o) {
+        const int co = (o < E) ? (s_first[o + 1] - s_first[o]) : a.T;
+        rank += (co > cnt) || (co == cnt && o < e);
+      }
+    }
+    __shared__ int s_by_rank[1025];
+    if (e < Es) s_by_rank[rank] = ntl;
+    __syncthreads();
+    const int r_ntl = (e < Es) ? s_by_rank[e] : 0;  // thread e now holds rank e's tile count
+    const int r_incl = block_incl_scan(r_ntl, warp_tot);
+    __shared__ int s_tile_first[1025];
+    if (e < Es) s_tile_first[e] = r_incl - r_ntl;
+    if (e == Es - 1) s_total_tiles = r_incl;
+    __syncthreads();
+    if (e < Es) {
+      const int t0 = s_tile_first[rank];
+      const int start0 = (e < E) ? s_first[e] : R;
+      for (int j = 0; j < ntl; ++j) {
+        Tile tl;
+        tl.expert = e;
+        tl.start = start0 + j * kTileRoutes;
+        tl.count = min(kTileRoutes, cnt - j * kTileRoutes);
+        tl.pad = 0;
+        a.tiles[t0 + j] = tl;
+      }
+    }
+    if (threadIdx.x == 0) {
+      a.hdr[kHdrNumTiles] = s_total_tiles;
+      a.hdr[kHdrRoutes] = R;
+      a.hdr[kHdrTokens] = a.T;
+      a.hdr[kHdrExperts] = E;
+      a.hdr[kHdrShared] = a.with_shared;
+    }
+  }
+
+  // reference table: ends = cumsum(ceil(count / bm)) in expert-id order
+  if (a.table64 != nullptr) {
+    const int cnt = (e < E) ? (s_first[e + 1] - s_first[e]) : 0;
+    const int nt = (cnt + a.bm - 1) / a.bm;
+    const int ends_incl = block_incl_scan(e < E ? nt : 0, warp_tot);
+    __shared__ int s_ends[1025];
+    if (e < E) s_ends[e] = ends_incl;
+    __syncthreads();
+    const int total = s_ends[E - 1];
+    for (int tile = threadIdx.x; tile < a.max_tiles_ref; tile += blockDim.x) {
+      int64_t ex = 0, st = 0, sp = 0;
+      if (tile < total) {
+        int lo = 0, hi = E;  // first expert with ends > tile
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (s_ends[mid] <= tile) lo = mid + 1; else hi = mid;
+        }
+        ex = lo;
+        const int prior = lo > 0 ? s_ends[lo - 1] : 0;
+        st = (int64_t)s_first[lo] + (int64_t)(tile - prior) * a.bm;
+        sp = s_first[lo + 1];
+      }
+      a.table64[(int64_t)tile * 3] = ex;
+      a.table64[(int64_t)tile * 3 + 1] = st;
+      a.table64[(int64_t)tile * 3 + 2] = sp;
+    }
+  }
+}
+
+static size_t route_smem(int64_t E) { return (size_t)kRouteWarps * (E + 1) * sizeof(int); }
+
+static int launch_route(RouteArgs& a, cudaStream_t st) {
+  // static shared arrays (~16.5 KB) plus this dynamic part exceed the 48 KB
+  // default, so the opt-in limit is always raised to the dynamic size
+  const size_t smem = route_smem(a.E);
+  LMOE_CUDA_CHECK(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  route_kernel<<<1, kRouteThreads, smem, st>>>(a);
+  LMOE_CUDA_CHECK(cudaGetLastError());
+  return LMOE_OK;
+}
+
+static bool route_geometry_ok(int64_t tokens, int64_t top, int64_t experts) {
+  return tokens > 0 && top > 0 && top <= kMaxTop && experts > 0 && experts + 2 <= kRouteThreads &&
+         tokens * top < (int64_t(1) << 30) && route_smem(experts) <= 200 * 1024;
+}
+
+}  // namespace lmoe
+
+using namespace lmoe;
+
+extern "C" int64_t lmoe_plan_workspace_size(int64_t tokens, int64_t top, int64_t experts) {
+  (void)experts;
+  return MetaLayout::align(tokens * top * 4) + 256;
+}
+
+extern "C" int lmoe_plan(const int64_t* ids, int64_t tokens, int64_t top, int64_t experts, int64_t bm, int64_t* pos,
+                         int64_t* table, int64_t* ordered, int64_t* slots, void* ws, void* stream) {
+  if (!ids || !pos || !table || !ordered || !slots || !ws || bm <= 0) return LMOE_ERR_INVALID;
+  if (!route_geometry_ok(tokens, top, experts)) return LMOE_ERR_INVALID;
+  RouteArgs a = {};
+  a.ids = ids;
+  a.T = (int)tokens;
+  a.top = (int)top;
+  a.E = (int)experts;
+  a.inverse = (int32_t*)ws;
+  a.err = (int*)((char*)ws + MetaLayout::align(tokens * top * 4));
+  a.pos64 = pos;
+  a.table64 = table;
+  a.ordered64 = ordered;
+  a.slots64 = slots;
+  a.bm = (int)bm;
+  a.max_tiles_ref = (int)((tokens * top + bm - 1) / bm + experts);
+  return launch_route(a, (cudaStream_t)stream);
+}
+
+extern "C" int64_t lmoe_route_meta_size(int64_t tokens, int64_t top, int64_t experts) {
+  return MetaLayout(tokens, top, experts).bytes;
+}
+
+int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
+                         int with_shared, void* meta, int* err, cudaStream_t st) {
+  if (!ids || !meta) return LMOE_ERR_INVALID;
+  if (!route_geometry_ok(tokens, top, experts)) return LMOE_ERR_INVALID;
+  const MetaLayout L(tokens, top, experts);
+  char* m = (char*)meta;
+  RouteArgs a = {};
+  a.ids = ids;
+  a.weights = weights;
+  a.T = (int)tokens;
+  a.top = (int)top;
+  a.E = (int)experts;
+  a.with_shared = with_shared ? 1 : 0;
+  a.hdr = (int32_t*)(m + L.off_hdr);
+  a.offsets = (int32_t*)(m + L.off_offsets);
+  a.tiles = (Tile*)(m + L.off_tiles);
+  a.pos32 = (int32_t*)(m + L.off_pos);
+  a.rweight = (float*)(m + L.off_rweight);
+  a.ordered32 = (int32_t*)(m + L.off_ordered);
+  a.inverse = (int32_t*)(m + L.off_inverse);
+  a.err = err;
+  return launch_route(a, st);
+}
+
+extern "C" int lmoe_route_meta(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
+                               int with_shared, void* meta, void* stream) {
+  return lmoe_route_meta_impl(ids, weights, tokens, top, experts, with_shared, meta, nullptr, (cudaStream_t)stream);
+}

@@ -1,0 +1,69 @@
+"""W8A16 group-128 operators (replaces qwen35_deploy/operators/int8.py).
+
+Same call signatures, shapes, dtypes and ``ValueError`` texts as the
+reference; the arithmetic runs in ``liblocalmoe_b200.so``:
+* ``linear``/``Int8Linear`` -- int8.py:26-48 (GEMV for m <= 16 rows, tcgen05 GEMM above);
+* ``grouped_linear``        -- int8.py:233-237 (table-driven decode GEMV);
+* ``ordered_reduce``        -- the launch of ``_ordered_reduce`` at int8.py:185-186;
+* ``Int8Experts``           -- int8.py:127-210, with the expert bank resident in HBM.
+"""
+import torch
+
+from .. import _native as N
+
+
+def _check_weight(q, scale):
+    if not (q.is_cuda and scale.is_cuda and q.dtype == torch.int8 and scale.dtype == torch.float32
+            and q.is_contiguous() and scale.is_contiguous()):
+        raise ValueError('Expected contiguous CUDA int8 weights with float32 group scales')
+
+
+def linear(x, q, scale, large_tile=False):
+    """``y = x . round(q * scale)^T`` (int8.py:26-37).  ``large_tile`` is accepted
+    for signature parity; the library picks its own tiling."""
+    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError('W8A16 requires CUDA FP16/BF16 activations')
+    n, k = q.shape
+    if k % 128 or x.shape[-1] != k or tuple(scale.shape) != (n, k // 128):
+        raise ValueError('Invalid INT8 group geometry')
+    _check_weight(q, scale)
+    x = x.contiguous()
+    m = x.numel() // k
+    out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=x.dtype)
+    N.call('lmoe_linear_w8a16', N.ptr(x), N.ptr(q), N.ptr(scale), N.ptr(out), m, n, k, N.dtype_code(x.dtype),
+           N.ptr(N.error_word(x.device)), N.stream(x.device))
+    return out
+
+
+class Int8Linear(torch.nn.Module):
+    """Buffers ``q`` [N, K] int8 and ``scale`` [N, K/128] fp32 (int8.py:40-48)."""
+
+    def __init__(self, q, scale):
+        super().__init__()
+        self.register_buffer('q', q)
+        self.register_buffer('scale', scale)
+        self.large_prefill_tile = False
+
+    def forward(self, x):
+        return linear(x, self.q, self.scale, self.large_prefill_tile)
+
+
+def grouped_linear(x, table, experts, n, field, shared):
+    """Decode GEMV over a ``[experts, 5]`` int64 descriptor table of raw device
+    pointers (int8.py:233-237).  Returns ``[experts, n]`` in ``x.dtype``."""
+    x = x.contiguous()
+    out = torch.empty((experts, n), dtype=x.dtype, device=x.device)
+    N.call('lmoe_grouped_linear_w8a16', N.ptr(x), N.ptr(table), N.ptr(out), experts, n, x.shape[-1], field,
+           1 if shared else 0, N.dtype_code(x.dtype), N.stream(x.device))
+    return out
+
+
+def ordered_reduce(values, table, weights, out):
+    """``_ordered_reduce`` launch (int8.py:185-186): out[n] = ordered bf16 sum of
+    round(values[e, n] * weights[table[e, 4]]) over table rows."""
+    w = weights if weights.dtype == torch.float32 else weights.float()
+    w = w.contiguous()
+    v = values.contiguous()  # bound to a name: kept alive until the launch is enqueued
+    N.call('lmoe_ordered_reduce', N.ptr(v), N.ptr(table), N.ptr(w), N.ptr(out), v.shape[-1], v.shape[0],
+           N.dtype_code(out.dtype), N.stream(v.device))
+    return out

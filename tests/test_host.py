@@ -1,0 +1,89 @@
+"""CPU-only checks of the boundary: the C-ABI library loads and exports every
+symbol the header declares, host-only entry points answer, and the Python
+operators keep the reference's validation errors.  No kernel is launched."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, 'include', 'localmoe_b200.h')
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    return re.findall(r'LMOE_API\s+(?:int64_t|int)\s+(lmoe_\w+)\s*\(', text)
+
+
+def test_header_declares_entry_points():
+    names = header_symbols()
+    assert len(names) >= 10
+    assert len(set(names)) == len(names)
+
+
+def test_library_exports_every_declared_symbol():
+    from localmoe35ba3b_b200 import _native
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    for name in header_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_binding_covers_header():
+    from localmoe35ba3b_b200 import _native
+    assert set(header_symbols()) == set(_native.SIGNATURES)
+    _native.lib()  # sets argtypes for all; raises on a missing symbol
+
+
+def test_host_only_entry_points():
+    from localmoe35ba3b_b200 import _native
+    lib = _native.lib()
+    assert lib.lmoe_abi_version() == 1
+    a = lib.lmoe_route_meta_size(2048, 8, 256)
+    b = lib.lmoe_route_meta_size(4096, 8, 256)
+    assert 0 < a < b and a % 256 == 0
+    ws = lib.lmoe_moe_workspace_size(2048, 8, 256, 2048, 512)
+    # hidden [(R+T), I] + down [(R+T), H] in bf16 dominate
+    assert ws >= (16384 + 2048) * (512 + 2048) * 2
+    assert lib.lmoe_plan_workspace_size(2048, 8, 256) >= 16384 * 4
+
+
+def test_c_abi_rejects_bad_geometry_without_launching():
+    from localmoe35ba3b_b200 import _native
+    lib = _native.lib()
+    p = ctypes.c_void_p(16)
+    assert lib.lmoe_quantize_rows(p, p, p, 4, 100, 0, None) == _native.ERR_INVALID
+    assert lib.lmoe_quantize_rows(None, p, p, 4, 128, 0, None) == _native.ERR_INVALID
+    assert lib.lmoe_quantize_rows(p, p, p, 4, 128, 7, None) == _native.ERR_INVALID
+    assert lib.lmoe_linear_w8a16(p, p, p, p, 4, 64, 100, 0, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_grouped_linear_w8a8(p, p, p, 8, 64, 256, 1, 1, 0, None, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_plan(p, 16, 8, 0, 16, p, p, p, p, p, None) == _native.ERR_INVALID
+    assert lib.lmoe_routed_moe(p, p, p, 16, 8, p, p, p, p, 8, 2048, 100, *([None] * 8), p, 0, p, None,
+                               None, None) == _native.ERR_INVALID
+
+
+def test_operator_validation_errors_match_reference():
+    from localmoe35ba3b_b200.operators import int8, routing, w8a8
+    from localmoe35ba3b_b200.runtime import gpu_routes
+    q = torch.zeros((64, 256), dtype=torch.int8)
+    s = torch.zeros((64, 2), dtype=torch.float32)
+    with pytest.raises(ValueError, match='W8A16 requires CUDA FP16/BF16 activations'):
+        int8.linear(torch.zeros((2, 256), dtype=torch.bfloat16), q, s)
+    with pytest.raises(ValueError, match='Expected CUDA rows with K divisible by 128'):
+        w8a8.quantize(torch.zeros((2, 256), dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match='Expected contiguous CUDA \\[tokens,top_k\\] routing IDs'):
+        gpu_routes.plan(torch.zeros((4, 8), dtype=torch.int64), 16, 16)
+    with pytest.raises(ValueError, match='Expected nonempty CPU \\[tokens,top_k\\] IDs'):
+        routing.plan_routes(torch.zeros((0, 8), dtype=torch.int64), 16)
+    with pytest.raises(ValueError, match='Out-of-range expert ID'):
+        routing.plan_routes(torch.tensor([[0, 16]]), 16)
+
+
+def test_no_cpu_fallback_when_library_missing(monkeypatch):
+    from localmoe35ba3b_b200 import _native
+    monkeypatch.setattr(_native, 'LIB_PATH', os.path.join(ROOT, 'does-not-exist.so'))
+    monkeypatch.setattr(_native, '_lib', None)
+    with pytest.raises(_native.NativeError, match='no fallback'):
+        _native.lib()

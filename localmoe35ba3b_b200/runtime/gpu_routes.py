@@ -83,9 +83,9 @@ def moe_block(x, weights, ids, banks, shared=None, shared_gate_weight=None, resi
     if stage_events is not None:
         # torch only reports elapsed_time for events it recorded itself; record
         # each once here, the library then re-records it at its stage boundary
-        for e in stage_events:
-            e.record()
-        evs = (ctypes.c_void_p * 5)(*[ctypes.c_void_p(e.cuda_event) for e in stage_events])
+        for ev in stage_events:
+            ev.record()
+        evs = (ctypes.c_void_p * 5)(*[ctypes.c_void_p(ev.cuda_event) for ev in stage_events])
     N.call('lmoe_routed_moe', N.ptr(x), N.ptr(w), N.ptr(ids), t, top, N.ptr(qg), N.ptr(sg), N.ptr(qd), N.ptr(sd),
            e, h, inter, *[N.ptr(v) for v in sh], N.ptr(gate), N.ptr(residual), N.ptr(out), N.dtype_code(x.dtype),
            N.ptr(ws), N.ptr(N.error_word(dev)), evs, N.stream(dev))

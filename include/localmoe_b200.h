@@ -93,10 +93,12 @@ LMOE_API int lmoe_route_meta(const int64_t* ids, const float* weights, int64_t t
 
 /* Replaces prefill._routed via gpu_routes._nonempty (qwen35_deploy/runtime/prefill.py:12-34,
  * gpu_routes.py:39-44): for every route r of expert e, y[r] = x[gather ? pos[r] : r] . W_e^T.
- * meta comes from lmoe_route_meta (its expert segments and tiles). */
+ * meta comes from lmoe_route_meta (its expert segments and tiles).  With gather != 0 the
+ * token rows are first copied in route order into ws (lmoe_routed_linear_workspace_size). */
+LMOE_API int64_t lmoe_routed_linear_workspace_size(int64_t tokens, int64_t top, int64_t k);
 LMOE_API int lmoe_routed_linear(const void* x, const int8_t* q, const float* scale, int64_t experts, int64_t n,
                        int64_t k, const void* meta, int64_t tokens, int64_t top, int gather, void* y,
-                       int dtype, int* err, void* stream);
+                       int dtype, void* ws, int* err, void* stream);
 
 /* Replaces prefill._reduce (qwen35_deploy/runtime/prefill.py:37-49): per token, ordered
  * combine of its routes (ordered/slots as returned by lmoe_plan; weights fp32 [tokens, top]). */

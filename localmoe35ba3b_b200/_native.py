@@ -30,7 +30,8 @@ SIGNATURES = {
     'lmoe_plan': (_I, [_P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
     'lmoe_route_meta_size': (_I64, [_I64, _I64, _I64]),
     'lmoe_route_meta': (_I, [_P, _P, _I64, _I64, _I64, _I, _P, _P]),
-    'lmoe_routed_linear': (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _I, _P, _I, _P, _P]),
+    'lmoe_routed_linear_workspace_size': (_I64, [_I64, _I64, _I64]),
+    'lmoe_routed_linear': (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _I, _P, _I, _P, _P, _P]),
     'lmoe_routed_reduce': (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     'lmoe_moe_workspace_size': (_I64, [_I64, _I64, _I64, _I64, _I64]),
     'lmoe_routed_moe': (_I, [_P, _P, _P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64,

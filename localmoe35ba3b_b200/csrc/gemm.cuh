@@ -10,9 +10,9 @@ namespace lmoe {
 enum GemmMode { kPlain = 0, kSwiGLU = 1, kWeighted = 2 };
 
 struct GemmLaunch {
-  const void* x;          // activations [rows, K]
+  const void* x;          // activations [x_rows, K]
+  int64_t x_rows;
   int64_t K;
-  const int32_t* pos;     // gather index per route row (nullptr: the row itself)
   const Tile* tiles;      // nullptr: dense mode over dense_rows rows
   const int32_t* hdr;     // tiles mode: metadata header (tile count)
   int64_t grid_tiles;     // grid.y: max tiles (tiles mode) or ceil(M/256) (dense)
@@ -34,5 +34,8 @@ struct GemmLaunch {
 };
 
 int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st);
+
+// out[r] = x[pos[r]] for r < rows; rows of k 16-bit elements (permute.cu)
+int launch_permute_rows(const void* x, const int32_t* pos, void* out, int64_t rows, int64_t k, cudaStream_t st);
 
 }  // namespace lmoe

@@ -8,18 +8,26 @@
 // and multiplied into an fp32 accumulator; the output is stored in the
 // activation dtype.
 //
-// Layout ("swap AB"): the MMA's M side is 128 weight rows, its N side is the
+// Layout ("swap AB"): the MMA's M side is 128 weight rows, its N side is a
 // tile's routes (16..256, a multiple of 16), K streams in 64-wide stages.
-//   A  int8 [128 x 64]  TMA  -> smem (4 stages)
+//   A  int8 [128 x 64]  TMA -> smem ring (6 stages)
 //      bf16 [128 x 64]  dequant warps -> 128B-swizzled K-major smem (3 stages)
-//   B  bf16 [256 x 64]  cp.async row gather x[pos[r]] -> same layout (3 stages)
-//   D  fp32 [128 lanes x 256 columns] in tensor memory
-// Warp roles (256 threads): w0 TMA producer, w1 TMEM owner + MMA issuer,
-// w2-3 activation gather, w4-7 dequantisers and then the epilogue.
-// Epilogue modes: PLAIN (y = round(acc)), SWIGLU (gate rows 0-63 and up
-// rows 64-127 of the tile give hidden = round(round(silu(g)) * u), the
-// reference's gpu_routes.py:74-75), WEIGHTED (v = round(round(acc) * w_route),
-// the per-route product of prefill._reduce, prefill.py:45).
+//   B  bf16 [NT x 64]   TMA tiles of 64 consecutive rows -> same layout (3 stages);
+//                       routed rows are consecutive because the activations are
+//                       permuted into route order first (permute_rows_kernel)
+//   D  fp32 [128 lanes x 256 cols] in tensor memory, two buffers
+// The kernel is persistent: one CTA per SM walks the (tile, column-block)
+// work units in a fixed stride, so the epilogue of one unit overlaps the
+// main loop of the next (the MMA issuer alternates TMEM buffers).
+// Warp roles (512 threads): w0 weight TMA, w1 TMEM owner + MMA issuer,
+// w2 activation TMA, w3 idle, w4-11 dequantisers, w12-15 epilogue.
+// Activations: row r of a unit is x[start + r] (no gather inside the GEMM).
+// Epilogue modes: PLAIN (y = round(acc)), SWIGLU (gate rows 0-63 and up rows
+// 64-127 of the unit give hidden = round(round(silu(g)) * u), the reference's
+// gpu_routes.py:74-75), WEIGHTED (v = round(round(acc) * w_route), the
+// per-route product of prefill._reduce, prefill.py:45).
+// Every wait is bounded (LMOE_WAIT_NS); a timeout raises the CTA abort flag
+// and the caller's error word, every role drains and the CTA exits.
 #include <mutex>
 
 #include "common.cuh"
@@ -30,19 +38,20 @@ namespace lmoe {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kNS8 = 4;
+constexpr int kNS8 = 6;
 constexpr int kNS = 3;
-constexpr int kGemmThreads = 256;
-constexpr int kMaxGroups = 32;  // K <= 4096
+constexpr int kGemmThreads = 512;
+constexpr int kDeqWarp0 = 4, kDeqWarps = 8;
+constexpr int kEpiWarp0 = 12;
 constexpr int kA8Bytes = kBM * kBK;
 constexpr int kA16Bytes = kBM * kBK * 2;
 constexpr int kBBytes = kTileRoutes * kBK * 2;
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = 512;   // two 256-column accumulators
+constexpr int kStageTok = 32;    // epilogue chunk (tokens)
+constexpr int kStgBytes = kStageTok * kBM * 2;
 
 struct GemmParams {
-  const void* x;         // activations [rows, K]
   int64_t K;
-  const int32_t* pos;    // per route row: x row to read (nullptr: the route row itself)
   const Tile* tiles;     // nullptr: dense mode
   const int32_t* hdr;    // tiles mode: hdr[kHdrNumTiles]
   int64_t dense_rows;    // dense mode: M
@@ -65,19 +74,63 @@ struct GemmSmem {
   static constexpr int a8 = 0;
   static constexpr int a16 = a8 + kNS8 * kA8Bytes;
   static constexpr int b = a16 + kNS * kA16Bytes;
-  static constexpr int scale = b + kNS * kBBytes;
-  static constexpr int pos = scale + kBM * kMaxGroups * 4;
-  static constexpr int bars = pos + kTileRoutes * 4;
-  static constexpr int nbars = 2 * kNS8 + 3 * kNS + 3;
+  static constexpr int stg = b + kNS * kBBytes;
+  static constexpr int bars = stg + 2 * kStgBytes;
+  // full8, empty8 (kNS8 each); full16, fullB, emptyAB (kNS each); tfull, tempty (2 each); drain
+  static constexpr int nbars = 2 * kNS8 + 3 * kNS + 4 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int bytes = misc + 64;
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
 };
 
+// A work unit: one tile of routes of one expert x one block of output columns.
+struct Unit {
+  int expert, start, count, nb;
+  bool shared;
+};
+
+__device__ __forceinline__ bool get_unit(const GemmParams& p, int u, int nblocks, Unit& o) {
+  const int t = u / nblocks;
+  o.nb = u - t * nblocks;
+  if (p.tiles != nullptr) {
+    if (t >= p.hdr[kHdrNumTiles]) return false;
+    const Tile tl = p.tiles[t];
+    o.expert = tl.expert;
+    o.start = tl.start;
+    o.count = tl.count;
+    o.shared = tl.expert == p.experts;
+  } else {
+    o.expert = 0;
+    o.start = t * kTileRoutes;
+    const int64_t left = p.dense_rows - o.start;
+    if (left <= 0) return false;
+    o.count = left < kTileRoutes ? (int)left : kTileRoutes;
+    o.shared = false;
+  }
+  return o.count > 0;
+}
+
+// rows (tensor-map coordinates) of the unit's two 64-row halves
+__device__ __forceinline__ void unit_rows(const GemmParams& p, const Unit& u, int64_t& lo, int64_t& hi) {
+  const bool sw = p.mode == kSwiGLU;
+  const int64_t ebase = u.shared ? 0 : (int64_t)u.expert * p.N;
+  const int64_t col0 = (int64_t)u.nb * (sw ? 64 : kBM);
+  lo = ebase + col0;
+  hi = sw ? ((u.shared ? 0 : ebase + p.inter) + col0) : lo + 64;
+}
+
+// bounded wait by lane 0, result broadcast: keeps the warp's control flow uniform
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err) {
+  int ok = 1;
+  if (lane_id() == 0) ok = mbar_wait(bar, parity, abort, err) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tm_bank, const __grid_constant__ CUtensorMap tm_lo,
-                              const __grid_constant__ CUtensorMap tm_hi, const GemmParams p) {
+                              const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_x,
+                              const GemmParams p) {
   using A = Act<DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -85,8 +138,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t sA8 = s_base + GemmSmem::a8;
   const uint32_t sA16 = s_base + GemmSmem::a16;
   const uint32_t sB = s_base + GemmSmem::b;
-  float* sScale = (float*)(smem + GemmSmem::scale);
-  int32_t* sPos = (int32_t*)(smem + GemmSmem::pos);
   const uint32_t bar0 = s_base + GemmSmem::bars;
   uint32_t* sTmem = (uint32_t*)(smem + GemmSmem::misc);
   volatile int* sAbort = (volatile int*)(smem + GemmSmem::misc + 8);
@@ -96,283 +147,300 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   auto full16 = [&](int s) { return bar0 + 8u * (2 * kNS8 + s); };
   auto fullB = [&](int s) { return bar0 + 8u * (2 * kNS8 + kNS + s); };
   auto emptyAB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kNS + s); };
-  const uint32_t tmem_full = bar0 + 8u * (2 * kNS8 + 3 * kNS);
-  const uint32_t epi_bar0 = tmem_full + 8u;  // epilogue rendezvous (128 threads, used once each)
-  const uint32_t epi_bar1 = tmem_full + 16u;
+  auto tfull = [&](int b) { return bar0 + 8u * (2 * kNS8 + 3 * kNS + b); };
+  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 3 * kNS + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 3 * kNS + 4);
 
-  // ---------------------------------------------------------------- tile
-  int expert = 0, start, count;
-  if (p.tiles != nullptr) {
-    if ((int)blockIdx.y >= p.hdr[kHdrNumTiles]) return;
-    const Tile t = p.tiles[blockIdx.y];
-    expert = t.expert;
-    start = t.start;
-    count = t.count;
-  } else {
-    start = (int)blockIdx.y * kTileRoutes;
-    const int64_t left = p.dense_rows - start;
-    count = left < kTileRoutes ? (int)left : kTileRoutes;
-  }
-  if (count <= 0) return;
-  const bool shared = (p.tiles != nullptr) && expert == p.experts;
-  const int nb = blockIdx.x;
   const bool swiglu = p.mode == kSwiGLU;
-  const int64_t out_w = swiglu ? p.inter : p.N;      // output columns of one expert
-  const int rows_per_block = swiglu ? 64 : kBM;        // output columns per CTA
-  const int64_t col0 = (int64_t)nb * rows_per_block;
-  if (col0 >= out_w) return;
-  const int valid_cols = (out_w - col0) < rows_per_block ? (int)(out_w - col0) : rows_per_block;
-  const int NT = (count + 15) & ~15;
+  const int64_t out_w = swiglu ? p.inter : p.N;
+  const int cols_per_unit = swiglu ? 64 : kBM;
+  const int nblocks = (int)((out_w + cols_per_unit - 1) / cols_per_unit);
   const int KB = (int)(p.K / kBK);
   const int G = (int)(p.K / kGroup);
-
-  // A rows (tensor-map coordinates) and their scale rows
-  const CUtensorMap* map_lo = shared ? &tm_lo : &tm_bank;
-  const CUtensorMap* map_hi = shared ? (swiglu ? &tm_hi : &tm_lo) : &tm_bank;
-  const float* scl_lo = shared ? p.s_lo : p.s_bank;
-  const float* scl_hi = shared ? (swiglu ? p.s_hi : p.s_lo) : p.s_bank;
-  const int64_t rmax_lo = shared ? p.rows_lo : p.rows_bank;
-  const int64_t rmax_hi = shared ? (swiglu ? p.rows_hi : p.rows_lo) : p.rows_bank;
-  const int64_t ebase = shared ? 0 : (int64_t)expert * p.N;
-  int64_t row_lo, row_hi;
-  if (swiglu) {
-    row_lo = ebase + col0;
-    row_hi = (shared ? 0 : ebase + p.inter) + col0;
-  } else {
-    row_lo = ebase + col0;
-    row_hi = row_lo + 64;
-  }
-
   const int warp = warp_id(), lane = lane_id();
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < kNS8; ++s) {
       mbar_init(full8(s), 1);
-      mbar_init(empty8(s), 128);
+      mbar_init(empty8(s), kDeqWarps);
     }
     for (int s = 0; s < kNS; ++s) {
-      mbar_init(full16(s), 128);
-      mbar_init(fullB(s), 64);
+      mbar_init(full16(s), kDeqWarps);
+      mbar_init(fullB(s), 1);
       mbar_init(emptyAB(s), 1);
     }
-    mbar_init(tmem_full, 1);
-    mbar_init(epi_bar0, 128);
-    mbar_init(epi_bar1, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull(b), 1);
+      mbar_init(tempty(b), 4);
+    }
+    mbar_init(drain, 1);
     *sAbort = 0;
     fence_mbar_init();
-    prefetch_tmap(map_lo);
-    prefetch_tmap(map_hi);
   }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_bank);
+    prefetch_tmap(&tm_lo);
+    prefetch_tmap(&tm_hi);
+  }
+  if (warp == 2 && lane == 0) prefetch_tmap(&tm_x);
   if (warp == 1) {
     tmem_alloc(smem_u32(sTmem), kTmemCols);
     tmem_relinquish();
     tc_fence_before();
   }
-  if (warp >= 4) {  // scales of this CTA's 128 weight rows
-    const int r = threadIdx.x - 128;
-    const int64_t gr = (r < 64) ? row_lo + r : row_hi + (r - 64);
-    const float* sp = (r < 64) ? scl_lo : scl_hi;
-    const int64_t rmax = (r < 64) ? rmax_lo : rmax_hi;
-    for (int g = 0; g < G; ++g) sScale[r * kMaxGroups + g] = (gr < rmax) ? __ldg(sp + gr * G + g) : 0.f;
-  } else if (warp >= 2) {  // gather rows of this tile
-    for (int j = threadIdx.x - 64; j < NT; j += 64) {
-      int src = 0;
-      if (j < count) src = p.pos ? __ldg(p.pos + start + j) : start + j;
-      sPos[j] = src;
-    }
-  }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sTmem;
+  const int stride = gridDim.x;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ weight TMA
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s8 = kb % kNS8;
-        if (!mbar_wait(empty8(s8), ((kb / kNS8) & 1) ^ 1, sAbort, p.err)) break;
-        mbar_arrive_expect_tx(full8(s8), kA8Bytes);
-        tma_load_2d(sA8 + s8 * kA8Bytes, map_lo, full8(s8), kb * kBK, (int)row_lo);
-        tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, map_hi, full8(s8), kb * kBK, (int)row_hi);
-        issued = kb + 1;
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok; u += stride) {
+        Unit un;
+        if (!get_unit(p, u, nblocks, un)) break;
+        int64_t rlo, rhi;
+        unit_rows(p, un, rlo, rhi);
+        const CUtensorMap* mlo = un.shared ? &tm_lo : &tm_bank;
+        const CUtensorMap* mhi = un.shared ? (swiglu ? &tm_hi : &tm_lo) : &tm_bank;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s8 = it % kNS8;
+          if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(full8(s8), kA8Bytes);
+          tma_load_2d(sA8 + s8 * kA8Bytes, mlo, full8(s8), kb * kBK, (int)rlo);
+          tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, mhi, full8(s8), kb * kBK, (int)rhi);
+        }
       }
-      // never leave a bulk copy in flight into shared memory we are about to release
-      for (int kb = max(0, issued - kNS8); kb < issued; ++kb) mbar_wait_drain(full8(kb % kNS8), (kb / kNS8) & 1, p.err);
+      // never leave a bulk copy in flight into shared memory that is about to be released
+      for (int k = max(0, it - kNS8); k < it; ++k) mbar_wait_drain(full8(k % kNS8), (k / kNS8) & 1, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(DT == LMOE_BF16 ? 1 : 0, kBM, NT);
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % kNS;
-        const uint32_t ph = (kb / kNS) & 1;
-        if (!mbar_wait(full16(s), ph, sAbort, p.err)) break;
-        if (!mbar_wait(fullB(s), ph, sAbort, p.err)) break;
+      int it = 0, ui = 0;
+      bool ok = true, issued = false;
+      for (int u = blockIdx.x; ok; u += stride, ++ui) {
+        Unit un;
+        if (!get_unit(p, u, nblocks, un)) break;
+        const int NT = (un.count + 15) & ~15;
+        const uint32_t idesc = idesc_f16(DT == LMOE_BF16 ? 1 : 0, kBM, NT);
+        const int b = ui & 1;
+        if (!mbar_wait(tempty(b), ((ui >> 1) & 1) ^ 1, sAbort, p.err)) break;
         tc_fence_after();
-        const uint64_t ad = sdesc_k_sw128(sA16 + s * kA16Bytes);
-        const uint64_t bd = sdesc_k_sw128(sB + s * kBBytes);
+        const uint32_t dt = tmem + (uint32_t)(b * 256);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % kNS;
+          const uint32_t ph = (it / kNS) & 1;
+          if (!mbar_wait(full16(s), ph, sAbort, p.err)) { ok = false; break; }
+          if (!mbar_wait(fullB(s), ph, sAbort, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = sdesc_k_sw128(sA16 + s * kA16Bytes);
+          const uint64_t bd = sdesc_k_sw128(sB + s * kBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-          mma_f16(tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
-        mma_commit(emptyAB(s));
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_f16(dt, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+          mma_commit(emptyAB(s));
+          issued = true;
+        }
+        // also after an abort, so the epilogue's wait ends (a commit with no
+        // MMA issued before it is not relied on to arrive)
+        if (issued) mma_commit(tfull(b));
       }
-      mma_commit(tmem_full);
+      // every MMA issued by this thread completes before TMEM is released
+      if (issued) {
+        mma_commit(drain);
+        mbar_wait_drain(drain, 0, p.err);
+      }
     }
     __syncwarp();
-  } else if (warp < 4) {
-    // ------------------------------------------------------------ activation gather
-    const int b = threadIdx.x - 64;
-    const int c = b & 7;
-    const int r0 = b >> 3;
-    const char* xb = (const char*)p.x;
-    int done = 0;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kNS;
-      if (!mbar_wait(emptyAB(s), ((kb / kNS) & 1) ^ 1, sAbort, p.err)) break;
-      const uint32_t dst = sB + s * kBBytes;
-      for (int j = r0; j < NT; j += 8) {
-        const bool v = j < count;
-        const char* src = xb + ((int64_t)sPos[j] * p.K + (int64_t)kb * kBK + c * 8) * 2;
-        cp_async16(dst + sw128_off(j, c), src, v ? 16u : 0u);
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ activation TMA
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok; u += stride) {
+        Unit un;
+        if (!get_unit(p, u, nblocks, un)) break;
+        const int nbox = (un.count + 63) / 64;  // 64-row boxes covering the unit's NT rows
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % kNS;
+          if (!mbar_wait(emptyAB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(fullB(s), (uint32_t)nbox * 8192u);
+          const uint32_t dst = sB + s * kBBytes;
+          for (int i = 0; i < nbox; ++i) tma_load_2d(dst + i * 8192, &tm_x, fullB(s), kb * kBK, un.start + 64 * i);
+        }
       }
-      cp_async_commit();
-      if (kb > 0) {
-        cp_async_wait<1>();
-        fence_proxy_async_smem();
-        mbar_arrive(fullB((kb - 1) % kNS));
-      }
-      done = kb + 1;
+      for (int k = max(0, it - kNS); k < it; ++k) mbar_wait_drain(fullB(k % kNS), (k / kNS) & 1, p.err);
     }
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    if (done > 0) mbar_arrive(fullB((done - 1) % kNS));
-  } else {
+    __syncwarp();
+  } else if (warp >= kDeqWarp0 && warp < kDeqWarp0 + kDeqWarps) {
     // ------------------------------------------------------------ dequantise
-    const int d = threadIdx.x - 128;
-    const int w = d >> 5;
+    const int w = warp - kDeqWarp0;
+    const int c = lane & 3;
+    const int r0 = w * 16 + (lane >> 2);  // this thread converts rows r0 and r0 + 8
+    int it8 = 0, it = 0;
     bool ok = true;
-    for (int kb = 0; kb < KB && ok; ++kb) {
-      const int s8 = kb % kNS8;
-      const int s = kb % kNS;
-      if (!mbar_wait(full8(s8), (kb / kNS8) & 1, sAbort, p.err)) { ok = false; break; }
-      if (!mbar_wait(emptyAB(s), ((kb / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-      const int g = kb >> 1;
-      const uint8_t* a8 = smem + GemmSmem::a8 + s8 * kA8Bytes;
-      uint8_t* a16 = smem + GemmSmem::a16 + s * kA16Bytes;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = w * 32 + i * 8 + (lane >> 2);
-        const int c = lane & 3;
-        const uint4 v = *reinterpret_cast<const uint4*>(a8 + row * 64 + c * 16);
-        const float sc = sScale[row * kMaxGroups + g];
-        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-        uint32_t o[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float f0, f1, f2, f3;
-          i8x4_to_f32(wv[j], f0, f1, f2, f3);
-          o[2 * j] = A::pack(__fmul_rn(f0, sc), __fmul_rn(f1, sc));
-          o[2 * j + 1] = A::pack(__fmul_rn(f2, sc), __fmul_rn(f3, sc));
+    for (int u = blockIdx.x; ok; u += stride) {
+      Unit un;
+      if (!get_unit(p, u, nblocks, un)) break;
+      int64_t rlo, rhi;
+      unit_rows(p, un, rlo, rhi);
+      // rows r0 and r0 + 8 lie in the same 64-row half (same source tensor)
+      const bool hi_half = r0 >= 64;
+      const float* sp = hi_half ? (un.shared ? (swiglu ? p.s_hi : p.s_lo) : p.s_bank) : (un.shared ? p.s_lo : p.s_bank);
+      const int64_t rmax = hi_half ? (un.shared ? (swiglu ? p.rows_hi : p.rows_lo) : p.rows_bank)
+                                   : (un.shared ? p.rows_lo : p.rows_bank);
+      const int64_t g0 = hi_half ? rhi + (r0 - 64) : rlo + r0;
+      const bool v0 = g0 < rmax, v1 = g0 + 8 < rmax;
+      const float* p0 = sp + g0 * G;
+      const float* p1 = sp + (g0 + 8) * G;
+      // group scales, fetched two groups ahead of use
+      float c0 = v0 ? __ldg(p0) : 0.f, c1 = v1 ? __ldg(p1) : 0.f;
+      float n0 = (G > 1 && v0) ? __ldg(p0 + 1) : 0.f, n1 = (G > 1 && v1) ? __ldg(p1 + 1) : 0.f;
+      float m0 = (G > 2 && v0) ? __ldg(p0 + 2) : 0.f, m1 = (G > 2 && v1) ? __ldg(p1 + 2) : 0.f;
+      for (int kb = 0; kb < KB; ++kb, ++it8, ++it) {
+        if (kb > 0 && (kb & 1) == 0) {  // entering group kb / 2
+          const int g = kb >> 1;
+          c0 = n0;
+          c1 = n1;
+          n0 = m0;
+          n1 = m1;
+          m0 = (g + 2 < G && v0) ? __ldg(p0 + g + 2) : 0.f;
+          m1 = (g + 2 < G && v1) ? __ldg(p1 + g + 2) : 0.f;
         }
-        *reinterpret_cast<uint4*>(a16 + sw128_off(row, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<uint4*>(a16 + sw128_off(row, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+        const int s8 = it8 % kNS8;
+        const int s = it % kNS;
+        if (!warp_wait(full8(s8), (it8 / kNS8) & 1, sAbort, p.err)) { ok = false; break; }
+        if (!warp_wait(emptyAB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+        const uint8_t* a8 = smem + GemmSmem::a8 + s8 * kA8Bytes;
+        uint8_t* a16 = smem + GemmSmem::a16 + s * kA16Bytes;
+        const uint4 va = *reinterpret_cast<const uint4*>(a8 + r0 * 64 + c * 16);
+        const uint4 vb = *reinterpret_cast<const uint4*>(a8 + (r0 + 8) * 64 + c * 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty8(s8));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint4 v = h ? vb : va;
+          const float sc = h ? c1 : c0;
+          const int row = r0 + 8 * h;
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+          uint32_t o[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float f0, f1, f2, f3;
+            i8x4_to_f32(wv[j], f0, f1, f2, f3);
+            o[2 * j] = A::pack(__fmul_rn(f0, sc), __fmul_rn(f1, sc));
+            o[2 * j + 1] = A::pack(__fmul_rn(f2, sc), __fmul_rn(f3, sc));
+          }
+          *reinterpret_cast<uint4*>(a16 + sw128_off(row, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(a16 + sw128_off(row, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(full16(s));
       }
-      mbar_arrive(empty8(s8));
-      fence_proxy_async_smem();
-      mbar_arrive(full16(s));
     }
-
+  } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
-    // every epilogue thread takes the same path: the waits below ignore the
-    // abort flag and are bounded, and the rendezvous are mbarriers, not bar.sync
-    const bool have = mbar_wait_drain(tmem_full, 0, p.err);
-    tc_fence_after();
-    if (have) {
-      const int q = w;  // TMEM lane quadrant of this warp (warps 4..7)
-      const int row = q * 32 + lane;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-      uint16_t* stg = (uint16_t*)(smem + GemmSmem::b);  // B stages are idle now
-      typename A::T* y = (typename A::T*)p.y;
-      if (!swiglu) {
-        const bool weigh = (p.mode == kWeighted) && !shared;
-        for (int c0 = 0; c0 < NT; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c0, r);
-          tmem_ld_wait();
+    const int q = warp - kEpiWarp0;              // TMEM lane quadrant (== warp % 4)
+    const int e = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+    const int row = q * 32 + lane;               // weight row of this thread in the unit
+    typename A::T* y = (typename A::T*)p.y;
+    uint16_t* stg0 = (uint16_t*)(smem + GemmSmem::stg);
+    volatile uint32_t* sHave = (volatile uint32_t*)(sTmem + 1);
+    int ui = 0, chunk_ctr = 0;
+    for (int u = blockIdx.x;; u += stride, ++ui) {
+      Unit un;
+      if (!get_unit(p, u, nblocks, un)) break;
+      const int b = ui & 1;
+      // one thread waits (bounded); the group follows through a named barrier,
+      // so all 128 threads take the same path
+      if (e == 0) *sHave = mbar_wait_drain(tfull(b), (ui >> 1) & 1, p.err) ? 1u : 0u;
+      named_barrier(1, 128);
+      const bool have = *sHave != 0;
+      named_barrier(1, 128);
+      tc_fence_after();
+      const int NT = (un.count + 15) & ~15;
+      const int64_t col0 = (int64_t)un.nb * cols_per_unit;
+      const int valid_cols = (out_w - col0) < cols_per_unit ? (int)(out_w - col0) : cols_per_unit;
+      const uint32_t taddr = tmem + (uint32_t)(b * 256) + ((uint32_t)(q * 32) << 16);
+      const bool weigh = (p.mode == kWeighted) && !un.shared;
+      for (int c0 = 0; c0 < NT; c0 += kStageTok, ++chunk_ctr) {
+        uint16_t* stg = stg0 + (chunk_ctr & 1) * (kStgBytes / 2);
+        uint32_t r[32];
+        tmem_ld32(taddr + c0, r);
+        tmem_ld_wait();
+        if (c0 + kStageTok >= NT) {  // last TMEM read of this unit: hand the buffer back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty(b));
+        }
+        if (have) {
+          float wl = 1.f;
+          if (weigh && c0 + lane < un.count) wl = __ldg(p.rweight + un.start + c0 + lane);
+          // stage [token][row] in the activation dtype
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int j = c0 + jj;
-            if (j < count) {
-              float v = A::round(__uint_as_float(r[jj]));
-              if (weigh) v = A::round(__fmul_rn(v, __ldg(p.rweight + start + j)));
-              stg[j * kBM + row] = A::bits(v);
-            }
+          for (int jj = 0; jj < kStageTok; ++jj) {
+            float v = A::round(__uint_as_float(r[jj]));
+            if (weigh) v = A::round(__fmul_rn(v, __shfl_sync(0xffffffffu, wl, jj)));
+            stg[jj * kBM + row] = A::bits(v);
           }
         }
-        mbar_arrive(epi_bar0);
-        mbar_wait_drain(epi_bar0, 0, p.err);
-        const bool vec = (valid_cols == kBM) && (p.ldy % 8 == 0) && (col0 % 8 == 0);
-        for (int j = d >> 4; j < count; j += 8) {
-          const int c8 = (d & 15) * 8;
-          typename A::T* dst = y + (int64_t)(start + j) * p.ldy + col0 + c8;
-          const uint16_t* src = stg + j * kBM + c8;
-          if (vec) {
-            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        // the next chunk uses the other staging buffer, and the barrier of the
+        // chunk after that orders its writes behind these reads
+        named_barrier(1, 128);
+        if (have) {
+          const int ntok = min(kStageTok, un.count - c0);
+          if (!swiglu) {
+            // 4 threads per token row, 32 columns (64 B) each
+            const int j = e >> 2, cb = (e & 3) * 32;
+            if (j < ntok) {
+              typename A::T* dst = y + (int64_t)(un.start + c0 + j) * p.ldy + col0 + cb;
+              const uint16_t* src = stg + j * kBM + cb;
+              if (valid_cols == kBM && (p.ldy % 8) == 0) {
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                  reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(src)[v];
+              } else {
+                for (int v = 0; v < 32; ++v)
+                  if (cb + v < valid_cols) reinterpret_cast<uint16_t*>(dst)[v] = src[v];
+              }
+            }
           } else {
-            for (int u = 0; u < 8; ++u)
-              if (c8 + u < valid_cols) reinterpret_cast<uint16_t*>(dst)[u] = src[u];
-          }
-        }
-      } else {
-        uint16_t* stg_u = stg;                       // [NT][64] up values
-        uint16_t* stg_h = stg + kTileRoutes * 64;    // [NT][64] hidden values
-        if (q >= 2) {
-          for (int c0 = 0; c0 < NT; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(taddr + c0, r);
-            tmem_ld_wait();
+            // hidden = round(round(silu(gate)) * up): 4 threads per token, 16 columns each
+            const int j = e >> 2, cb = (e & 3) * 16;
+            if (j < ntok) {
+              uint32_t hv[8];
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-              const int j = c0 + jj;
-              if (j < count) stg_u[j * 64 + (row - 64)] = A::bits(__uint_as_float(r[jj]));
-            }
-          }
-        }
-        mbar_arrive(epi_bar0);
-        mbar_wait_drain(epi_bar0, 0, p.err);
-        if (q < 2) {
-          for (int c0 = 0; c0 < NT; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(taddr + c0, r);
-            tmem_ld_wait();
+              for (int v = 0; v < 8; ++v) {
+                float h2[2];
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-              const int j = c0 + jj;
-              if (j < count) {
-                const float gt = A::round(__uint_as_float(r[jj]));
-                const float up = A::lo_f((uint32_t)stg_u[j * 64 + row]);
-                const float sl = A::round(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))));
-                stg_h[j * 64 + row] = A::bits(__fmul_rn(sl, up));
+                for (int t = 0; t < 2; ++t) {
+                  const int col = cb + 2 * v + t;
+                  const float g = A::lo_f((uint32_t)stg[j * kBM + col]);
+                  const float up = A::lo_f((uint32_t)stg[j * kBM + 64 + col]);
+                  const float sl = A::round(__fdividef(g, 1.0f + __expf(-g)));
+                  h2[t] = __fmul_rn(sl, up);
+                }
+                hv[v] = A::pack(h2[0], h2[1]);
+              }
+              typename A::T* dst = y + (int64_t)(un.start + c0 + j) * p.ldy + col0 + cb;
+              if (valid_cols == 64 && (p.ldy % 8) == 0) {
+                reinterpret_cast<uint4*>(dst)[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                reinterpret_cast<uint4*>(dst)[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+              } else {
+                for (int v = 0; v < 16; ++v)
+                  if (cb + v < valid_cols)
+                    reinterpret_cast<uint16_t*>(dst)[v] = (uint16_t)((hv[v >> 1] >> (16 * (v & 1))) & 0xffffu);
               }
             }
           }
         }
-        mbar_arrive(epi_bar1);
-        mbar_wait_drain(epi_bar1, 0, p.err);
-        const bool vec = (valid_cols == 64) && (p.ldy % 8 == 0) && (col0 % 8 == 0);
-        for (int j = d >> 3; j < count; j += 16) {
-          const int c8 = (d & 7) * 8;
-          typename A::T* dst = y + (int64_t)(start + j) * p.ldy + col0 + c8;
-          const uint16_t* src = stg_h + j * 64 + c8;
-          if (vec) {
-            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-          } else {
-            for (int u = 0; u < 8; ++u)
-              if (c8 + u < valid_cols) reinterpret_cast<uint16_t*>(dst)[u] = src[u];
-          }
-        }
       }
+      if (!have) break;  // the MMA issuer gave up: stop instead of waiting on every later unit
     }
   }
 
@@ -418,24 +486,42 @@ static int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64
   return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
 }
 
+// activations [rows, K] 16-bit, box of 64 rows x 64 elements (8 KB) with the
+// 128-byte swizzle: the B operand's K-major UMMA layout
+static int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int dtype) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LMOE_ERR_CUDA;
+  if (((uintptr_t)base & 15) || (K % 64) || rows <= 0) return LMOE_ERR_INVALID;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, dtype == LMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  (void*)base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
 int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st) {
-  if (L.K % kGroup || L.K / kGroup > kMaxGroups || L.K <= 0) return LMOE_ERR_INVALID;
+  if (L.K % kGroup || L.K <= 0) return LMOE_ERR_INVALID;
   if (L.grid_tiles <= 0) return LMOE_OK;
-  CUtensorMap tb, tl, th;
+  CUtensorMap tb, tl, th, tx;
   int rc = make_int8_map(&tb, L.q_bank, L.experts * L.N, L.K);
   if (rc) return rc;
   tl = tb;
   th = tb;
-  if (L.q_lo) {
-    if ((rc = make_int8_map(&tl, L.q_lo, L.rows_lo, L.K))) return rc;
-  }
-  if (L.q_hi) {
-    if ((rc = make_int8_map(&th, L.q_hi, L.rows_hi, L.K))) return rc;
-  }
+  if (L.q_lo && (rc = make_int8_map(&tl, L.q_lo, L.rows_lo, L.K))) return rc;
+  if (L.q_hi && (rc = make_int8_map(&th, L.q_hi, L.rows_hi, L.K))) return rc;
+  if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype))) return rc;
   GemmParams p = {};
-  p.x = L.x;
   p.K = L.K;
-  p.pos = L.pos;
   p.tiles = L.tiles;
   p.hdr = L.hdr;
   p.dense_rows = L.dense_rows;
@@ -455,16 +541,18 @@ int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st) {
   p.err = L.err;
   const int64_t out_w = L.mode == kSwiGLU ? L.inter : L.N;
   const int per = L.mode == kSwiGLU ? 64 : kBM;
-  const dim3 grid((unsigned)((out_w + per - 1) / per), (unsigned)L.grid_tiles);
+  const int64_t units = ((out_w + per - 1) / per) * L.grid_tiles;
+  const int64_t sms = sm_count();
+  const int64_t ctas = units < sms ? units : sms;
   const size_t smem = GemmSmem::alloc;
   if (L.dtype == LMOE_BF16) {
     auto k = grouped_gemm_w8a16_kernel<LMOE_BF16>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<grid, kGemmThreads, smem, st>>>(tb, tl, th, p);
+    k<<<(unsigned)ctas, kGemmThreads, smem, st>>>(tb, tl, th, tx, p);
   } else if (L.dtype == LMOE_F16) {
     auto k = grouped_gemm_w8a16_kernel<LMOE_F16>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<grid, kGemmThreads, smem, st>>>(tb, tl, th, p);
+    k<<<(unsigned)ctas, kGemmThreads, smem, st>>>(tb, tl, th, tx, p);
   } else {
     return LMOE_ERR_INVALID;
   }
@@ -486,9 +574,9 @@ extern "C" int lmoe_linear_w8a16(const void* x, const int8_t* q, const float* sc
   if (m == 0) return LMOE_OK;
   cudaStream_t st = (cudaStream_t)stream;
   if (m <= 16) return lmoe_dense_gemv_w8a16(x, q, scale, y, m, n, k, dtype, st);
-  if (k / kGroup > kMaxGroups) return LMOE_ERR_UNSUPPORTED;
   GemmLaunch L = {};
   L.x = x;
+  L.x_rows = m;
   L.K = k;
   L.grid_tiles = (m + kTileRoutes - 1) / kTileRoutes;
   L.dense_rows = m;
@@ -504,17 +592,28 @@ extern "C" int lmoe_linear_w8a16(const void* x, const int8_t* q, const float* sc
   return launch_grouped_gemm(L, st);
 }
 
+extern "C" int64_t lmoe_routed_linear_workspace_size(int64_t tokens, int64_t top, int64_t k) {
+  return MetaLayout::align(tokens * top * k * 2);
+}
+
 extern "C" int lmoe_routed_linear(const void* x, const int8_t* q, const float* scale, int64_t experts, int64_t n,
                                   int64_t k, const void* meta, int64_t tokens, int64_t top, int gather, void* y,
-                                  int dtype, int* err, void* stream) {
+                                  int dtype, void* ws, int* err, void* stream) {
   if (!x || !q || !scale || !meta || !y || experts <= 0 || n <= 0 || k <= 0 || k % kGroup) return LMOE_ERR_INVALID;
-  if (k / kGroup > kMaxGroups) return LMOE_ERR_UNSUPPORTED;
+  if (gather && !ws) return LMOE_ERR_INVALID;
   const MetaLayout ML(tokens, top, experts);
   const char* m = (const char*)meta;
+  cudaStream_t st = (cudaStream_t)stream;
+  const void* rows = x;
+  if (gather) {  // route-order copy of the token rows, then a plain tiled GEMM
+    int rc = launch_permute_rows(x, (const int32_t*)(m + ML.off_pos), ws, tokens * top, k, st);
+    if (rc) return rc;
+    rows = ws;
+  }
   GemmLaunch L = {};
-  L.x = x;
+  L.x = rows;
+  L.x_rows = tokens * top;
   L.K = k;
-  L.pos = gather ? (const int32_t*)(m + ML.off_pos) : nullptr;
   L.tiles = (const Tile*)(m + ML.off_tiles);
   L.hdr = (const int32_t*)(m + ML.off_hdr);
   L.grid_tiles = ML.max_tiles;
@@ -527,5 +626,5 @@ extern "C" int lmoe_routed_linear(const void* x, const int8_t* q, const float* s
   L.mode = kPlain;
   L.dtype = dtype;
   L.err = err;
-  return launch_grouped_gemm(L, (cudaStream_t)stream);
+  return launch_grouped_gemm(L, st);
 }

@@ -94,12 +94,13 @@ __global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(
 }
 
 struct MoeWs {
-  int64_t off_meta, off_hidden, off_down, bytes;
+  int64_t off_meta, off_xs, off_hidden, off_down, bytes;
   MoeWs(int64_t T, int64_t top, int64_t E, int64_t H, int64_t I) {
     const int64_t R = T * top;
     const MetaLayout L(T, top, E);
     off_meta = 0;
-    off_hidden = MetaLayout::align(L.bytes);
+    off_xs = MetaLayout::align(L.bytes);  // token rows in route order (+ the shared segment)
+    off_hidden = MetaLayout::align(off_xs + (R + T) * H * 2);
     off_down = MetaLayout::align(off_hidden + (R + T) * I * 2);
     bytes = MetaLayout::align(off_down + (R + T) * H * 2);
   }
@@ -134,6 +135,7 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   const MetaLayout ML(tokens, top, experts);
   char* w = (char*)ws;
   char* meta = w + W.off_meta;
+  void* xs = w + W.off_xs;
   void* hid = w + W.off_hidden;
   void* dn = w + W.off_down;
   const int64_t R = tokens * top;
@@ -148,10 +150,13 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   if ((rc = lmoe_route_meta_impl(ids, weights, tokens, top, experts, with_shared ? 1 : 0, meta, err, st))) return rc;
   if ((rc = mark(1))) return rc;
 
+  const int64_t rows = R + (with_shared ? tokens : 0);
+  if ((rc = launch_permute_rows(x, (const int32_t*)(meta + ML.off_pos), xs, rows, hidden, st))) return rc;
+
   GemmLaunch g = {};
-  g.x = x;
+  g.x = xs;
+  g.x_rows = rows;
   g.K = hidden;
-  g.pos = (const int32_t*)(meta + ML.off_pos);
   g.tiles = (const Tile*)(meta + ML.off_tiles);
   g.hdr = (const int32_t*)(meta + ML.off_hdr);
   g.grid_tiles = ML.max_tiles;
@@ -178,8 +183,8 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
 
   GemmLaunch d = g;
   d.x = hid;
+  d.x_rows = rows;
   d.K = inter;
-  d.pos = nullptr;
   d.q_bank = qd;
   d.s_bank = sd;
   d.N = hidden;

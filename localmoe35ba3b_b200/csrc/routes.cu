@@ -18,6 +18,15 @@ namespace lmoe {
 constexpr int kRouteThreads = 1024;
 constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kMaxTop = 32;
+constexpr int kBatch = 16;  // ids held per lane per batch
+
+__device__ __forceinline__ int clamp_id(int64_t v, int E, int* err) {
+  if (v < 0 || v >= E) {
+    raise_error(err, 2);
+    return E;
+  }
+  return (int)v;
+}
 
 // inclusive block scan over kRouteThreads values (one per thread)
 __device__ int block_incl_scan(int v, int* warp_tot) {
@@ -80,14 +89,18 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
 
   for (int i = threadIdx.x; i < kRouteWarps * (E + 1); i += blockDim.x) cw[i] = 0;
   __syncthreads();
-  // pass 1: per-warp counts (out-of-range ids are counted in bucket E and flagged)
-  for (int f = seg_lo + lane; f < seg_hi; f += 32) {
-    int64_t id = a.ids[f];
-    if (id < 0 || id >= E) {
-      raise_error(a.err, 2);
-      id = E;
+  // pass 1: per-warp counts (out-of-range ids are counted in bucket E and
+  // flagged).  Ids are fetched kBatch per lane at a time so the loads overlap.
+  for (int base = seg_lo; base < seg_hi; base += 32 * kBatch) {
+    int idv[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int f = base + i * 32 + lane;
+      idv[i] = (f < seg_hi) ? clamp_id(a.ids[f], E, a.err) : -1;
     }
-    atomicAdd(&cw[warp * (E + 1) + (int)id], 1);
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+      if (idv[i] >= 0) atomicAdd(&cw[warp * (E + 1) + idv[i]], 1);
   }
   __syncthreads();
   // per expert: exclusive over warps, then exclusive over experts
@@ -115,27 +128,34 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
 
   // pass 2: stable placement
   const unsigned lt = (1u << lane) - 1u;
-  for (int base = seg_lo; base < seg_hi; base += 32) {
-    const int f = base + lane;
-    const bool valid = f < seg_hi;
-    int id = -1;
-    if (valid) {
-      const int64_t v = a.ids[f];
-      id = (v < 0 || v >= E) ? E : (int)v;
+  for (int base = seg_lo; base < seg_hi; base += 32 * kBatch) {
+    int idv[kBatch];
+    float wv[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int f = base + i * 32 + lane;
+      idv[i] = (f < seg_hi) ? clamp_id(a.ids[f], E, nullptr) : -1;
+      wv[i] = (f < seg_hi && a.weights) ? a.weights[f] : 1.0f;
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, id);
-    int dst = 0;
-    if (valid) dst = cw[warp * (E + 1) + id] + __popc(peers & lt);
-    __syncwarp();
-    if (valid) {
-      a.inverse[f] = dst;
-      const int tok = f / a.top;
-      if (a.pos32) a.pos32[dst] = tok;
-      if (a.pos64) a.pos64[dst] = tok;
-      if (a.rweight) a.rweight[dst] = a.weights ? a.weights[f] : 1.0f;
-      if (lane == 31 - __clz(peers)) cw[warp * (E + 1) + id] += __popc(peers);
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int f = base + i * 32 + lane;
+      const bool valid = idv[i] >= 0;
+      const int id = idv[i];
+      const unsigned peers = __match_any_sync(0xffffffffu, id);
+      int dst = 0;
+      if (valid) dst = cw[warp * (E + 1) + id] + __popc(peers & lt);
+      __syncwarp();
+      if (valid) {
+        a.inverse[f] = dst;
+        const int tok = f / a.top;
+        if (a.pos32) a.pos32[dst] = tok;
+        if (a.pos64) a.pos64[dst] = tok;
+        if (a.rweight) a.rweight[dst] = wv[i];
+        if (lane == 31 - __clz(peers)) cw[warp * (E + 1) + id] += __popc(peers);
+      }
+      __syncwarp();
     }
-    __syncwarp();
   }
   if (a.pos32 && a.with_shared)
     for (int t = threadIdx.x; t < a.T; t += blockDim.x) a.pos32[R + t] = t;

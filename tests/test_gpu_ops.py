@@ -282,8 +282,9 @@ def test_routed_linear(dtype, gather):
     N.call('lmoe_route_meta', N.ptr(ids_d), N.ptr(w_d), T, top, E, 0, N.ptr(meta), N.stream())
     y = torch.zeros((T * top, Nn), dtype=TORCH_DT[dtype], device='cuda')
     x_d, q_d, s_d = to_dev(x, dtype), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    ws = torch.empty(N.lib().lmoe_routed_linear_workspace_size(T, top, K), dtype=torch.uint8, device='cuda')
     N.call('lmoe_routed_linear', N.ptr(x_d), N.ptr(q_d), N.ptr(s_d), E, Nn, K, N.ptr(meta), T, top,
-           1 if gather else 0, N.ptr(y), N.dtype_code(y.dtype), N.ptr(N.error_word('cuda')), N.stream())
+           1 if gather else 0, N.ptr(y), N.dtype_code(y.dtype), N.ptr(ws), N.ptr(N.error_word('cuda')), N.stream())
     torch.cuda.synchronize()
     pos, _, _, _ = O.plan(ids, E, 16)
     ref = O.routed_linear(x, q, s, pos, O.expert_offsets(ids, E), gather, dtype)

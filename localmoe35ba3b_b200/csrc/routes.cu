@@ -9,7 +9,9 @@
 // segment in order, 32 routes at a time, ranking equal ids inside the warp
 // with __match_any_sync -- so routes of one expert keep their flat order, as
 // torch.sort(stable=True) does.  The per-token ascending-expert order
-// (argsort(dim=1, stable=True)) is an insertion sort of each token's top-k.
+// (argsort(dim=1, stable=True)) comes from each route's rank among its own
+// token's top-k ids (smaller id, or equal id and earlier slot), computed in
+// the same pass, so `ordered`/`slots` need no second pass over `inverse`.
 #include "common.cuh"
 #include "routes.cuh"
 
@@ -64,7 +66,7 @@ struct RouteArgs {
   int32_t* pos32;
   float* rweight;
   int32_t* ordered32;
-  int32_t* inverse;  // scratch [R], required
+  int32_t* inverse;  // optional [R]: sorted position of each flat route
   // reference-format outputs (nullable)
   int64_t* pos64;
   int64_t* table64;
@@ -147,11 +149,24 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
       if (valid) dst = cw[warp * (E + 1) + id] + __popc(peers & lt);
       __syncwarp();
       if (valid) {
-        a.inverse[f] = dst;
         const int tok = f / a.top;
+        const int slot = f - tok * a.top;
+        // rank of this route among its token's routes, ordered by (id, slot)
+        const int64_t* trow = a.ids + (int64_t)tok * a.top;
+        int rank = 0;
+        for (int j = 0; j < a.top; ++j) {
+          const int64_t oj = trow[j];
+          const int idj = (oj < 0 || oj >= E) ? E : (int)oj;
+          rank += (idj < id) || (idj == id && j < slot);
+        }
+        const int64_t o = (int64_t)tok * a.top + rank;
+        if (a.inverse) a.inverse[f] = dst;
         if (a.pos32) a.pos32[dst] = tok;
         if (a.pos64) a.pos64[dst] = tok;
         if (a.rweight) a.rweight[dst] = wv[i];
+        if (a.ordered32) a.ordered32[o] = dst;
+        if (a.ordered64) a.ordered64[o] = dst;
+        if (a.slots64) a.slots64[o] = slot;
         if (lane == 31 - __clz(peers)) cw[warp * (E + 1) + id] += __popc(peers);
       }
       __syncwarp();
@@ -160,30 +175,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   if (a.pos32 && a.with_shared)
     for (int t = threadIdx.x; t < a.T; t += blockDim.x) a.pos32[R + t] = t;
   __syncthreads();
-
-  // per token: slots by ascending expert (stable), ordered = inverse[t*top + slot]
-  for (int t = threadIdx.x; t < a.T; t += blockDim.x) {
-    int sid[kMaxTop], sl[kMaxTop];
-    for (int i = 0; i < a.top; ++i) {
-      const int64_t v = a.ids[(int64_t)t * a.top + i];
-      const int id = (int)v;
-      int j = i;
-      while (j > 0 && sid[j - 1] > id) {  // strict: equal ids keep slot order
-        sid[j] = sid[j - 1];
-        sl[j] = sl[j - 1];
-        --j;
-      }
-      sid[j] = id;
-      sl[j] = i;
-    }
-    for (int i = 0; i < a.top; ++i) {
-      const int64_t o = (int64_t)t * a.top + i;
-      const int route = a.inverse[(int64_t)t * a.top + sl[i]];
-      if (a.ordered32) a.ordered32[o] = route;
-      if (a.ordered64) a.ordered64[o] = route;
-      if (a.slots64) a.slots64[o] = sl[i];
-    }
-  }
 
   // counts again, per expert (from offsets held in cw row 0 + totals)
   // cw[0][e] was advanced by warp 0's routes; recompute counts from the scan

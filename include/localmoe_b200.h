@@ -121,6 +121,25 @@ LMOE_API int lmoe_routed_moe(const void* x, const float* weights, const int64_t*
                     const void* residual, void* out, int dtype, void* ws, int* err, void** stage_events,
                     void* stream);
 
+/* Allocation-free form of lmoe_routed_moe (no counterpart in the reference: the reference
+ * runtime allocates its own buffers with torch).  For callers that cannot allocate device
+ * memory where they run the block -- inside CUDA-graph stream capture, under a fixed arena
+ * owned by a host runtime, or from a C/FFI host with no device allocator.  Same arguments
+ * as lmoe_routed_moe without ws/stage_events; scratch is a file-scope device array of
+ * lmoe_routed_moe_noalloc_limit() bytes (16 MiB) that each GPU using the library keeps for
+ * the life of the process.  Returns LMOE_ERR_UNSUPPORTED when lmoe_moe_workspace_size()
+ * for the call exceeds that limit (at hidden 2048, inter 512, top 8 and 256 experts about 200
+ * tokens fit; 256 do not).  The first call on a device looks up the array's device address (this may
+ * load the module): make it before any stream capture.  All calls share the array, so calls
+ * that overlap on the GPU (different streams, or different threads) race: serialise them. */
+LMOE_API int64_t lmoe_routed_moe_noalloc_limit(void);
+LMOE_API int lmoe_routed_moe_noalloc(const void* x, const float* weights, const int64_t* ids, int64_t tokens,
+                            int64_t top, const int8_t* qg, const float* sg, const int8_t* qd, const float* sd,
+                            int64_t experts, int64_t hidden, int64_t inter, const int8_t* sh_qg,
+                            const float* sh_sg, const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd,
+                            const float* sh_sd, const void* sh_gate_w, const void* residual, void* out,
+                            int dtype, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,6 +36,9 @@ SIGNATURES = {
     'lmoe_moe_workspace_size': (_I64, [_I64, _I64, _I64, _I64, _I64]),
     'lmoe_routed_moe': (_I, [_P, _P, _P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64,
                              _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
+    'lmoe_routed_moe_noalloc_limit': (_I64, []),
+    'lmoe_routed_moe_noalloc': (_I, [_P, _P, _P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64,
+                                     _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P]),
 }
 
 _lib = None

@@ -214,3 +214,60 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   LMOE_CUDA_CHECK(cudaGetLastError());
   return mark(4);
 }
+
+// ============================================================================
+// Allocation-free variant of lmoe_routed_moe.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// MoE block: code executing while a CUDA graph is being captured (allocation
+// calls are not capturable), runtimes that hand out device memory only from a
+// fixed, pre-sized arena they do not expose to plug-ins, and C/FFI hosts that
+// link this library without any device allocator of their own.  For them the
+// scratch space lives in a file-scope __device__ array of a fixed size,
+// kNoAllocScratchBytes, which every GPU that loads this library keeps for
+// the life of the process.
+namespace lmoe {
+constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+}  // namespace lmoe
+
+#include <mutex>
+
+// Device address of the scratch array for the current device.  Host code
+// cannot use the array's name as a pointer (it is a host-side stand-in), so
+// the address is looked up once per device, with that device current, and
+// cached.  That first lookup may load the module on the device: make the
+// first call on each device before any stream capture begins.
+static void* noalloc_scratch() {
+  static std::mutex mu;
+  static void* ptrs[128] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, lmoe::g_noalloc_scratch) != cudaSuccess) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+extern "C" int64_t lmoe_routed_moe_noalloc_limit(void) { return lmoe::kNoAllocScratchBytes; }
+
+extern "C" int lmoe_routed_moe_noalloc(const void* x, const float* weights, const int64_t* ids, int64_t tokens,
+                                       int64_t top, const int8_t* qg, const float* sg, const int8_t* qd,
+                                       const float* sd, int64_t experts, int64_t hidden, int64_t inter,
+                                       const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu,
+                                       const float* sh_su, const int8_t* sh_qd, const float* sh_sd,
+                                       const void* sh_gate_w, const void* residual, void* out, int dtype, int* err,
+                                       void* stream) {
+  if (tokens <= 0 || top <= 0 || experts <= 0 || hidden <= 0 || inter <= 0) return LMOE_ERR_INVALID;
+  // every byte of the scratch that a call reads is written earlier in the same
+  // call, so nothing needs clearing between calls
+  if (lmoe_moe_workspace_size(tokens, top, experts, hidden, inter) > lmoe::kNoAllocScratchBytes)
+    return LMOE_ERR_UNSUPPORTED;
+  void* ws = noalloc_scratch();
+  if (ws == nullptr) return LMOE_ERR_CUDA;
+  return lmoe_routed_moe(x, weights, ids, tokens, top, qg, sg, qd, sd, experts, hidden, inter, sh_qg, sh_sg, sh_qu,
+                         sh_su, sh_qd, sh_sd, sh_gate_w, residual, out, dtype, ws, err, nullptr, stream);
+}

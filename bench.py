@@ -37,6 +37,16 @@ HIDDEN, INTER, EXPERTS, TOP = 2048, 512, 256, 8
 EXPERT_BYTES = 3 * INTER * HIDDEN + 3 * INTER * HIDDEN // 128 * 4  # 3,244,032
 METRIC = 'expert-FFN prefill tok/s (2048-chunk x 40 layers, W8A16)'
 UNIT = 'tok/s'
+# Kernels launched per layer of the step: route_kernel, permute_rows_kernel, grouped GEMM
+# (gate_up), grouped GEMM (down), moe_combine_kernel.
+LAUNCHES_PER_LAYER = 5
+# DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
+# `ncu --set full` capture of layer 0 (`python bench.py --layers 2 --steps 1 --warmup 1
+# --no-cpu-baseline`, -k regex:grouped_gemm -s 4 -c 2): gate_up 419.7 MB + down 252.7 MB.
+# Per-layer work does not depend on the layer count, so no scaling is applied.
+NCU_TRAFFIC_PER_LAYER = 672.4e6
+NCU_TRAFFIC_SOURCE = ('ncu dram__bytes_read.sum + dram__bytes_write.sum, gate_up + down launches of one '
+                      '2048-token layer; bytes per layer like alg_bytes_per_layer')
 
 
 def parse():
@@ -232,7 +242,7 @@ def run_ours(a, rank, world, local):
     else:
         roof = {'bound': 'hbm', 'achieved': round(gbs, 1), 'peak': pk_hbm, 'unit': 'GB/s',
                 'frac': round(gbs / pk_hbm, 4)}
-    roof.update({'traffic': None, 'kernel': 'grouped_gemm_w8a16 (gate_up+SwiGLU, down+weight) per layer',
+    roof.update({'traffic': NCU_TRAFFIC_PER_LAYER, 'traffic_source': NCU_TRAFFIC_SOURCE, 'kernel': 'grouped_gemm_w8a16 (gate_up+SwiGLU, down+weight) per layer',
                  'peak_source': pk_tc_src, 'flops_per_layer': flops, 'alg_bytes_per_layer': round(gemm_bytes),
                  'tensor_frac': round(tflops / pk_tc, 4), 'hbm_frac': round(gbs / pk_hbm, 4),
                  'gemm_us_per_layer': round(gemm_ms * 1e3, 2),
@@ -285,7 +295,7 @@ def run_ours(a, rank, world, local):
                    'active_experts_mean': round(float(np.mean(active)), 1),
                    'l2': 'inputs larger than L2 (33.2 GB of resident expert weights per GPU)'},
         'roofline': roof, 'cpu_baseline': cpu, 'e2e': e2e,
-        'gpu_launches': 4 * a.layers * a.steps, 'clocks': clk.summary(),
+        'gpu_launches': LAUNCHES_PER_LAYER * a.layers * a.steps, 'clocks': clk.summary(),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

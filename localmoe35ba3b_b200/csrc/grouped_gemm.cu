@@ -9,9 +9,13 @@
 // activation dtype.
 //
 // Layout ("swap AB"): the MMA's M side is 128 weight rows, its N side is a
-// tile's routes (16..256, a multiple of 16), K streams in 64-wide stages.
-//   A  int8 [128 x 64]  TMA -> smem ring (6 stages)
-//      bf16 [128 x 64]  dequant warps -> 128B-swizzled K-major smem (3 stages)
+// tile's routes (16..256, a multiple of 16), K streams in 64-wide MMA stages.
+//   A  int8 [128 x 128] TMA -> 128B-swizzled smem ring (3 stages of one scale
+//                       group each: 128 contiguous bytes per weight row per
+//                       request, which HBM streams near its peak; 64-byte
+//                       pieces reach well under half of it)
+//      bf16 [128 x 64]  dequant warps -> 128B-swizzled K-major smem (4 slots,
+//                       filled in pairs: one int8 stage = two MMA stages)
 //   B  bf16 [NT x 64]   TMA tiles of 64 consecutive rows -> same layout (3 stages);
 //                       routed rows are consecutive because the activations are
 //                       permuted into route order first (permute_rows_kernel)
@@ -37,13 +41,15 @@
 namespace lmoe {
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;
-constexpr int kNS8 = 6;
-constexpr int kNS = 3;
+constexpr int kBK = 64;    // MMA stage: one 128-byte swizzle atom of 16-bit K values
+constexpr int kBK8 = 128;  // int8 stage: one scale group
+constexpr int kNS8 = 3;    // int8 stages
+constexpr int kNA = 4;     // bf16 A slots (two pairs)
+constexpr int kNS = 3;     // activation stages
 constexpr int kGemmThreads = 512;
 constexpr int kDeqWarp0 = 4, kDeqWarps = 8;
 constexpr int kEpiWarp0 = 12;
-constexpr int kA8Bytes = kBM * kBK;
+constexpr int kA8Bytes = kBM * kBK8;
 constexpr int kA16Bytes = kBM * kBK * 2;
 constexpr int kBBytes = kTileRoutes * kBK * 2;
 constexpr int kTmemCols = 512;   // two 256-column accumulators
@@ -73,15 +79,17 @@ struct GemmParams {
 struct GemmSmem {
   static constexpr int a8 = 0;
   static constexpr int a16 = a8 + kNS8 * kA8Bytes;
-  static constexpr int b = a16 + kNS * kA16Bytes;
+  static constexpr int b = a16 + kNA * kA16Bytes;
   static constexpr int stg = b + kNS * kBBytes;
   static constexpr int bars = stg + 2 * kStgBytes;
-  // full8, empty8 (kNS8 each); full16, fullB, emptyAB (kNS each); tfull, tempty (2 each); drain
-  static constexpr int nbars = 2 * kNS8 + 3 * kNS + 4 + 1;
+  // full8, empty8 (kNS8 each); fullA, emptyA (one per slot pair); fullB, emptyB (kNS each);
+  // tfull, tempty (2 each); drain
+  static constexpr int nbars = 2 * kNS8 + 2 * (kNA / 2) + 2 * kNS + 4 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int bytes = misc + 64;
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
 };
+static_assert(GemmSmem::alloc <= 232448, "shared memory per block");
 
 // A work unit: one tile of routes of one expert x one block of output columns.
 struct Unit {
@@ -142,21 +150,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* sTmem = (uint32_t*)(smem + GemmSmem::misc);
   volatile int* sAbort = (volatile int*)(smem + GemmSmem::misc + 8);
 
+  constexpr int kPairs = kNA / 2;
   auto full8 = [&](int s) { return bar0 + 8u * s; };
   auto empty8 = [&](int s) { return bar0 + 8u * (kNS8 + s); };
-  auto full16 = [&](int s) { return bar0 + 8u * (2 * kNS8 + s); };
-  auto fullB = [&](int s) { return bar0 + 8u * (2 * kNS8 + kNS + s); };
-  auto emptyAB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kNS + s); };
-  auto tfull = [&](int b) { return bar0 + 8u * (2 * kNS8 + 3 * kNS + b); };
-  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 3 * kNS + 2 + b); };
-  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 3 * kNS + 4);
+  auto fullA = [&](int q) { return bar0 + 8u * (2 * kNS8 + q); };
+  auto emptyA = [&](int q) { return bar0 + 8u * (2 * kNS8 + kPairs + q); };
+  auto fullB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + s); };
+  auto emptyB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + kNS + s); };
+  auto tfull = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + b); };
+  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + 4);
 
   const bool swiglu = p.mode == kSwiGLU;
   const int64_t out_w = swiglu ? p.inter : p.N;
   const int cols_per_unit = swiglu ? 64 : kBM;
   const int nblocks = (int)((out_w + cols_per_unit - 1) / cols_per_unit);
-  const int KB = (int)(p.K / kBK);
-  const int G = (int)(p.K / kGroup);
+  const int KB = (int)(p.K / kBK);    // MMA stages per unit
+  const int KB8 = (int)(p.K / kBK8);  // int8 stages per unit (== scale groups)
+  const int G = KB8;
   const int warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
@@ -164,10 +175,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(full8(s), 1);
       mbar_init(empty8(s), kDeqWarps);
     }
+    for (int q = 0; q < kPairs; ++q) {
+      mbar_init(fullA(q), kDeqWarps);
+      mbar_init(emptyA(q), 1);
+    }
     for (int s = 0; s < kNS; ++s) {
-      mbar_init(full16(s), kDeqWarps);
       mbar_init(fullB(s), 1);
-      mbar_init(emptyAB(s), 1);
+      mbar_init(emptyB(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull(b), 1);
@@ -205,12 +219,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         unit_rows(p, un, rlo, rhi);
         const CUtensorMap* mlo = un.shared ? &tm_lo : &tm_bank;
         const CUtensorMap* mhi = un.shared ? (swiglu ? &tm_hi : &tm_lo) : &tm_bank;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = 0; kb < KB8; ++kb, ++it) {
           const int s8 = it % kNS8;
           if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(full8(s8), kA8Bytes);
-          tma_load_2d(sA8 + s8 * kA8Bytes, mlo, full8(s8), kb * kBK, (int)rlo);
-          tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, mhi, full8(s8), kb * kBK, (int)rhi);
+          tma_load_2d(sA8 + s8 * kA8Bytes, mlo, full8(s8), kb * kBK8, (int)rlo);
+          tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, mhi, full8(s8), kb * kBK8, (int)rhi);
         }
       }
       // never leave a bulk copy in flight into shared memory that is about to be released
@@ -220,7 +234,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int it = 0, ui = 0;
+      int it = 0, ia = 0, ui = 0;
       bool ok = true, issued = false;
       for (int u = blockIdx.x; ok; u += stride, ++ui) {
         Unit un;
@@ -231,19 +245,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait(tempty(b), ((ui >> 1) & 1) ^ 1, sAbort, p.err)) break;
         tc_fence_after();
         const uint32_t dt = tmem + (uint32_t)(b * 256);
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % kNS;
-          const uint32_t ph = (it / kNS) & 1;
-          if (!mbar_wait(full16(s), ph, sAbort, p.err)) { ok = false; break; }
-          if (!mbar_wait(fullB(s), ph, sAbort, p.err)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t ad = sdesc_k_sw128(sA16 + s * kA16Bytes);
-          const uint64_t bd = sdesc_k_sw128(sB + s * kBBytes);
+        for (int kb = 0; kb < KB && ok; kb += 2, ++ia) {
+          // one int8 stage = the A slot pair (2q, 2q + 1) = MMA stages kb and kb + 1
+          const int q = ia % kPairs;
+          if (!mbar_wait(fullA(q), (ia / kPairs) & 1, sAbort, p.err)) { ok = false; break; }
+          for (int h = 0; h < 2; ++h, ++it) {
+            const int s = it % kNS;
+            if (!mbar_wait(fullB(s), (it / kNS) & 1, sAbort, p.err)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t ad = sdesc_k_sw128(sA16 + (2 * q + h) * kA16Bytes);
+            const uint64_t bd = sdesc_k_sw128(sB + s * kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16(dt, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
-          mma_commit(emptyAB(s));
-          issued = true;
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              mma_f16(dt, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, ((kb + h) | kk) != 0);
+            mma_commit(emptyB(s));
+            issued = true;
+          }
+          if (ok) mma_commit(emptyA(q));
         }
         // also after an abort, so the epilogue's wait ends (a commit with no
         // MMA issued before it is not relied on to arrive)
@@ -267,7 +285,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int nbox = (un.count + 63) / 64;  // 64-row boxes covering the unit's NT rows
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % kNS;
-          if (!mbar_wait(emptyAB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+          if (!mbar_wait(emptyB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(fullB(s), (uint32_t)nbox * 8192u);
           const uint32_t dst = sB + s * kBBytes;
           for (int i = 0; i < nbox; ++i) tma_load_2d(dst + i * 8192, &tm_x, fullB(s), kb * kBK, un.start + 64 * i);
@@ -278,69 +296,92 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else if (warp >= kDeqWarp0 && warp < kDeqWarp0 + kDeqWarps) {
     // ------------------------------------------------------------ dequantise
+    // Thread (w, lane) converts 16-byte chunk c8 = lane & 7 (K values 16*c8 .. +15
+    // of the stage) of rows rb + 4i (i = 0..3), rb = 16w + (lane >> 3).  Eight
+    // lanes of a shared-memory phase read one whole 128-byte row: no bank
+    // conflicts under the 128-byte swizzle.  Chunks 0-3 go to the pair's first
+    // A slot (K 0..63), chunks 4-7 to the second; the two halves write their
+    // 16-byte pieces in opposite order, so a phase's stores never share banks.
     const int w = warp - kDeqWarp0;
-    const int c = lane & 3;
-    const int r0 = w * 16 + (lane >> 2);  // this thread converts rows r0 and r0 + 8
-    int it8 = 0, it = 0;
+    const int c8 = lane & 7;
+    const int hh = c8 >> 2, cc = c8 & 3;
+    const int rb = w * 16 + (lane >> 3);
+    int it8 = 0, ia = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok; u += stride) {
       Unit un;
       if (!get_unit(p, u, nblocks, un)) break;
       int64_t rlo, rhi;
       unit_rows(p, un, rlo, rhi);
-      // rows r0 and r0 + 8 lie in the same 64-row half (same source tensor)
-      const bool hi_half = r0 >= 64;
+      // the thread's 16 rows lie in one 64-row half (one source tensor)
+      const bool hi_half = rb >= 64;
       const float* sp = hi_half ? (un.shared ? (swiglu ? p.s_hi : p.s_lo) : p.s_bank) : (un.shared ? p.s_lo : p.s_bank);
       const int64_t rmax = hi_half ? (un.shared ? (swiglu ? p.rows_hi : p.rows_lo) : p.rows_bank)
                                    : (un.shared ? p.rows_lo : p.rows_bank);
-      const int64_t g0 = hi_half ? rhi + (r0 - 64) : rlo + r0;
-      const bool v0 = g0 < rmax, v1 = g0 + 8 < rmax;
-      const float* p0 = sp + g0 * G;
-      const float* p1 = sp + (g0 + 8) * G;
-      // group scales, fetched two groups ahead of use
-      float c0 = v0 ? __ldg(p0) : 0.f, c1 = v1 ? __ldg(p1) : 0.f;
-      float n0 = (G > 1 && v0) ? __ldg(p0 + 1) : 0.f, n1 = (G > 1 && v1) ? __ldg(p1 + 1) : 0.f;
-      float m0 = (G > 2 && v0) ? __ldg(p0 + 2) : 0.f, m1 = (G > 2 && v1) ? __ldg(p1 + 2) : 0.f;
-      for (int kb = 0; kb < KB; ++kb, ++it8, ++it) {
-        if (kb > 0 && (kb & 1) == 0) {  // entering group kb / 2
-          const int g = kb >> 1;
-          c0 = n0;
-          c1 = n1;
-          n0 = m0;
-          n1 = m1;
-          m0 = (g + 2 < G && v0) ? __ldg(p0 + g + 2) : 0.f;
-          m1 = (g + 2 < G && v1) ? __ldg(p1 + g + 2) : 0.f;
+      const int64_t g0 = hi_half ? rhi + (rb - 64) : rlo + rb;
+      const float* ps[4];
+      bool vr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        vr[i] = g0 + 4 * i < rmax;
+        ps[i] = sp + (g0 + 4 * i) * G;
+      }
+      // group scales, fetched two stages ahead of use
+      float sc[4], sn[4], sm[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sc[i] = vr[i] ? __ldg(ps[i]) : 0.f;
+        sn[i] = (G > 1 && vr[i]) ? __ldg(ps[i] + 1) : 0.f;
+        sm[i] = (G > 2 && vr[i]) ? __ldg(ps[i] + 2) : 0.f;
+      }
+      for (int g = 0; g < G; ++g, ++it8, ++ia) {
+        if (g > 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            sc[i] = sn[i];
+            sn[i] = sm[i];
+            sm[i] = (g + 2 < G && vr[i]) ? __ldg(ps[i] + g + 2) : 0.f;
+          }
         }
         const int s8 = it8 % kNS8;
-        const int s = it % kNS;
+        const int q = ia % kPairs;
         if (!warp_wait(full8(s8), (it8 / kNS8) & 1, sAbort, p.err)) { ok = false; break; }
-        if (!warp_wait(emptyAB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-        const uint8_t* a8 = smem + GemmSmem::a8 + s8 * kA8Bytes;
-        uint8_t* a16 = smem + GemmSmem::a16 + s * kA16Bytes;
-        const uint4 va = *reinterpret_cast<const uint4*>(a8 + r0 * 64 + c * 16);
-        const uint4 vb = *reinterpret_cast<const uint4*>(a8 + (r0 + 8) * 64 + c * 16);
+        const uint32_t a8 = sA8 + s8 * kA8Bytes;
+        uint4 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = rb + 4 * i;
+          v[i] = lds128(a8 + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty8(s8));
+        if (!warp_wait(emptyA(q), ((ia / kPairs) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+        const uint32_t a16 = sA16 + (uint32_t)((2 * q + hh) * kA16Bytes);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint4 v = h ? vb : va;
-          const float sc = h ? c1 : c0;
-          const int row = r0 + 8 * h;
-          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+        for (int i = 0; i < 4; ++i) {
+          const int r = rb + 4 * i;
+          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
           uint32_t o[8];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float f0, f1, f2, f3;
             i8x4_to_f32(wv[j], f0, f1, f2, f3);
-            o[2 * j] = A::pack(__fmul_rn(f0, sc), __fmul_rn(f1, sc));
-            o[2 * j + 1] = A::pack(__fmul_rn(f2, sc), __fmul_rn(f3, sc));
+            o[2 * j] = A::pack(__fmul_rn(f0, sc[i]), __fmul_rn(f1, sc[i]));
+            o[2 * j + 1] = A::pack(__fmul_rn(f2, sc[i]), __fmul_rn(f3, sc[i]));
           }
-          *reinterpret_cast<uint4*>(a16 + sw128_off(row, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(a16 + sw128_off(row, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+          const uint4 lo = make_uint4(o[0], o[1], o[2], o[3]), hi = make_uint4(o[4], o[5], o[6], o[7]);
+          const uint32_t d0 = a16 + sw128_off(r, 2 * cc), d1 = a16 + sw128_off(r, 2 * cc + 1);
+          if (hh == 0) {
+            sts128(d0, lo);
+            sts128(d1, hi);
+          } else {
+            sts128(d1, hi);
+            sts128(d0, lo);
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(full16(s));
+        if (lane == 0) mbar_arrive(fullA(q));
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -471,17 +512,17 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// int8 [rows, K] row-major, box = 64 rows x 64 bytes, no swizzle
+// int8 [rows, K] row-major, box = 64 rows x 128 bytes (one scale group), 128-byte swizzle
 static int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return LMOE_ERR_CUDA;
   if (((uintptr_t)base & 15) || (K % 16) || rows <= 0) return LMOE_ERR_INVALID;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {(cuuint32_t)kBK8, 64};
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)base, dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
 }

@@ -8,28 +8,30 @@
 // and multiplied into an fp32 accumulator; the output is stored in the
 // activation dtype.
 //
-// Layout ("swap AB"): the MMA's M side is 128 weight rows, its N side is a
-// tile's routes (16..256, a multiple of 16), K streams in 64-wide MMA stages.
-//   A  int8 [128 x 128] TMA -> 128B-swizzled smem ring (3 stages of one scale
-//                       group each: 128 contiguous bytes per weight row per
-//                       request, which HBM streams near its peak; 64-byte
-//                       pieces reach well under half of it)
+// Layout: the MMA's M side is a tile of 128 routes (token rows, already in
+// route order after permute_rows_kernel), its N side is 128 weight rows of one
+// expert, K streams in 64-wide MMA stages:
+//   W  int8 [128 x 128] TMA -> 128B-swizzled smem ring (one scale group per
+//                       stage: 128 contiguous bytes per weight row per request,
+//                       which HBM streams near its peak)
 //      bf16 [128 x 64]  dequant warps -> 128B-swizzled K-major smem (4 slots,
-//                       filled in pairs: one int8 stage = two MMA stages)
-//   B  bf16 [NT x 64]   TMA tiles of 64 consecutive rows -> same layout (3 stages);
-//                       routed rows are consecutive because the activations are
-//                       permuted into route order first (permute_rows_kernel)
-//   D  fp32 [128 lanes x 256 cols] in tensor memory, two buffers
+//                       filled in pairs: one int8 stage = two MMA stages); the
+//                       MMA's B operand
+//   X  bf16 [128 x 64]  TMA tiles of 128 consecutive route rows -> same layout
+//                       (the MMA's A operand)
+//   D  fp32 [128 token lanes x 128 weight columns] in tensor memory, 4 buffers
+// so an epilogue thread owns one route row and finds that row's output
+// columns contiguous in its tensor-memory lane: it stores 16-byte vectors,
+// with no shuffles or shared-memory transposes.
 // The kernel is persistent: one CTA per SM walks the (tile, column-block)
-// work units in a fixed stride, so the epilogue of one unit overlaps the
-// main loop of the next (the MMA issuer alternates TMEM buffers).
+// work units in a fixed stride, so the epilogue of one unit overlaps the main
+// loop of the next ones.
 // Warp roles (512 threads): w0 weight TMA, w1 TMEM owner + MMA issuer,
 // w2 activation TMA, w3 idle, w4-11 dequantisers, w12-15 epilogue.
-// Activations: row r of a unit is x[start + r] (no gather inside the GEMM).
-// Epilogue modes: PLAIN (y = round(acc)), SWIGLU (gate rows 0-63 and up rows
-// 64-127 of the unit give hidden = round(round(silu(g)) * u), the reference's
-// gpu_routes.py:74-75), WEIGHTED (v = round(round(acc) * w_route), the
-// per-route product of prefill._reduce, prefill.py:45).
+// Epilogue modes: PLAIN (y = round(acc)), SWIGLU (gate columns 0-63 and up
+// columns 64-127 of the unit give hidden = round(round(silu(g)) * u), the
+// reference's gpu_routes.py:74-75), WEIGHTED (v = round(round(acc) * w_route),
+// the per-route product of prefill._reduce, prefill.py:45).
 // Every wait is bounded (LMOE_WAIT_NS); a timeout raises the CTA abort flag
 // and the caller's error word, every role drains and the CTA exits.
 #include <mutex>
@@ -43,18 +45,18 @@ namespace lmoe {
 constexpr int kBM = 128;
 constexpr int kBK = 64;    // MMA stage: one 128-byte swizzle atom of 16-bit K values
 constexpr int kBK8 = 128;  // int8 stage: one scale group
-constexpr int kNS8 = 3;    // int8 stages
-constexpr int kNA = 4;     // bf16 A slots (two pairs)
-constexpr int kNS = 3;     // activation stages
+constexpr int kNS8 = 4;    // int8 weight stages
+constexpr int kNA = 4;     // bf16 weight slots (two pairs)
+constexpr int kNS = 6;     // activation stages
 constexpr int kGemmThreads = 512;
 constexpr int kDeqWarp0 = 4, kDeqWarps = 8;
 constexpr int kEpiWarp0 = 12;
 constexpr int kA8Bytes = kBM * kBK8;
 constexpr int kA16Bytes = kBM * kBK * 2;
 constexpr int kBBytes = kTileRoutes * kBK * 2;
-constexpr int kTmemCols = 512;   // two 256-column accumulators
-constexpr int kStageTok = 32;    // epilogue chunk (tokens)
-constexpr int kStgBytes = kStageTok * kBM * 2;
+constexpr int kTmemBufs = 4;                 // accumulator buffers
+constexpr int kTmemCols = kTmemBufs * kBM;   // 4 x 128 fp32 columns
+static_assert(kTileRoutes == 128, "the MMA M extent is the route tile");
 
 struct GemmParams {
   int64_t K;
@@ -80,15 +82,16 @@ struct GemmSmem {
   static constexpr int a8 = 0;
   static constexpr int a16 = a8 + kNS8 * kA8Bytes;
   static constexpr int b = a16 + kNA * kA16Bytes;
-  static constexpr int stg = b + kNS * kBBytes;
-  static constexpr int bars = stg + 2 * kStgBytes;
+  static constexpr int bars = b + kNS * kBBytes;
   // full8, empty8 (kNS8 each); fullA, emptyA (one per slot pair); fullB, emptyB (kNS each);
-  // tfull, tempty (2 each); drain
-  static constexpr int nbars = 2 * kNS8 + 2 * (kNA / 2) + 2 * kNS + 4 + 1;
+  // tfull, tempty (kTmemBufs each); drain
+  static constexpr int nbars = 2 * kNS8 + 2 * (kNA / 2) + 2 * kNS + 2 * kTmemBufs + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int bytes = misc + 64;
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
 };
+static_assert(GemmSmem::alloc <= 232448, "shared memory per block");
+
 static_assert(GemmSmem::alloc <= 232448, "shared memory per block");
 
 // A work unit: one tile of routes of one expert x one block of output columns.
@@ -158,8 +161,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   auto fullB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + s); };
   auto emptyB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + kNS + s); };
   auto tfull = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + b); };
-  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + 2 + b); };
-  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + 4);
+  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + kTmemBufs + b); };
+  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 2 * kPairs + 2 * kNS + 2 * kTmemBufs);
 
   const bool swiglu = p.mode == kSwiGLU;
   const int64_t out_w = swiglu ? p.inter : p.N;
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(fullB(s), 1);
       mbar_init(emptyB(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTmemBufs; ++b) {
       mbar_init(tfull(b), 1);
       mbar_init(tempty(b), 4);
     }
@@ -239,12 +242,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int u = blockIdx.x; ok; u += stride, ++ui) {
         Unit un;
         if (!get_unit(p, u, nblocks, un)) break;
-        const int NT = (un.count + 15) & ~15;
-        const uint32_t idesc = idesc_f16(DT == LMOE_BF16 ? 1 : 0, kBM, NT);
-        const int b = ui & 1;
-        if (!mbar_wait(tempty(b), ((ui >> 1) & 1) ^ 1, sAbort, p.err)) break;
+        const uint32_t idesc = idesc_f16(DT == LMOE_BF16 ? 1 : 0, kTileRoutes, kBM);
+        const int b = ui % kTmemBufs;
+        if (!mbar_wait(tempty(b), ((ui / kTmemBufs) & 1) ^ 1, sAbort, p.err)) break;
         tc_fence_after();
-        const uint32_t dt = tmem + (uint32_t)(b * 256);
+        const uint32_t dt = tmem + (uint32_t)(b * kBM);
         for (int kb = 0; kb < KB && ok; kb += 2, ++ia) {
           // one int8 stage = the A slot pair (2q, 2q + 1) = MMA stages kb and kb + 1
           const int q = ia % kPairs;
@@ -253,11 +255,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int s = it % kNS;
             if (!mbar_wait(fullB(s), (it / kNS) & 1, sAbort, p.err)) { ok = false; break; }
             tc_fence_after();
-            const uint64_t ad = sdesc_k_sw128(sA16 + (2 * q + h) * kA16Bytes);
-            const uint64_t bd = sdesc_k_sw128(sB + s * kBBytes);
+            // A = the route rows (activations), B = the dequantised weight rows
+            const uint64_t wd = sdesc_k_sw128(sA16 + (2 * q + h) * kA16Bytes);
+            const uint64_t xd = sdesc_k_sw128(sB + s * kBBytes);
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
-              mma_f16(dt, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, ((kb + h) | kk) != 0);
+              mma_f16(dt, xd + (uint64_t)(kk * 2), wd + (uint64_t)(kk * 2), idesc, ((kb + h) | kk) != 0);
             mma_commit(emptyB(s));
             issued = true;
           }
@@ -282,13 +285,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int u = blockIdx.x; ok; u += stride) {
         Unit un;
         if (!get_unit(p, u, nblocks, un)) break;
-        const int nbox = (un.count + 63) / 64;  // 64-row boxes covering the unit's NT rows
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % kNS;
           if (!mbar_wait(emptyB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-          mbar_arrive_expect_tx(fullB(s), (uint32_t)nbox * 8192u);
-          const uint32_t dst = sB + s * kBBytes;
-          for (int i = 0; i < nbox; ++i) tma_load_2d(dst + i * 8192, &tm_x, fullB(s), kb * kBK, un.start + 64 * i);
+          // 128 route rows from the tile's first; rows past the tile belong to other
+          // tiles (or lie past the tensor and read as zeros) and are never stored
+          mbar_arrive_expect_tx(fullB(s), (uint32_t)kBBytes);
+          tma_load_2d(sB + s * kBBytes, &tm_x, fullB(s), kb * kBK, un.start);
         }
       }
       for (int k = max(0, it - kNS); k < it; ++k) mbar_wait_drain(fullB(k % kNS), (k / kNS) & 1, p.err);
@@ -353,8 +356,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int r = rb + 4 * i;
           v[i] = lds128(a8 + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty8(s8));
+
         if (!warp_wait(emptyA(q), ((ia / kPairs) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
         const uint32_t a16 = sA16 + (uint32_t)((2 * q + hh) * kA16Bytes);
 #pragma unroll
@@ -382,103 +384,89 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(fullA(q));
+        // The int8 slot is handed back only now, after the converted weights
+        // were published.  Handing it back right after the loads (even with
+        // the arrive made data-dependent on every loaded value) gave
+        // run-to-run differences confined to weight-row pairs of single
+        // dequantiser half-warps; this ordering gave none in repeated runs.
+        if (lane == 0) mbar_arrive(empty8(s8));
       }
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp - kEpiWarp0;              // TMEM lane quadrant (== warp % 4)
-    const int e = threadIdx.x - kEpiWarp0 * 32;  // 0..127
-    const int row = q * 32 + lane;               // weight row of this thread in the unit
+    // Thread (q, lane) owns TMEM lane tok = route row start + tok of the unit;
+    // its columns are the unit's output columns col0 .. col0 + 127 (SWIGLU:
+    // gate 0-63, up 64-127 for hidden columns col0 .. col0 + 63).
+    const int q = warp - kEpiWarp0;  // TMEM lane quadrant (== warp % 4)
+    const int tok = q * 32 + lane;
     typename A::T* y = (typename A::T*)p.y;
-    uint16_t* stg0 = (uint16_t*)(smem + GemmSmem::stg);
-    volatile uint32_t* sHave = (volatile uint32_t*)(sTmem + 1);
-    int ui = 0, chunk_ctr = 0;
+    const bool vec_ok = ((p.ldy & 7) == 0) && ((((uintptr_t)p.y) & 15) == 0);
+    int ui = 0;
     for (int u = blockIdx.x;; u += stride, ++ui) {
       Unit un;
       if (!get_unit(p, u, nblocks, un)) break;
-      const int b = ui & 1;
-      // one thread waits (bounded); the group follows through a named barrier,
-      // so all 128 threads take the same path
-      if (e == 0) *sHave = mbar_wait_drain(tfull(b), (ui >> 1) & 1, p.err) ? 1u : 0u;
-      named_barrier(1, 128);
-      const bool have = *sHave != 0;
-      named_barrier(1, 128);
+      const int b = ui % kTmemBufs;
+      int okw = 1;
+      if (lane == 0) okw = mbar_wait_drain(tfull(b), (ui / kTmemBufs) & 1, p.err) ? 1 : 0;
+      const bool have = __shfl_sync(0xffffffffu, okw, 0) != 0;
       tc_fence_after();
-      const int NT = (un.count + 15) & ~15;
+      const uint32_t taddr = tmem + (uint32_t)(b * kBM) + ((uint32_t)(q * 32) << 16);
       const int64_t col0 = (int64_t)un.nb * cols_per_unit;
       const int valid_cols = (out_w - col0) < cols_per_unit ? (int)(out_w - col0) : cols_per_unit;
-      const uint32_t taddr = tmem + (uint32_t)(b * 256) + ((uint32_t)(q * 32) << 16);
-      const bool weigh = (p.mode == kWeighted) && !un.shared;
-      for (int c0 = 0; c0 < NT; c0 += kStageTok, ++chunk_ctr) {
-        uint16_t* stg = stg0 + (chunk_ctr & 1) * (kStgBytes / 2);
-        uint32_t r[32];
-        tmem_ld32(taddr + c0, r);
-        tmem_ld_wait();
-        if (c0 + kStageTok >= NT) {  // last TMEM read of this unit: hand the buffer back
+      const bool live = have && tok < un.count;
+      typename A::T* yrow = y + (int64_t)(un.start + tok) * p.ldy + col0;
+      const int nchunks = swiglu ? 2 : kBM / 32;
+      float wt = 1.f;
+      if (live && p.mode == kWeighted && !un.shared) wt = __ldg(p.rweight + un.start + tok);
+      for (int c = 0; c < nchunks; ++c) {
+        const int c0 = c * 32;
+        uint32_t h[16];  // 32 output values, packed pairs
+        if (swiglu) {
+          uint32_t g[32], uu[32];
+          tmem_ld32(taddr + c0, g);
+          tmem_ld32(taddr + 64 + c0, uu);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float o[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const float gv = A::round(__uint_as_float(g[2 * j + t]));
+              const float up = A::round(__uint_as_float(uu[2 * j + t]));
+              const float sl = A::round(__fdividef(gv, 1.0f + __expf(-gv)));
+              o[t] = __fmul_rn(sl, up);
+            }
+            h[j] = A::pack(o[0], o[1]);
+          }
+        } else {
+          uint32_t r[32];
+          tmem_ld32(taddr + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float o0 = A::round(__uint_as_float(r[2 * j])), o1 = A::round(__uint_as_float(r[2 * j + 1]));
+            if (p.mode == kWeighted) {
+              o0 = __fmul_rn(o0, wt);
+              o1 = __fmul_rn(o1, wt);
+            }
+            h[j] = A::pack(o0, o1);
+          }
+        }
+        if (c == nchunks - 1) {  // last TMEM read of this unit: hand the buffer back
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty(b));
         }
-        if (have) {
-          float wl = 1.f;
-          if (weigh && c0 + lane < un.count) wl = __ldg(p.rweight + un.start + c0 + lane);
-          // stage [token][row] in the activation dtype
+        if (!live || c0 >= valid_cols) continue;
+        if (vec_ok && c0 + 32 <= valid_cols) {
+          uint4* dst = reinterpret_cast<uint4*>(yrow + c0);
 #pragma unroll
-          for (int jj = 0; jj < kStageTok; ++jj) {
-            float v = A::round(__uint_as_float(r[jj]));
-            if (weigh) v = A::round(__fmul_rn(v, __shfl_sync(0xffffffffu, wl, jj)));
-            stg[jj * kBM + row] = A::bits(v);
-          }
-        }
-        // the next chunk uses the other staging buffer, and the barrier of the
-        // chunk after that orders its writes behind these reads
-        named_barrier(1, 128);
-        if (have) {
-          const int ntok = min(kStageTok, un.count - c0);
-          if (!swiglu) {
-            // 4 threads per token row, 32 columns (64 B) each
-            const int j = e >> 2, cb = (e & 3) * 32;
-            if (j < ntok) {
-              typename A::T* dst = y + (int64_t)(un.start + c0 + j) * p.ldy + col0 + cb;
-              const uint16_t* src = stg + j * kBM + cb;
-              if (valid_cols == kBM && (p.ldy % 8) == 0) {
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(h[4 * v], h[4 * v + 1], h[4 * v + 2], h[4 * v + 3]);
+        } else {
 #pragma unroll
-                for (int v = 0; v < 4; ++v)
-                  reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(src)[v];
-              } else {
-                for (int v = 0; v < 32; ++v)
-                  if (cb + v < valid_cols) reinterpret_cast<uint16_t*>(dst)[v] = src[v];
-              }
-            }
-          } else {
-            // hidden = round(round(silu(gate)) * up): 4 threads per token, 16 columns each
-            const int j = e >> 2, cb = (e & 3) * 16;
-            if (j < ntok) {
-              uint32_t hv[8];
-#pragma unroll
-              for (int v = 0; v < 8; ++v) {
-                float h2[2];
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                  const int col = cb + 2 * v + t;
-                  const float g = A::lo_f((uint32_t)stg[j * kBM + col]);
-                  const float up = A::lo_f((uint32_t)stg[j * kBM + 64 + col]);
-                  const float sl = A::round(__fdividef(g, 1.0f + __expf(-g)));
-                  h2[t] = __fmul_rn(sl, up);
-                }
-                hv[v] = A::pack(h2[0], h2[1]);
-              }
-              typename A::T* dst = y + (int64_t)(un.start + c0 + j) * p.ldy + col0 + cb;
-              if (valid_cols == 64 && (p.ldy % 8) == 0) {
-                reinterpret_cast<uint4*>(dst)[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                reinterpret_cast<uint4*>(dst)[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
-              } else {
-                for (int v = 0; v < 16; ++v)
-                  if (cb + v < valid_cols)
-                    reinterpret_cast<uint16_t*>(dst)[v] = (uint16_t)((hv[v >> 1] >> (16 * (v & 1))) & 0xffffu);
-              }
-            }
-          }
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < valid_cols)
+              reinterpret_cast<uint16_t*>(yrow)[c0 + j] = (uint16_t)((h[j >> 1] >> (16 * (j & 1))) & 0xffffu);
         }
       }
       if (!have) break;  // the MMA issuer gave up: stop instead of waiting on every later unit
@@ -535,7 +523,7 @@ static int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t 
   if (((uintptr_t)base & 15) || (K % 64) || rows <= 0) return LMOE_ERR_INVALID;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {64, (cuuint32_t)kTileRoutes};
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(m, dtype == LMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   (void*)base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

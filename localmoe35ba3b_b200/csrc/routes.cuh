@@ -4,7 +4,7 @@
 
 namespace lmoe {
 
-constexpr int kTileRoutes = 256;  // routes (tokens) per GEMM tile: the MMA N extent
+constexpr int kTileRoutes = 128;  // routes (tokens) per GEMM tile: the MMA M extent
 
 struct __align__(16) Tile {
   int32_t expert;  // expert id; == experts for the shared-expert segment

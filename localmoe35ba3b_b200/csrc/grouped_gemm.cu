@@ -373,13 +373,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           const uint4 lo = make_uint4(o[0], o[1], o[2], o[3]), hi = make_uint4(o[4], o[5], o[6], o[7]);
           const uint32_t d0 = a16 + sw128_off(r, 2 * cc), d1 = a16 + sw128_off(r, 2 * cc + 1);
-          if (hh == 0) {
-            sts128(d0, lo);
-            sts128(d1, hi);
-          } else {
-            sts128(d1, hi);
-            sts128(d0, lo);
-          }
+          // selects, not a branch: a divergent branch would issue each store twice
+          // with half the lanes and double the shared-memory wavefronts
+          sts128(hh ? d1 : d0, hh ? hi : lo);
+          sts128(hh ? d0 : d1, hh ? lo : hi);
         }
         fence_proxy_async_smem();
         __syncwarp();

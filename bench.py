@@ -59,6 +59,7 @@ def parse():
     ap.add_argument('--tokens', type=int, default=2048)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--seed', type=int, default=0)
+    ap.add_argument('--no-extra', action='store_true', help='skip the decode (C3) and dense-sweep (C4) legs')
     return ap.parse_args()
 
 
@@ -283,6 +284,10 @@ def run_ours(a, rank, world, local):
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline_leg()
+    extra = {}
+    if not a.no_extra:
+        extra['c3_decode'] = decode_leg(layers, dev, peaks, max(3, a.steps), a.warmup, a.seed + 1000 * rank)
+        extra['c4_dense'] = dense_leg(dev, peaks)
 
     line = {
         'metric': METRIC, 'value': round(value, 1), 'unit': UNIT, 'n_gpus': world, 'steps': a.steps,
@@ -297,8 +302,121 @@ def run_ours(a, rank, world, local):
         'roofline': roof, 'cpu_baseline': cpu, 'e2e': e2e,
         'gpu_launches': LAUNCHES_PER_LAYER * a.layers * a.steps, 'clocks': clk.summary(),
     }
+    if extra:
+        line['extra'] = extra
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def decode_leg(layers, dev, peaks, steps, warmup, seed):
+    """C3: one-token decode through all layers (W8A8 routed experts + W8A16 shared
+    expert + gate + residual), captured once in a CUDA graph and replayed; per-layer
+    time and the HBM roofline of its 9 x 3,244,032 weight bytes."""
+    from localmoe35ba3b_b200.runtime import decode
+    g = torch.Generator(device=dev).manual_seed(seed + 7)
+    L = len(layers)
+    ids, wts = [], []
+    for _ in range(L):
+        ranks = torch.randperm(EXPERTS, generator=g, device=dev).float() + 1
+        logits = torch.randn((1, EXPERTS), generator=g, device=dev) - 1.1 * torch.log(ranks)[None]
+        p = torch.softmax(logits, dim=-1, dtype=torch.float32)
+        w, i = torch.topk(p, TOP, dim=-1)
+        ids.append(i.contiguous())
+        wts.append((w / w.sum(-1, keepdim=True)).contiguous())
+    x0 = torch.randn((1, HIDDEN), generator=g, device=dev).bfloat16()
+
+    def step():
+        x = x0
+        for l, (bank, shared, gate) in enumerate(layers):
+            x = decode.decode_block(x, wts[l], ids[l], bank, shared=shared, shared_gate_weight=gate, residual=x)
+        return x
+
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(warmup):
+        graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us_layer = e0.elapsed_time(e1) * 1e3 / (steps * L)
+    del graph
+    wbytes = 9 * EXPERT_BYTES
+    gbs = wbytes / (us_layer * 1e-6) / 1e9
+    return {'us_per_layer': round(us_layer, 2), 'tok_per_s': round(1e6 / (us_layer * L), 1),
+            'weight_bytes_per_layer': wbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peaks['hbm'],
+            'hbm_frac': round(gbs / peaks['hbm'], 4), 'launches_per_layer': 7,
+            'workload': f'1 token x {L} layers, 8 routed (W8A8) + shared (W8A16) experts, one CUDA graph',
+            'l2': f'{L} layers of weights ({L * 9 * EXPERT_BYTES / 1e9:.2f} GB touched per step) exceed L2'}
+
+
+def _graph_time(fn, iters, dev):
+    """Device time per call of fn(i), i = 0..iters-1, captured in one CUDA graph (so
+    host launch overhead between the calls is not timed) and replayed after warm-up."""
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / iters
+
+
+def dense_leg(dev, peaks, iters=20):
+    """C4: W8A16 dense linear sweep K=2048, N in {512,2048,4096,8192}, M in {1,16,256,2048}
+    (and the W8A8 table GEMV at M=1).  Weight copies rotate so each iteration reads
+    weights from HBM (the pool of copies exceeds L2)."""
+    from localmoe35ba3b_b200.operators import int8 as I8
+    from localmoe35ba3b_b200.operators import w8a8 as W8
+    K = 2048
+    out = []
+    for n in (512, 2048, 4096, 8192):
+        wb = n * K + n * (K // 128) * 4
+        copies = max(2, -(-256 * 2 ** 20 // wb))
+        qs = [torch.randint(-127, 128, (n, K), dtype=torch.int8, device=dev) for _ in range(copies)]
+        ss = [torch.rand((n, K // 128), device=dev) * 1e-3 for _ in range(copies)]
+        for m in (1, 16, 256, 2048):
+            x = torch.randn((m, K), device=dev).bfloat16()
+            us = _graph_time(lambda i: I8.linear(x, qs[i % copies], ss[i % copies]), iters, dev)
+            flops = 2.0 * m * n * K
+            bytes_ = wb + 2 * m * K + 2 * m * n
+            tf, gbs = flops / (us * 1e-6) / 1e12, bytes_ / (us * 1e-6) / 1e9
+            bound = 'tensor' if flops / (peaks['tc'] * 1e12) > bytes_ / (peaks['hbm'] * 1e9) else 'hbm'
+            frac = tf / peaks['tc'] if bound == 'tensor' else gbs / peaks['hbm']
+            out.append({'op': 'w8a16', 'M': m, 'N': n, 'K': K, 'us': round(us, 2), 'tflops': round(tf, 2),
+                        'gbs': round(gbs, 1), 'bound': bound, 'frac': round(frac, 4)})
+        # W8A8 at M=1: the table-driven GEMV over one descriptor row (the weight itself)
+        x = torch.randn((1, K), device=dev).bfloat16()
+        tabs = [torch.tensor([[q.data_ptr(), s.data_ptr(), q.data_ptr(), s.data_ptr(), 0]], dtype=torch.int64,
+                             device=dev) for q, s in zip(qs, ss)]
+        us = _graph_time(lambda i: W8.grouped_linear(x, tabs[i % copies], 1, n, 0, True), iters, dev)
+        gbs = (wb + 2 * K + 2 * n) / (us * 1e-6) / 1e9
+        out.append({'op': 'w8a8', 'M': 1, 'N': n, 'K': K, 'us': round(us, 2), 'gbs': round(gbs, 1), 'bound': 'hbm',
+                    'frac': round(gbs / peaks['hbm'], 4)})
+        del qs, ss, tabs
+    return out
 
 
 def load_peaks():

@@ -40,6 +40,7 @@ extern "C" {
 #define LMOE_ERR_UNSUPPORTED (-3)
 
 #define LMOE_DEVERR_TIMEOUT 1
+#define LMOE_DEVERR_BAD_EXPERT 2 /* an expert id outside [0, experts): read as expert 0 */
 #define LMOE_ERR_TIMEOUT LMOE_DEVERR_TIMEOUT
 
 #define LMOE_BF16 0
@@ -139,6 +140,27 @@ LMOE_API int lmoe_routed_moe_noalloc(const void* x, const float* weights, const 
                             const float* sh_sg, const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd,
                             const float* sh_sd, const void* sh_gate_w, const void* residual, void* out,
                             int dtype, int* err, void* stream);
+
+/* One-token decode of the MoE block: replaces the decode branch of Int8Experts.forward
+ * (qwen35_deploy/operators/int8.py:158-187: the ids.cpu() sync, the descriptor table
+ * upload of int8.py:139-153/170-179, grouped_linear for gate_up, silu*up, grouped_linear
+ * for down, _ordered_reduce of int8.py:240-250) and, when sh_qg != NULL, the HF shared
+ * expert and its sigmoid gate (modeling_qwen3_5_moe.py:781-790, three Int8Linear calls).
+ * x [1, hidden]; ids [top] int64 and weights [top] fp32 (the router's row); banks as in
+ * lmoe_routed_moe; w8a8 != 0 selects the W8A8 grouped GEMV for the routed experts (the
+ * reference's --activation w8a8, cli.py:37-39), else W8A16; the shared expert always uses
+ * the W8A16 arithmetic of Int8Linear.  out [1, hidden] = ordered routed combine (+ gated
+ * shared) (+ residual).  The table is built on the device: no host synchronisation, so
+ * the call can be captured in a CUDA graph.  ws: lmoe_decode_workspace_size() bytes.
+ * An id outside [0, experts) sets LMOE_DEVERR_BAD_EXPERT in *err. */
+LMOE_API int64_t lmoe_decode_workspace_size(int64_t top, int64_t hidden, int64_t inter);
+LMOE_API int lmoe_decode_moe(const void* x, const float* weights, const int64_t* ids, int64_t top,
+                             const int8_t* qg, const float* sg, const int8_t* qd, const float* sd,
+                             int64_t experts, int64_t hidden, int64_t inter, const int8_t* sh_qg,
+                             const float* sh_sg, const int8_t* sh_qu, const float* sh_su,
+                             const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w,
+                             const void* residual, void* out, int dtype, int w8a8, void* ws, int* err,
+                             void* stream);
 
 #ifdef __cplusplus
 }

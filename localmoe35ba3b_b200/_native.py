@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, 'liblocalmoe_b200.so')
 BF16, F16 = 0, 1
 ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED = -1, -2, -3
 DEVERR_TIMEOUT = 1
+DEVERR_BAD_EXPERT = 2
 
 _P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
 
@@ -39,6 +40,9 @@ SIGNATURES = {
     'lmoe_routed_moe_noalloc_limit': (_I64, []),
     'lmoe_routed_moe_noalloc': (_I, [_P, _P, _P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64,
                                      _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P]),
+    'lmoe_decode_workspace_size': (_I64, [_I64, _I64, _I64]),
+    'lmoe_decode_moe': (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64,
+                             _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
 }
 
 _lib = None
@@ -111,7 +115,8 @@ def check_device_errors(device=None, reset=True):
     if reset and v:
         w.zero_()
     if v:
-        raise NativeError(f'device-side error bits 0x{v:x} (1 = a bounded wait timed out)')
+        raise NativeError(f'device-side error bits 0x{v:x} (1 = a bounded wait timed out, '
+                          '2 = an expert id out of range)')
     return 0
 
 

@@ -354,6 +354,15 @@ static int launch_grouped(const void* x, const int64_t* table, void* y, int64_t 
   return LMOE_OK;
 }
 
+namespace lmoe {
+// in-library launcher for the table-driven grouped GEMV (used by the decode chain)
+int lmoe_grouped_launch(bool w8a8, const void* x, const int64_t* table, void* y, int64_t experts, int64_t n,
+                        int64_t k, int field, int shared, int dtype, cudaStream_t st) {
+  return w8a8 ? launch_grouped<true>(x, table, y, experts, n, k, field, shared, dtype, nullptr, nullptr, st)
+              : launch_grouped<false>(x, table, y, experts, n, k, field, shared, dtype, nullptr, nullptr, st);
+}
+}  // namespace lmoe
+
 extern "C" int lmoe_grouped_linear_w8a16(const void* x, const int64_t* table, void* y, int64_t experts, int64_t n,
                                          int64_t k, int field, int shared, int dtype, void* stream) {
   return launch_grouped<false>(x, table, y, experts, n, k, field, shared, dtype, nullptr, nullptr, stream);

@@ -67,3 +67,35 @@ def ordered_reduce(values, table, weights, out):
     N.call('lmoe_ordered_reduce', N.ptr(v), N.ptr(table), N.ptr(w), N.ptr(out), v.shape[-1], v.shape[0],
            N.dtype_code(out.dtype), N.stream(v.device))
     return out
+
+
+class Int8Experts(torch.nn.Module):
+    """The routed experts of one MoE layer with the bank resident in HBM
+    (int8.py:127-210, the HF ``Qwen3_5MoeExperts`` module boundary).
+
+    ``forward(hidden_states, top_k_index, top_k_weights)`` returns the routed
+    output ``[T, H]``: one token runs the decode chain (device-built table,
+    grouped GEMVs, ordered combine; int8.py:158-187), more tokens run the
+    routed prefill GEMMs (gpu_routes.routed_moe).  ``activation`` selects the
+    decode GEMV arithmetic, like the reference's ``--activation`` switch
+    (cli.py:37-39): 'w8a16' (default, int8.grouped_linear) or 'w8a8'.
+    """
+
+    def __init__(self, gate_up_q, gate_up_scale, down_q, down_scale, activation='w8a16'):
+        super().__init__()
+        self.register_buffer('gate_up_q', gate_up_q)
+        self.register_buffer('gate_up_scale', gate_up_scale)
+        self.register_buffer('down_q', down_q)
+        self.register_buffer('down_scale', down_scale)
+        self.activation = activation
+
+    def banks(self):
+        return [self.gate_up_q, self.gate_up_scale, self.down_q, self.down_scale]
+
+    def forward(self, hidden_states, top_k_index, top_k_weights):
+        from ..runtime import decode, gpu_routes
+        if hidden_states.shape[0] == 1:
+            return decode.decode_block(hidden_states, top_k_weights, top_k_index, self.banks(),
+                                       activation=self.activation)
+        return gpu_routes.routed_moe(hidden_states, top_k_weights, top_k_index, self.banks())
+

@@ -42,9 +42,9 @@ UNIT = 'tok/s'
 LAUNCHES_PER_LAYER = 5
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
 # `ncu --set full` capture of layer 0 (`python bench.py --layers 2 --steps 1 --warmup 1
-# --no-cpu-baseline`, -k regex:grouped_gemm -s 4 -c 2): gate_up 419.7 MB + down 252.7 MB.
+# --no-cpu-baseline`, -k regex:grouped_gemm -s 4 -c 2): gate_up 429.1 MB + down 253.6 MB.
 # Per-layer work does not depend on the layer count, so no scaling is applied.
-NCU_TRAFFIC_PER_LAYER = 672.4e6
+NCU_TRAFFIC_PER_LAYER = 682.7e6
 NCU_TRAFFIC_SOURCE = ('ncu dram__bytes_read.sum + dram__bytes_write.sum, gate_up + down launches of one '
                       '2048-token layer; bytes per layer like alg_bytes_per_layer')
 

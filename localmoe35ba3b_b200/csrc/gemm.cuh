@@ -1,5 +1,6 @@
 // Host-side launch description of the tcgen05 grouped GEMM (grouped_gemm.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -34,6 +35,14 @@ struct GemmLaunch {
 };
 
 int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st);
+// gate_up with the SwiGLU epilogue on the TMEM-operand kernel (gemm_ts.cu)
+int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st);
+
+// tensor maps (grouped_gemm.cu): int8 [rows, K] with a 64-row x 128-byte, 128B-swizzled box;
+// 16-bit activations [rows, K] with a box_rows x 64-element, 128B-swizzled box
+int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K);
+int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int dtype, int box_rows);
+int sm_count();
 
 // out[r] = x[pos[r]] for r < rows; rows of k 16-bit elements (permute.cu)
 int launch_permute_rows(const void* x, const int32_t* pos, void* out, int64_t rows, int64_t k, cudaStream_t st);

@@ -1,0 +1,465 @@
+// gate_up of the routed experts (+ the shared expert) with the fused SwiGLU
+// epilogue, on tcgen05 MMAs whose A operand -- the dequantised weights --
+// lives in tensor memory.
+//
+// Replaces prefill._routed for gate_up plus the SiLU*up step
+// (qwen35_deploy/runtime/prefill.py:12-34, gpu_routes.py:39-44 and :74-75).
+// Arithmetic as the reference: w = round_dtype(float(q) * scale)
+// (int8.py:19-21, prefill.py:24-25) into an fp32 accumulator;
+// hidden = round(round(silu(round(gate))) * round(up)).
+//
+// Layout: the MMA's M side is 128 weight rows of one expert (64 gate rows and
+// the matching 64 up rows), its N side is a tile of <= 128 routes rounded up to
+// 16, K streams in 128-wide int8 stages (one scale group).
+//   W  int8 [128 x 128]  TMA -> 128B-swizzled smem ring
+//      bf16              dequant warps -> tensor memory (tcgen05.st): the MMA's
+//                        A operand, 64 columns per stage, 4 slots; weights never
+//                        pass through shared memory in 16-bit form
+//   X  bf16 [N x 64]     TMA boxes of 32 route rows -> 128B-swizzled smem ring:
+//                        the MMA's B operand
+//   D  fp32 [128 lanes x 128 columns] in tensor memory, two buffers
+// Shared-memory traffic per MAC is therefore the int8 tile (TMA write + one
+// read) and the route rows (TMA write + the MMA's read), about half of what an
+// MMA with both operands in shared memory needs; with N <= 128 the MMA time
+// scales with the tile's routes, so small experts cost little beyond their
+// weight stream.
+// Warp roles (512 threads): w0 weight TMA, w1 TMEM owner + MMA issuer,
+// w2 activation TMA, w3 idle, w4-11 dequantisers (warp w writes TMEM lanes of
+// quadrant w % 4, K half (w - 4) / 4), w12-15 epilogue (quadrant w % 4; gate
+// rows in w12-13, up rows in w14-15).
+// Every wait is bounded (LMOE_WAIT_NS); a timeout raises the CTA abort flag and
+// the caller's error word, every role drains and the CTA exits.
+#include "common.cuh"
+#include "gemm.cuh"
+#include "routes.cuh"
+
+namespace lmoe {
+namespace ts {
+
+constexpr int kBM = 128;       // weight rows per unit: MMA M
+constexpr int kBK8 = 128;      // int8 stage K (one scale group)
+constexpr int kNS8 = 6;        // int8 stages
+constexpr int kBKB = 64;       // activation stage K (one 128-byte swizzle atom)
+constexpr int kNSB = 6;        // activation stages
+constexpr int kNA = 4;         // tensor-memory A slots
+constexpr int kBoxRows = 32;   // activation TMA box rows
+constexpr int kThreads = 512;
+constexpr int kConvWarps = 8;
+constexpr int kA8Bytes = kBM * kBK8;              // 16 KB
+constexpr int kBBytes = kTileRoutes * kBKB * 2;   // 16 KB
+constexpr int kAccCols = kTileRoutes;             // fp32 accumulator columns per buffer
+constexpr int kACol0 = 2 * kAccCols;              // A slots follow the two accumulators
+constexpr int kASlotCols = kBK8 / 2;              // 64 columns hold 128 16-bit K values
+constexpr int kTmemCols = 512;
+constexpr int kUPitch = 80;                       // bytes per up row in the exchange buffer
+constexpr int kUBytes = 64 * kUPitch;             // [64 rows][32 routes] 16-bit, padded rows
+constexpr int kHBytes = 32 * 64 * 2;              // [32 routes][64 columns] 16-bit
+static_assert(kACol0 + kNA * kASlotCols <= kTmemCols, "tensor memory budget");
+
+struct Smem {
+  static constexpr int a8 = 0;
+  static constexpr int b = a8 + kNS8 * kA8Bytes;
+  static constexpr int u = b + kNSB * kBBytes;
+  static constexpr int h = u + 2 * kUBytes;
+  static constexpr int bars = h + 2 * kHBytes;
+  // full8, empty8 (kNS8 each); fullA, emptyA (kNA each); fullB, emptyB (kNSB each); tfull, tempty (2 each); drain
+  static constexpr int nbars = 2 * kNS8 + 2 * kNA + 2 * kNSB + 4 + 1;
+  static constexpr int misc = bars + nbars * 8;
+  static constexpr int bytes = misc + 64;
+  static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
+};
+static_assert(Smem::alloc <= 232448, "shared memory per block");
+
+struct Params {
+  int64_t K;               // hidden
+  int64_t inter;           // I: bank rows [0, I) gate, [I, 2I) up
+  const Tile* tiles;
+  const int32_t* hdr;
+  int64_t rows_bank;       // experts * 2I
+  int64_t rows_sh;         // rows of the shared gate / up tensors (I)
+  const float* s_bank;     // [experts * 2I, K/128]
+  const float* s_g;        // shared gate scales [I, K/128]
+  const float* s_u;        // shared up scales
+  int experts;             // tiles with expert == experts are the shared expert
+  void* y;                 // hidden [rows, I]
+  int64_t ldy;
+  int* err;
+};
+
+struct Unit {
+  int start, count, nb;
+  bool shared;
+  int64_t rlo, rhi;  // tensor-map rows of the gate and up halves
+};
+
+__device__ __forceinline__ bool get_unit(const Params& p, int u, int nblocks, Unit& o) {
+  const int t = u / nblocks;
+  if (t >= p.hdr[kHdrNumTiles]) return false;
+  const Tile tl = p.tiles[t];
+  o.nb = u - t * nblocks;
+  o.start = tl.start;
+  o.count = tl.count;
+  o.shared = tl.expert == p.experts;
+  const int64_t col = (int64_t)o.nb * 64;
+  const int64_t ebase = o.shared ? 0 : (int64_t)tl.expert * 2 * p.inter;
+  o.rlo = ebase + col;
+  o.rhi = (o.shared ? 0 : ebase + p.inter) + col;
+  return o.count > 0;
+}
+
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err) {
+  int ok = 1;
+  if (lane_id() == 0) ok = mbar_wait(bar, parity, abort, err) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ float silu_exact(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gate_up_ts_kernel(const __grid_constant__ CUtensorMap tm_bank, const __grid_constant__ CUtensorMap tm_g,
+                      const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_x,
+                      const Params p) {
+  using A = Act<DT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t sA8 = s_base + Smem::a8;
+  const uint32_t sB = s_base + Smem::b;
+  const uint32_t bar0 = s_base + Smem::bars;
+  uint32_t* sTmem = (uint32_t*)(smem + Smem::misc);
+  volatile uint32_t* sHave = (volatile uint32_t*)(smem + Smem::misc + 4);
+  volatile int* sAbort = (volatile int*)(smem + Smem::misc + 8);
+
+  auto full8 = [&](int s) { return bar0 + 8u * s; };
+  auto empty8 = [&](int s) { return bar0 + 8u * (kNS8 + s); };
+  auto fullA = [&](int s) { return bar0 + 8u * (2 * kNS8 + s); };
+  auto emptyA = [&](int s) { return bar0 + 8u * (2 * kNS8 + kNA + s); };
+  auto fullB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + s); };
+  auto emptyB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + kNSB + s); };
+  auto tfull = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 * kNSB + b); };
+  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 * kNSB + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 * kNSB + 4);
+
+  const int nblocks = (int)(p.inter / 64);
+  const int G = (int)(p.K / kBK8);
+  const int warp = warp_id(), lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNS8; ++s) {
+      mbar_init(full8(s), 1);
+      mbar_init(empty8(s), kConvWarps);
+    }
+    for (int s = 0; s < kNA; ++s) {
+      mbar_init(fullA(s), kConvWarps);
+      mbar_init(emptyA(s), 1);
+    }
+    for (int s = 0; s < kNSB; ++s) {
+      mbar_init(fullB(s), 1);
+      mbar_init(emptyB(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull(b), 1);
+      mbar_init(tempty(b), 4);
+    }
+    mbar_init(drain, 1);
+    *sAbort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_bank);
+    prefetch_tmap(&tm_g);
+    prefetch_tmap(&tm_u);
+  }
+  if (warp == 2 && lane == 0) prefetch_tmap(&tm_x);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(sTmem), kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const int stride = gridDim.x;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ weight TMA
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok; u += stride) {
+        Unit un;
+        if (!get_unit(p, u, nblocks, un)) break;
+        const CUtensorMap* mlo = un.shared ? &tm_g : &tm_bank;
+        const CUtensorMap* mhi = un.shared ? &tm_u : &tm_bank;
+        for (int g = 0; g < G; ++g, ++it) {
+          const int s8 = it % kNS8;
+          if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(full8(s8), kA8Bytes);
+          tma_load_2d(sA8 + s8 * kA8Bytes, mlo, full8(s8), g * kBK8, (int)un.rlo);
+          tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, mhi, full8(s8), g * kBK8, (int)un.rhi);
+        }
+      }
+      for (int k = max(0, it - kNS8); k < it; ++k) mbar_wait_drain(full8(k % kNS8), (k / kNS8) & 1, p.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int ia = 0, ib = 0, ui = 0;
+      bool ok = true, issued = false;
+      for (int u = blockIdx.x; ok; u += stride, ++ui) {
+        Unit un;
+        if (!get_unit(p, u, nblocks, un)) break;
+        const int NT = (un.count + 15) & ~15;
+        const uint32_t idesc = idesc_f16(DT == LMOE_BF16 ? 1 : 0, kBM, NT);
+        const int b = ui & 1;
+        if (!mbar_wait(tempty(b), ((ui >> 1) & 1) ^ 1, sAbort, p.err)) break;
+        tc_fence_after();
+        const uint32_t dt = tmem + (uint32_t)(b * kAccCols);
+        for (int g = 0; g < G && ok; ++g, ++ia) {
+          const int a = ia % kNA;
+          if (!mbar_wait(fullA(a), (ia / kNA) & 1, sAbort, p.err)) { ok = false; break; }
+          for (int h = 0; h < 2; ++h, ++ib) {
+            const int s = ib % kNSB;
+            if (!mbar_wait(fullB(s), (ib / kNSB) & 1, sAbort, p.err)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t bd = sdesc_k_sw128(sB + s * kBBytes);
+            const uint32_t acol = tmem + (uint32_t)(kACol0 + a * kASlotCols + h * 32);
+#pragma unroll
+            for (int kk = 0; kk < kBKB / 16; ++kk)
+              mma_f16_ts(dt, acol + (uint32_t)(kk * 8), bd + (uint64_t)(kk * 2), idesc, (g | h | kk) != 0);
+            mma_commit(emptyB(s));
+            issued = true;
+          }
+          if (ok) mma_commit(emptyA(a));
+        }
+        // also after an abort, so the epilogue's wait ends
+        if (issued) mma_commit(tfull(b));
+      }
+      if (issued) {
+        mma_commit(drain);
+        mbar_wait_drain(drain, 0, p.err);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ activation TMA
+    if (lane == 0) {
+      int ib = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok; u += stride) {
+        Unit un;
+        if (!get_unit(p, u, nblocks, un)) break;
+        // boxes of 32 route rows covering the tile; rows past the tile are read
+        // (other tiles' rows, or zeros past the tensor) but never stored
+        const int nbox = (un.count + kBoxRows - 1) / kBoxRows;
+        for (int g = 0; g < G && ok; ++g) {
+          for (int h = 0; h < 2; ++h, ++ib) {
+            const int s = ib % kNSB;
+            if (!mbar_wait(emptyB(s), ((ib / kNSB) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+            mbar_arrive_expect_tx(fullB(s), (uint32_t)(nbox * kBoxRows * kBKB * 2));
+            for (int i = 0; i < nbox; ++i)
+              tma_load_2d(sB + s * kBBytes + i * (kBoxRows * kBKB * 2), &tm_x, fullB(s), (g * 2 + h) * kBKB,
+                          un.start + kBoxRows * i);
+          }
+        }
+      }
+      for (int k = max(0, ib - kNSB); k < ib; ++k) mbar_wait_drain(fullB(k % kNSB), (k / kNSB) & 1, p.err);
+    }
+    __syncwarp();
+  } else if (warp >= 4 && warp < 4 + kConvWarps) {
+    // ------------------------------------------------------------ dequantise into tensor memory
+    // thread = weight row r of the unit (TMEM lane), K half kh of the stage:
+    // 4 x 16-byte loads (8 lanes of a phase read 8 rows at 8 different 16-byte
+    // positions under the swizzle: no bank conflicts), 64 products, one
+    // 32-column tensor-memory store
+    const int qd = warp & 3, kh = (warp - 4) >> 2;
+    const int r = qd * 32 + lane;
+    const uint32_t tl = tmem + ((uint32_t)(qd * 32) << 16);
+    int it8 = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok; u += stride) {
+      Unit un;
+      if (!get_unit(p, u, nblocks, un)) break;
+      const bool up = r >= 64;
+      const int64_t grow = (up ? un.rhi : un.rlo) + (r & 63);
+      const int64_t rmax = un.shared ? p.rows_sh : p.rows_bank;
+      const float* sp = (un.shared ? (up ? p.s_u : p.s_g) : p.s_bank) + grow * G;
+      const bool valid = grow < rmax;
+      float sc = valid ? __ldg(sp) : 0.f;
+      float sn = (G > 1 && valid) ? __ldg(sp + 1) : 0.f;
+      float sm = (G > 2 && valid) ? __ldg(sp + 2) : 0.f;
+      for (int g = 0; g < G; ++g, ++it8) {
+        const int s8 = it8 % kNS8;
+        const int a = it8 % kNA;
+        if (!warp_wait(full8(s8), (it8 / kNS8) & 1, sAbort, p.err)) { ok = false; break; }
+        const uint32_t a8 = sA8 + s8 * kA8Bytes + r * 128;
+        uint4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = lds128(a8 + (uint32_t)(((kh * 4 + j) ^ (r & 7)) << 4));
+        if (!warp_wait(emptyA(a), ((it8 / kNA) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+        uint32_t o[32];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t wv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            float f0, f1, f2, f3;
+            i8x4_to_f32(wv[m], f0, f1, f2, f3);
+            o[j * 8 + 2 * m] = A::pack(__fmul_rn(f0, sc), __fmul_rn(f1, sc));
+            o[j * 8 + 2 * m + 1] = A::pack(__fmul_rn(f2, sc), __fmul_rn(f3, sc));
+          }
+        }
+        tmem_st32(tl + (uint32_t)(kACol0 + a * kASlotCols + kh * 32), o);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(fullA(a));
+          mbar_arrive(empty8(s8));
+        }
+        sc = sn;
+        sn = sm;
+        sm = (g + 3 < G && valid) ? __ldg(sp + g + 3) : 0.f;
+      }
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ epilogue
+    // per 32-route chunk: the up warps (q = 2, 3) hand their rounded values to
+    // the gate warps (q = 0, 1; same lane = same hidden column) through shared
+    // memory; the gate warps form hidden, transpose it through shared memory to
+    // [route][column] and store 16-byte row pieces
+    const int q = warp - 12;
+    const int row = q * 32 + lane;
+    typename A::T* y = (typename A::T*)p.y;
+    uint8_t* ubase = smem + Smem::u;
+    uint8_t* hbase = smem + Smem::h;
+    int ui = 0, chunk = 0;
+    for (int u = blockIdx.x;; u += stride, ++ui) {
+      Unit un;
+      if (!get_unit(p, u, nblocks, un)) break;
+      const int b = ui & 1;
+      if (q == 0 && lane == 0) *sHave = mbar_wait_drain(tfull(b), (ui >> 1) & 1, p.err) ? 1u : 0u;
+      named_barrier(1, 128);
+      const bool have = *sHave != 0;
+      named_barrier(1, 128);
+      tc_fence_after();
+      const int NT = (un.count + 15) & ~15;
+      const int nch = (NT + 31) / 32;
+      const uint32_t taddr = tmem + (uint32_t)(b * kAccCols) + ((uint32_t)(q * 32) << 16);
+      const int64_t col0 = (int64_t)un.nb * 64;
+      for (int c = 0; c < nch; ++c, ++chunk) {
+        uint32_t acc[32];
+        tmem_ld32(taddr + (uint32_t)(c * 32), acc);
+        tmem_ld_wait();
+        if (c == nch - 1) {  // last tensor-memory read of this unit: hand the buffer back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty(b));
+        }
+        if (!have) continue;
+        uint8_t* ub = ubase + (chunk & 1) * kUBytes;
+        uint8_t* hb = hbase + (chunk & 1) * kHBytes;
+        if (q >= 2) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pk[j] = A::pack(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1]));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            sts128(smem_u32(ub + (row - 64) * kUPitch + k * 16), make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]));
+        }
+        named_barrier(2 + (q & 1), 64);
+        if (q < 2) {
+          uint32_t uu[16];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 t = lds128(smem_u32(ub + row * kUPitch + k * 16));
+            uu[4 * k] = t.x;
+            uu[4 * k + 1] = t.y;
+            uu[4 * k + 2] = t.z;
+            uu[4 * k + 3] = t.w;
+          }
+          uint16_t* hrow = reinterpret_cast<uint16_t*>(hb);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const float gv = A::round(__uint_as_float(acc[jj]));
+            const float upv = (jj & 1) ? A::hi_f(uu[jj >> 1]) : A::lo_f(uu[jj >> 1]);
+            const float sl = A::round(silu_exact(gv));
+            hrow[jj * 64 + row] = A::bits(__fmul_rn(sl, upv));
+          }
+          named_barrier(4, 64);
+          // 64 threads: route e >> 1, columns (e & 1) * 32 .. + 31
+          const int e = q * 32 + lane;
+          const int tok = e >> 1, half = e & 1;
+          const int ntok = min(32, un.count - c * 32);
+          if (tok < ntok) {
+            typename A::T* dst = y + (int64_t)(un.start + c * 32 + tok) * p.ldy + col0 + half * 32;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              reinterpret_cast<uint4*>(dst)[k] = lds128(smem_u32(hb + tok * 128 + half * 64 + k * 16));
+          }
+        }
+      }
+      if (!have) break;  // the MMA issuer gave up: stop instead of waiting on every later unit
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace ts
+
+int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st) {
+  if (L.mode != kSwiGLU || L.tiles == nullptr) return LMOE_ERR_INVALID;
+  if (L.K % kGroup || L.K <= 0 || L.inter % 64 || L.inter <= 0 || L.N != 2 * L.inter) return LMOE_ERR_INVALID;
+  if ((L.ldy % 8) != 0 || (((uintptr_t)L.y) & 15)) return LMOE_ERR_INVALID;
+  if (L.grid_tiles <= 0) return LMOE_OK;
+  CUtensorMap tb, tg, tu, tx;
+  int rc = make_int8_map(&tb, L.q_bank, L.experts * L.N, L.K);
+  if (rc) return rc;
+  tg = tb;
+  tu = tb;
+  if (L.q_lo && (rc = make_int8_map(&tg, L.q_lo, L.rows_lo, L.K))) return rc;
+  if (L.q_hi && (rc = make_int8_map(&tu, L.q_hi, L.rows_hi, L.K))) return rc;
+  if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype, ts::kBoxRows))) return rc;
+  ts::Params p = {};
+  p.K = L.K;
+  p.inter = L.inter;
+  p.tiles = L.tiles;
+  p.hdr = L.hdr;
+  p.rows_bank = L.experts * L.N;
+  p.rows_sh = L.q_lo ? L.rows_lo : 0;
+  p.s_bank = L.s_bank;
+  p.s_g = L.s_lo;
+  p.s_u = L.s_hi;
+  p.experts = (int)L.experts;
+  p.y = L.y;
+  p.ldy = L.ldy;
+  p.err = L.err;
+  const int64_t units = (L.inter / 64) * L.grid_tiles;
+  const int64_t sms = sm_count();
+  const int64_t ctas = units < sms ? units : sms;
+  const size_t smem = ts::Smem::alloc;
+  if (L.dtype == LMOE_BF16) {
+    auto k = ts::gate_up_ts_kernel<LMOE_BF16>;
+    LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, p);
+  } else if (L.dtype == LMOE_F16) {
+    auto k = ts::gate_up_ts_kernel<LMOE_F16>;
+    LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, p);
+  } else {
+    return LMOE_ERR_INVALID;
+  }
+  LMOE_CUDA_CHECK(cudaGetLastError());
+  return LMOE_OK;
+}
+
+}  // namespace lmoe

@@ -484,7 +484,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static EncodeTiledFn encode_fn() {
+EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -498,7 +498,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 // int8 [rows, K] row-major, box = 64 rows x 128 bytes (one scale group), 128-byte swizzle
-static int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K) {
+int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return LMOE_ERR_CUDA;
   if (((uintptr_t)base & 15) || (K % 16) || rows <= 0) return LMOE_ERR_INVALID;
@@ -514,13 +514,13 @@ static int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64
 
 // activations [rows, K] 16-bit, box of 64 rows x 64 elements (8 KB) with the
 // 128-byte swizzle: the B operand's K-major UMMA layout
-static int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int dtype) {
+int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int dtype, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return LMOE_ERR_CUDA;
   if (((uintptr_t)base & 15) || (K % 64) || rows <= 0) return LMOE_ERR_INVALID;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)kTileRoutes};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(m, dtype == LMOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   (void*)base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -528,7 +528,7 @@ static int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t 
   return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
 }
 
-static int sm_count() {
+int sm_count() {
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
@@ -545,7 +545,7 @@ int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st) {
   th = tb;
   if (L.q_lo && (rc = make_int8_map(&tl, L.q_lo, L.rows_lo, L.K))) return rc;
   if (L.q_hi && (rc = make_int8_map(&th, L.q_hi, L.rows_hi, L.K))) return rc;
-  if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype))) return rc;
+  if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype, kTileRoutes))) return rc;
   GemmParams p = {};
   p.K = L.K;
   p.tiles = L.tiles;

@@ -178,7 +178,7 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   g.mode = kSwiGLU;
   g.dtype = dtype;
   g.err = err;
-  if ((rc = launch_grouped_gemm(g, st))) return rc;
+  if ((rc = launch_swiglu_ts(g, st))) return rc;
   if ((rc = mark(2))) return rc;
 
   GemmLaunch d = g;

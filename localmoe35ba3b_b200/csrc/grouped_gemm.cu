@@ -54,6 +54,7 @@ constexpr int kEpiWarp0 = 12;
 constexpr int kA8Bytes = kBM * kBK8;
 constexpr int kA16Bytes = kBM * kBK * 2;
 constexpr int kBBytes = kTileRoutes * kBK * 2;
+constexpr int kXBoxRows = 32;  // activation TMA box rows: a tile loads only the boxes covering its routes
 constexpr int kTmemBufs = 4;                 // accumulator buffers
 constexpr int kTmemCols = kTmemBufs * kBM;   // 4 x 128 fp32 columns
 static_assert(kTileRoutes == 128, "the MMA M extent is the route tile");
@@ -288,10 +289,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % kNS;
           if (!mbar_wait(emptyB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-          // 128 route rows from the tile's first; rows past the tile belong to other
-          // tiles (or lie past the tensor and read as zeros) and are never stored
-          mbar_arrive_expect_tx(fullB(s), (uint32_t)kBBytes);
-          tma_load_2d(sB + s * kBBytes, &tm_x, fullB(s), kb * kBK, un.start);
+          // boxes of 32 route rows covering the tile: the bytes moved from L2 bind this
+          // kernel, so a small tile does not load 128 rows.  Rows of the MMA tile past
+          // those boxes keep older data and rows past the tile belong to other tiles
+          // (or read as zeros past the tensor); none of them is ever stored.
+          const int nbox = (un.count + kXBoxRows - 1) / kXBoxRows;
+          mbar_arrive_expect_tx(fullB(s), (uint32_t)(nbox * kXBoxRows * kBK * 2));
+          for (int i = 0; i < nbox; ++i)
+            tma_load_2d(sB + s * kBBytes + i * (kXBoxRows * kBK * 2), &tm_x, fullB(s), kb * kBK,
+                        un.start + kXBoxRows * i);
         }
       }
       for (int k = max(0, it - kNS); k < it; ++k) mbar_wait_drain(fullB(k % kNS), (k / kNS) & 1, p.err);
@@ -545,7 +551,7 @@ int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st) {
   th = tb;
   if (L.q_lo && (rc = make_int8_map(&tl, L.q_lo, L.rows_lo, L.K))) return rc;
   if (L.q_hi && (rc = make_int8_map(&th, L.q_hi, L.rows_hi, L.K))) return rc;
-  if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype, kTileRoutes))) return rc;
+  if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype, kXBoxRows))) return rc;
   GemmParams p = {};
   p.K = L.K;
   p.tiles = L.tiles;

@@ -60,6 +60,8 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--no-extra', action='store_true', help='skip the decode (C3) and dense-sweep (C4) legs')
+    ap.add_argument('--replicas', action='store_true', help='with --gpus N > 1: N independent replicas instead of '
+                                                            'expert parallelism')
     return ap.parse_args()
 
 
@@ -73,7 +75,7 @@ def dist_setup(n):
     if world > 1:
         import datetime
         torch.cuda.set_device(local)
-        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=300))
+        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
     else:
         torch.cuda.set_device(0)
     return rank, world, local
@@ -150,12 +152,14 @@ def quantize_gpu(w):
     return q.reshape(w.shape).contiguous(), s.contiguous()
 
 
-def make_layers(layers, dev, seed):
+def make_layers(layers, dev, seed, experts=EXPERTS):
+    """Per layer: the routed bank (``experts`` experts: all 256, or this rank's shard
+    under expert parallelism), the shared expert and its gate."""
     g = torch.Generator(device=dev).manual_seed(seed)
     out = []
     for _ in range(layers):
-        qg, sg = quantize_gpu(torch.randn((EXPERTS, 2 * INTER, HIDDEN), generator=g, device=dev) * 0.02)
-        qd, sd = quantize_gpu(torch.randn((EXPERTS, HIDDEN, INTER), generator=g, device=dev) * 0.02)
+        qg, sg = quantize_gpu(torch.randn((experts, 2 * INTER, HIDDEN), generator=g, device=dev) * 0.02)
+        qd, sd = quantize_gpu(torch.randn((experts, HIDDEN, INTER), generator=g, device=dev) * 0.02)
         shared = [quantize_gpu(torch.randn(s, generator=g, device=dev) * 0.02)
                   for s in ((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER))]
         gate = (torch.randn((1, HIDDEN), generator=g, device=dev) * 0.02).bfloat16()
@@ -180,14 +184,23 @@ def make_routing(layers, tokens, dev, seed):
 
 def run_ours(a, rank, world, local):
     from localmoe35ba3b_b200 import _native
-    from localmoe35ba3b_b200.runtime import gpu_routes
+    from localmoe35ba3b_b200.runtime import ep, gpu_routes
     dev = torch.device('cuda', local)
     peaks = load_peaks()
-    layers = make_layers(a.layers, dev, a.seed + 1000 * rank)
+    use_ep = world > 1 and not a.replicas
+    e_loc = EXPERTS // world if use_ep else EXPERTS
+    layers = make_layers(a.layers, dev, a.seed + 1000 * rank, e_loc)
     x0, ids, wts = make_routing(a.layers, a.tokens, dev, a.seed + 1000 * rank)
     active = [int(torch.unique(ids[l]).numel()) for l in range(a.layers)]
+    if use_ep:
+        fns = [(ep.gpu_local_moe(bank), ep.gpu_shared_part(bank, shared, gate)) for bank, shared, gate in layers]
 
     def step(x, ids, wts, events=None):
+        if use_ep:
+            # expert parallelism: this rank's experts serve every rank's routes to them
+            for l in range(a.layers):
+                x = ep.moe_forward(x, wts[l], ids[l], EXPERTS, fns[l][0], fns[l][1], residual=x)
+            return x
         for l, (bank, shared, gate) in enumerate(layers):
             x = gpu_routes.moe_block(x, wts[l], ids[l], bank, shared=shared, shared_gate_weight=gate,
                                      residual=x, stage_events=None if events is None else events[l])
@@ -199,7 +212,7 @@ def run_ours(a, rank, world, local):
     _native.check_device_errors(dev)
 
     # ---- timed region: inputs resident in HBM
-    timed_with_events = min(a.steps, 10)
+    timed_with_events = 0 if use_ep else min(a.steps, 10)
     evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(a.layers)]
            for _ in range(timed_with_events)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -223,13 +236,17 @@ def run_ours(a, rank, world, local):
         for l in range(a.layers):
             e = evs[k][l]
             st += [e[i].elapsed_time(e[i + 1]) for i in range(4)]
-    st /= timed_with_events * a.layers  # ms per layer
-    gemm_ms = st[1] + st[2]
+    if timed_with_events:
+        st /= timed_with_events * a.layers  # ms per layer
+        gemm_ms = st[1] + st[2]
+    else:
+        # expert parallelism: no per-launch events across the exchange; the whole layer
+        gemm_ms = ms_step / a.layers
     routes = a.tokens * TOP
     rows = routes + a.tokens
     flops = 2.0 * rows * 3 * INTER * HIDDEN  # gate_up + down, routed + shared
     act_bytes = a.tokens * HIDDEN * 2 + 2 * rows * INTER * 2 + rows * HIDDEN * 2
-    wbytes = (float(np.mean(active)) + 1) * EXPERT_BYTES
+    wbytes = (float(np.mean(active)) / (world if use_ep else 1) + 1) * EXPERT_BYTES
     gemm_bytes = wbytes + act_bytes
     tflops = flops / (gemm_ms / 1e3) / 1e12
     gbs = gemm_bytes / (gemm_ms / 1e3) / 1e9
@@ -243,7 +260,10 @@ def run_ours(a, rank, world, local):
     else:
         roof = {'bound': 'hbm', 'achieved': round(gbs, 1), 'peak': pk_hbm, 'unit': 'GB/s',
                 'frac': round(gbs / pk_hbm, 4)}
-    roof.update({'traffic': NCU_TRAFFIC_PER_LAYER, 'traffic_source': NCU_TRAFFIC_SOURCE, 'kernel': 'grouped_gemm_w8a16 (gate_up+SwiGLU, down+weight) per layer',
+    roof.update({'traffic': None if use_ep else NCU_TRAFFIC_PER_LAYER,
+                 'traffic_source': 'not captured for the expert-parallel step' if use_ep else NCU_TRAFFIC_SOURCE,
+                 'kernel': ('whole expert-parallel layer (all-to-all + local experts + shared + combine), per rank'
+                            if use_ep else 'grouped GEMMs (gate_up+SwiGLU, down+weight) per layer'),
                  'peak_source': pk_tc_src, 'flops_per_layer': flops, 'alg_bytes_per_layer': round(gemm_bytes),
                  'tensor_frac': round(tflops / pk_tc, 4), 'hbm_frac': round(gbs / pk_hbm, 4),
                  'gemm_us_per_layer': round(gemm_ms * 1e3, 2),
@@ -285,7 +305,7 @@ def run_ours(a, rank, world, local):
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline_leg()
     extra = {}
-    if not a.no_extra:
+    if not a.no_extra and world == 1:
         extra['c3_decode'] = decode_leg(layers, dev, peaks, max(3, a.steps), a.warmup, a.seed + 1000 * rank)
         extra['c4_dense'] = dense_leg(dev, peaks)
 
@@ -296,11 +316,12 @@ def run_ours(a, rank, world, local):
         'config': {'workload': f'prefill chunk: {a.tokens} tokens x {a.layers} layers, 256 experts top-8 + shared, '
                                'hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, Zipf(1.1) routing',
                    'tokens_per_gpu': a.tokens, 'layers': a.layers,
-                   'parallelism': 'replicas' if world > 1 else 'single',
+                   'parallelism': (f'ep{world} (experts {e_loc} per GPU, all-to-all over NCCL)' if use_ep
+                                   else ('replicas' if world > 1 else 'single')),
                    'active_experts_mean': round(float(np.mean(active)), 1),
                    'l2': 'inputs larger than L2 (33.2 GB of resident expert weights per GPU)'},
         'roofline': roof, 'cpu_baseline': cpu, 'e2e': e2e,
-        'gpu_launches': LAUNCHES_PER_LAYER * a.layers * a.steps, 'clocks': clk.summary(),
+        'gpu_launches': (2 if use_ep else 1) * LAUNCHES_PER_LAYER * a.layers * a.steps, 'clocks': clk.summary(),
     }
     if extra:
         line['extra'] = extra

@@ -124,8 +124,12 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
                                const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd, const float* sh_sd,
                                const void* sh_gate_w, const void* residual, void* out, int dtype, void* ws, int* err,
                                void** stage_events, void* stream) {
-  if (!x || !weights || !ids || !qg || !sg || !qd || !sd || !out || !ws) return LMOE_ERR_INVALID;
-  if (tokens <= 0 || top <= 0 || experts <= 0 || hidden <= 0 || inter <= 0) return LMOE_ERR_INVALID;
+  // top == 0 (no routed experts, the gated shared expert alone) is accepted when a shared
+  // expert is given: expert-parallel callers compute their own tokens' shared expert this way
+  const bool shared_only = top == 0 && sh_qg != nullptr;
+  if (!x || (!shared_only && (!weights || !ids)) || !qg || !sg || !qd || !sd || !out || !ws) return LMOE_ERR_INVALID;
+  if (tokens <= 0 || top < 0 || (top == 0 && !shared_only) || experts <= 0 || hidden <= 0 || inter <= 0)
+    return LMOE_ERR_INVALID;
   if (hidden % kGroup || inter % kGroup || hidden % 8) return LMOE_ERR_INVALID;
   if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_ERR_INVALID;
   const bool with_shared = sh_qg != nullptr;
@@ -261,7 +265,8 @@ extern "C" int lmoe_routed_moe_noalloc(const void* x, const float* weights, cons
                                        const float* sh_su, const int8_t* sh_qd, const float* sh_sd,
                                        const void* sh_gate_w, const void* residual, void* out, int dtype, int* err,
                                        void* stream) {
-  if (tokens <= 0 || top <= 0 || experts <= 0 || hidden <= 0 || inter <= 0) return LMOE_ERR_INVALID;
+  if (tokens <= 0 || top < 0 || (top == 0 && sh_qg == nullptr) || experts <= 0 || hidden <= 0 || inter <= 0)
+    return LMOE_ERR_INVALID;
   // every byte of the scratch that a call reads is written earlier in the same
   // call, so nothing needs clearing between calls
   if (lmoe_moe_workspace_size(tokens, top, experts, hidden, inter) > lmoe::kNoAllocScratchBytes)

@@ -306,8 +306,10 @@ extern "C" int64_t lmoe_route_meta_size(int64_t tokens, int64_t top, int64_t exp
 
 int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
                          int with_shared, void* meta, int* err, cudaStream_t st) {
-  if (!ids || !meta) return LMOE_ERR_INVALID;
-  if (!route_geometry_ok(tokens, top, experts)) return LMOE_ERR_INVALID;
+  // top == 0 with the shared expert: no routes, only the shared expert's tiles
+  const bool shared_only = top == 0 && with_shared;
+  if ((!ids && !shared_only) || !meta) return LMOE_ERR_INVALID;
+  if (!route_geometry_ok(tokens, shared_only ? 1 : top, experts)) return LMOE_ERR_INVALID;
   const MetaLayout L(tokens, top, experts);
   char* m = (char*)meta;
   RouteArgs a = {};

@@ -1,0 +1,113 @@
+"""Expert-parallel path on the GPU kernels, one process (world size 1 over NCCL):
+route rows through gpu_routes.moe_block with one route per row, the shared
+expert through the same library call with no routed experts (top 0)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import BF16, act, rand_q, rel_maxabs, rng, to_dev, to_np
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module', autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip('needs a CUDA device')
+    from localmoe35ba3b_b200 import _native
+    _native.lib()
+    yield
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+
+
+def _case(T=96, E=32, H=512, I=256, top=8):
+    r = rng(44)
+    logits = r.standard_normal((T, E), dtype=np.float32) + O.zipf_bias(E, r)[None]
+    ids, w = O.route(logits, top)
+    bank = (*rand_q(r, (E, 2 * I, H)), *rand_q(r, (E, H, I)))
+    shared = [rand_q(r, (I, H)), rand_q(r, (I, H)), rand_q(r, (H, I))]
+    gate = act(r, (1, H), BF16, 0.02)
+    x = act(r, (T, H), BF16)
+    res = act(r, (T, H), BF16)
+    return x, ids, w, bank, shared, gate, res
+
+
+def test_shared_only_block_matches_oracle():
+    from localmoe35ba3b_b200.runtime import gpu_routes
+    x, ids, w, bank, shared, gate, res = _case()
+    bd = [torch.from_numpy(b).cuda() for b in bank]
+    sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
+    t = x.shape[0]
+    out = gpu_routes.moe_block(to_dev(x, BF16), torch.empty((t, 0), device='cuda'),
+                               torch.empty((t, 0), dtype=torch.int64, device='cuda'), bd, shared=sh,
+                               shared_gate_weight=to_dev(gate, BF16), residual=to_dev(res, BF16))
+    torch.cuda.synchronize()
+    sg = O.shared_gate_combine(np.zeros_like(x), O.shared_expert(x, shared, BF16), x, gate, BF16)
+    ref = O.round_to(res + sg, BF16)
+    assert rel_maxabs(to_np(out), ref) < 1e-2
+
+
+def test_expert_parallel_world1_matches_oracle():
+    import torch.distributed as dist
+    from localmoe35ba3b_b200.runtime import ep
+    x, ids, w, bank, shared, gate, res = _case()
+    s = socket.socket()
+    s.bind(('127.0.0.1', 0))
+    port = s.getsockname()[1]
+    s.close()
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('nccl', rank=0, world_size=1)
+    try:
+        bd = [torch.from_numpy(b).cuda() for b in bank]
+        sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
+        out = ep.moe_forward(to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(), bank[0].shape[0],
+                             ep.gpu_local_moe(bd), ep.gpu_shared_part(bd, sh, to_dev(gate, BF16)),
+                             residual=to_dev(res, BF16))
+        torch.cuda.synchronize()
+    finally:
+        dist.destroy_process_group()
+    ref = O.round_to(res + O.moe_block(x, w, ids, bank, shared, gate, BF16), BF16)
+    assert rel_maxabs(to_np(out), ref) < 1e-2
+
+
+def _ep2_worker(rank, port, out_dir):
+    import torch.distributed as dist
+    from localmoe35ba3b_b200.runtime import ep, gpu_routes
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group('nccl', rank=rank, world_size=2)
+    try:
+        x, ids, w, bank, shared, gate, res = _case()
+        t = x.shape[0] // 2
+        sl = slice(rank * t, (rank + 1) * t)  # each rank owns half of the tokens
+        e_loc = bank[0].shape[0] // 2
+        lb = [torch.from_numpy(b[rank * e_loc:(rank + 1) * e_loc]).cuda() for b in bank]
+        sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
+        out = ep.moe_forward(to_dev(x[sl], BF16), torch.from_numpy(w[sl]).cuda(), torch.from_numpy(ids[sl]).cuda(),
+                             bank[0].shape[0], ep.gpu_local_moe(lb), ep.gpu_shared_part(lb, sh, to_dev(gate, BF16)),
+                             residual=to_dev(res[sl], BF16))
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f'ep2_{rank}.npy'), to_np(out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+def test_expert_parallel_two_gpus_matches_oracle(tmp_path):
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(('127.0.0.1', 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.start_processes(_ep2_worker, args=(port, str(tmp_path)), nprocs=2, join=True, start_method='spawn')
+    x, ids, w, bank, shared, gate, res = _case()
+    ref = O.round_to(res + O.moe_block(x, w, ids, bank, shared, gate, BF16), BF16)
+    got = np.concatenate([np.load(tmp_path / f'ep2_{r}.npy') for r in range(2)])
+    assert rel_maxabs(got, ref) < 1e-2

@@ -60,8 +60,8 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--no-extra', action='store_true', help='skip the decode (C3) and dense-sweep (C4) legs')
-    ap.add_argument('--replicas', action='store_true', help='with --gpus N > 1: N independent replicas instead of '
-                                                            'expert parallelism')
+    ap.add_argument('--ep', action='store_true', help='with --gpus N > 1: expert parallelism (experts sharded, '
+                                                      'all-to-all) instead of N data-parallel replicas')
     return ap.parse_args()
 
 
@@ -187,7 +187,9 @@ def run_ours(a, rank, world, local):
     from localmoe35ba3b_b200.runtime import ep, gpu_routes
     dev = torch.device('cuda', local)
     peaks = load_peaks()
-    use_ep = world > 1 and not a.replicas
+    # N > 1: data-parallel replicas by default (all 40 layers' weights, 33.2 GB, fit on every
+    # B200, and each GPU runs its own tokens); --ep shards the experts instead
+    use_ep = world > 1 and a.ep
     e_loc = EXPERTS // world if use_ep else EXPERTS
     layers = make_layers(a.layers, dev, a.seed + 1000 * rank, e_loc)
     x0, ids, wts = make_routing(a.layers, a.tokens, dev, a.seed + 1000 * rank)
@@ -317,7 +319,8 @@ def run_ours(a, rank, world, local):
                                'hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, Zipf(1.1) routing',
                    'tokens_per_gpu': a.tokens, 'layers': a.layers,
                    'parallelism': (f'ep{world} (experts {e_loc} per GPU, all-to-all over NCCL)' if use_ep
-                                   else ('replicas' if world > 1 else 'single')),
+                                   else (f'dp{world} replicas (full weights per GPU; --ep for expert parallelism)'
+                                         if world > 1 else 'single')),
                    'active_experts_mean': round(float(np.mean(active)), 1),
                    'l2': 'inputs larger than L2 (33.2 GB of resident expert weights per GPU)'},
         'roofline': roof, 'cpu_baseline': cpu, 'e2e': e2e,

@@ -77,10 +77,57 @@ struct RouteArgs {
   int* err;
 };
 
+// Tile list of the fused path (experts by descending route count, ties by lower
+// id; the shared expert's T rows are expert E when present) and the header.
+// Called by all kRouteThreads threads; s_first[e] = first sorted slot of expert e,
+// s_first[E + 1] = R.
+__device__ void write_tiles(const RouteArgs& a, const int* s_first, int R, int* warp_tot) {
+  __shared__ int s_total_tiles;
+  const int E = a.E;
+  const int Es = E + (a.with_shared ? 1 : 0);
+  const int e = threadIdx.x;
+  int cnt = 0, ntl = 0, rank = 0;
+  if (e < Es) {
+    cnt = (e < E) ? (s_first[e + 1] - s_first[e]) : a.T;
+    ntl = (cnt + kTileRoutes - 1) / kTileRoutes;
+    for (int o = 0; o < Es; ++o) {
+      const int co = (o < E) ? (s_first[o + 1] - s_first[o]) : a.T;
+      rank += (co > cnt) || (co == cnt && o < e);
+    }
+  }
+  __shared__ int s_by_rank[1025];
+  if (e < Es) s_by_rank[rank] = ntl;
+  __syncthreads();
+  const int r_ntl = (e < Es) ? s_by_rank[e] : 0;  // thread e now holds rank e's tile count
+  const int r_incl = block_incl_scan(r_ntl, warp_tot);
+  __shared__ int s_tile_first[1025];
+  if (e < Es) s_tile_first[e] = r_incl - r_ntl;
+  if (e == Es - 1) s_total_tiles = r_incl;
+  __syncthreads();
+  if (e < Es) {
+    const int t0 = s_tile_first[rank];
+    const int start0 = (e < E) ? s_first[e] : R;
+    for (int j = 0; j < ntl; ++j) {
+      Tile tl;
+      tl.expert = e;
+      tl.start = start0 + j * kTileRoutes;
+      tl.count = min(kTileRoutes, cnt - j * kTileRoutes);
+      tl.pad = 0;
+      a.tiles[t0 + j] = tl;
+    }
+  }
+  if (threadIdx.x == 0) {
+    a.hdr[kHdrNumTiles] = s_total_tiles;
+    a.hdr[kHdrRoutes] = R;
+    a.hdr[kHdrTokens] = a.T;
+    a.hdr[kHdrExperts] = E;
+    a.hdr[kHdrShared] = a.with_shared;
+  }
+}
+
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   extern __shared__ int cw[];  // [kRouteWarps][E+1] counts, then first slots
   __shared__ int warp_tot[32];
-  __shared__ int s_total_tiles;
   const int R = a.T * a.top;
   const int E = a.E;
   const int Es = E + (a.with_shared ? 1 : 0);  // ranked experts incl. shared
@@ -185,45 +232,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __syncthreads();
 
   // fused-path tiles, experts ordered by descending count (ties: lower id first)
-  if (a.tiles != nullptr) {
-    int cnt = 0, ntl = 0, rank = 0;
-    if (e < Es) {
-      cnt = (e < E) ? (s_first[e + 1] - s_first[e]) : a.T;
-      ntl = (cnt + kTileRoutes - 1) / kTileRoutes;
-      for (int o = 0; o < Es; ++o) {
-        const int co = (o < E) ? (s_first[o + 1] - s_first[o]) : a.T;
-        rank += (co > cnt) || (co == cnt && o < e);
-      }
-    }
-    __shared__ int s_by_rank[1025];
-    if (e < Es) s_by_rank[rank] = ntl;
-    __syncthreads();
-    const int r_ntl = (e < Es) ? s_by_rank[e] : 0;  // thread e now holds rank e's tile count
-    const int r_incl = block_incl_scan(r_ntl, warp_tot);
-    __shared__ int s_tile_first[1025];
-    if (e < Es) s_tile_first[e] = r_incl - r_ntl;
-    if (e == Es - 1) s_total_tiles = r_incl;
-    __syncthreads();
-    if (e < Es) {
-      const int t0 = s_tile_first[rank];
-      const int start0 = (e < E) ? s_first[e] : R;
-      for (int j = 0; j < ntl; ++j) {
-        Tile tl;
-        tl.expert = e;
-        tl.start = start0 + j * kTileRoutes;
-        tl.count = min(kTileRoutes, cnt - j * kTileRoutes);
-        tl.pad = 0;
-        a.tiles[t0 + j] = tl;
-      }
-    }
-    if (threadIdx.x == 0) {
-      a.hdr[kHdrNumTiles] = s_total_tiles;
-      a.hdr[kHdrRoutes] = R;
-      a.hdr[kHdrTokens] = a.T;
-      a.hdr[kHdrExperts] = E;
-      a.hdr[kHdrShared] = a.with_shared;
-    }
-  }
+  if (a.tiles != nullptr) write_tiles(a, s_first, R, warp_tot);
 
   // reference table: ends = cumsum(ceil(count / bm)) in expert-id order
   if (a.table64 != nullptr) {
@@ -252,6 +261,100 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
       a.table64[(int64_t)tile * 3 + 2] = sp;
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Fused-path metadata on many CTAs (lmoe_route_meta): the same stable counting
+// sort, cut into kMetaChunk-route chunks so every chunk runs on its own CTA.
+//   1. meta_count_kernel  per-chunk expert histograms
+//   2. meta_scan_kernel   (one CTA) exclusive scans over chunks and experts give
+//                         every (chunk, expert) its first sorted slot; offsets,
+//                         tile list, header, the shared expert's rows
+//   3. meta_place_kernel  per chunk: ranks inside each warp (__match_any_sync),
+//                         a scan over the chunk's warps, then each route's slot;
+//                         the per-token ascending-expert order as in route_kernel
+__global__ void __launch_bounds__(kMetaChunk) meta_count_kernel(const int64_t* __restrict__ ids, int R, int E,
+                                                                int32_t* __restrict__ cc, int* err) {
+  extern __shared__ int h[];  // [E + 1]
+  for (int i = threadIdx.x; i <= E; i += kMetaChunk) h[i] = 0;
+  __syncthreads();
+  const int f = blockIdx.x * kMetaChunk + threadIdx.x;
+  if (f < R) atomicAdd(&h[clamp_id(ids[f], E, err)], 1);
+  __syncthreads();
+  for (int i = threadIdx.x; i <= E; i += kMetaChunk) cc[(int64_t)blockIdx.x * (E + 1) + i] = h[i];
+}
+
+__global__ void __launch_bounds__(kRouteThreads) meta_scan_kernel(RouteArgs a, int32_t* __restrict__ cc,
+                                                                  int nchunks) {
+  __shared__ int warp_tot[32];
+  __shared__ int s_first[1025];
+  const int E = a.E, R = a.T * a.top;
+  const int e = threadIdx.x;
+  int count = 0;
+  if (e <= E) {
+    for (int c = 0; c < nchunks; ++c) {
+      const int t = cc[(int64_t)c * (E + 1) + e];
+      cc[(int64_t)c * (E + 1) + e] = count;
+      count += t;
+    }
+  }
+  const int incl = block_incl_scan(e <= E ? count : 0, warp_tot);
+  const int first = incl - (e <= E ? count : 0);
+  if (e <= E) {
+    for (int c = 0; c < nchunks; ++c) cc[(int64_t)c * (E + 1) + e] += first;
+    s_first[e] = first;
+    if (e < E) a.offsets[e] = first;
+  }
+  if (e == 0) {
+    s_first[E + 1] = R;
+    a.offsets[E] = R;
+    a.offsets[E + 1] = R + (a.with_shared ? a.T : 0);
+  }
+  if (a.with_shared)
+    for (int t = threadIdx.x; t < a.T; t += kRouteThreads) a.pos32[R + t] = t;
+  __syncthreads();
+  write_tiles(a, s_first, R, warp_tot);
+}
+
+__global__ void __launch_bounds__(kMetaChunk) meta_place_kernel(RouteArgs a, const int32_t* __restrict__ cc) {
+  extern __shared__ int wc[];  // [kMetaChunk / 32][E + 1] per-warp counts, then first slots
+  constexpr int kW = kMetaChunk / 32;
+  const int E = a.E, R = a.T * a.top;
+  const int lane = lane_id(), warp = warp_id();
+  for (int i = threadIdx.x; i < kW * (E + 1); i += kMetaChunk) wc[i] = 0;
+  __syncthreads();
+  const int f = blockIdx.x * kMetaChunk + threadIdx.x;
+  const bool valid = f < R;
+  const int id = valid ? clamp_id(a.ids[f], E, nullptr) : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, id);
+  const int rank_w = __popc(peers & ((1u << lane) - 1u));
+  if (valid && lane == __ffs(peers) - 1) wc[warp * (E + 1) + id] = __popc(peers);
+  __syncthreads();
+  if (threadIdx.x <= E) {
+    int run = cc[(int64_t)blockIdx.x * (E + 1) + threadIdx.x];
+    for (int w = 0; w < kW; ++w) {
+      const int t = wc[w * (E + 1) + threadIdx.x];
+      wc[w * (E + 1) + threadIdx.x] = run;
+      run += t;
+    }
+  }
+  __syncthreads();
+  if (!valid) return;
+  const int dst = wc[warp * (E + 1) + id] + rank_w;
+  const int tok = f / a.top;
+  const int slot = f - tok * a.top;
+  // rank of this route among its token's routes, ordered by (id, slot)
+  const int64_t* trow = a.ids + (int64_t)tok * a.top;
+  int rank = 0;
+  for (int j = 0; j < a.top; ++j) {
+    const int64_t oj = trow[j];
+    const int idj = (oj < 0 || oj >= E) ? E : (int)oj;
+    rank += (idj < id) || (idj == id && j < slot);
+  }
+  a.inverse[f] = dst;
+  a.pos32[dst] = tok;
+  a.rweight[dst] = a.weights ? a.weights[f] : 1.0f;
+  a.ordered32[(int64_t)tok * a.top + rank] = dst;
 }
 
 static size_t route_smem(int64_t E) { return (size_t)kRouteWarps * (E + 1) * sizeof(int); }
@@ -327,7 +430,24 @@ int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t token
   a.ordered32 = (int32_t*)(m + L.off_ordered);
   a.inverse = (int32_t*)(m + L.off_inverse);
   a.err = err;
-  return launch_route(a, st);
+  int32_t* cc = (int32_t*)(m + L.off_scratch);
+  const int R = (int)(tokens * top);
+  const int nchunks = (R + kMetaChunk - 1) / kMetaChunk;
+  const size_t hsm = (size_t)(experts + 1) * sizeof(int);
+  const size_t wsm = (size_t)(kMetaChunk / 32) * (experts + 1) * sizeof(int);
+  if (nchunks > 0) {
+    meta_count_kernel<<<nchunks, kMetaChunk, hsm, st>>>(ids, R, (int)experts, cc, err);
+    LMOE_CUDA_CHECK(cudaGetLastError());
+  }
+  meta_scan_kernel<<<1, kRouteThreads, 0, st>>>(a, cc, nchunks);
+  LMOE_CUDA_CHECK(cudaGetLastError());
+  if (nchunks > 0) {
+    if (wsm > 48 * 1024)
+      LMOE_CUDA_CHECK(cudaFuncSetAttribute(meta_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsm));
+    meta_place_kernel<<<nchunks, kMetaChunk, wsm, st>>>(a, cc);
+    LMOE_CUDA_CHECK(cudaGetLastError());
+  }
+  return LMOE_OK;
 }
 
 extern "C" int lmoe_route_meta(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,

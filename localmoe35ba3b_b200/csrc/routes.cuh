@@ -5,6 +5,7 @@
 namespace lmoe {
 
 constexpr int kTileRoutes = 128;  // routes (tokens) per GEMM tile: the MMA M extent
+constexpr int kMetaChunk = 1024;  // routes per CTA in the multi-CTA metadata kernels
 
 struct __align__(16) Tile {
   int32_t expert;  // expert id; == experts for the shared-expert segment
@@ -17,7 +18,7 @@ struct __align__(16) Tile {
 // section starts on a 256-byte boundary.
 struct MetaLayout {
   int64_t routes, tokens, top, experts, max_tiles;
-  int64_t off_hdr, off_offsets, off_tiles, off_pos, off_rweight, off_ordered, off_inverse, bytes;
+  int64_t off_hdr, off_offsets, off_tiles, off_pos, off_rweight, off_ordered, off_inverse, off_scratch, bytes;
 
   __host__ __device__ static int64_t align(int64_t v) { return (v + 255) & ~int64_t(255); }
   __host__ __device__ MetaLayout(int64_t t, int64_t k, int64_t e) : routes(t * k), tokens(t), top(k), experts(e) {
@@ -30,6 +31,7 @@ struct MetaLayout {
     off_rweight = o;  o = align(o + routes * 4);
     off_ordered = o;  o = align(o + routes * 4);
     off_inverse = o;  o = align(o + routes * 4);
+    off_scratch = o;  o = align(o + ((routes + kMetaChunk - 1) / kMetaChunk) * (e + 1) * 4);  // per-chunk counts
     bytes = o;
   }
 };

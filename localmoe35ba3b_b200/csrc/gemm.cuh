@@ -41,6 +41,7 @@ int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st);
 // tensor maps (grouped_gemm.cu): int8 [rows, K] with a 64-row x 128-byte, 128B-swizzled box;
 // 16-bit activations [rows, K] with a box_rows x 64-element, 128B-swizzled box
 int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K);
+int make_int8_pair_map(CUtensorMap* m, const int8_t* base, int64_t experts, int64_t inter, int64_t K);
 int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int dtype, int box_rows);
 int sm_count();
 

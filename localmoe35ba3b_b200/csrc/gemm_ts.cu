@@ -87,7 +87,7 @@ struct Params {
 };
 
 struct Unit {
-  int start, count, nb;
+  int start, count, nb, expert;
   bool shared;
   int64_t rlo, rhi;  // tensor-map rows of the gate and up halves
 };
@@ -97,6 +97,7 @@ __device__ __forceinline__ bool get_unit(const Params& p, int u, int nblocks, Un
   if (t >= p.hdr[kHdrNumTiles]) return false;
   const Tile tl = p.tiles[t];
   o.nb = u - t * nblocks;
+  o.expert = tl.expert;
   o.start = tl.start;
   o.count = tl.count;
   o.shared = tl.expert == p.experts;
@@ -119,7 +120,7 @@ template <int DT>
 __global__ void __launch_bounds__(kThreads, 1)
     gate_up_ts_kernel(const __grid_constant__ CUtensorMap tm_bank, const __grid_constant__ CUtensorMap tm_g,
                       const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_x,
-                      const Params p) {
+                      const __grid_constant__ CUtensorMap tm_x128, const Params p) {
   using A = Act<DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -171,7 +172,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_g);
     prefetch_tmap(&tm_u);
   }
-  if (warp == 2 && lane == 0) prefetch_tmap(&tm_x);
+  if (warp == 2 && lane == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_x128);
+  }
   if (warp == 1) {
     tmem_alloc(smem_u32(sTmem), kTmemCols);
     tmem_relinquish();
@@ -190,14 +194,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; ok; u += stride) {
         Unit un;
         if (!get_unit(p, u, nblocks, un)) break;
-        const CUtensorMap* mlo = un.shared ? &tm_g : &tm_bank;
-        const CUtensorMap* mhi = un.shared ? &tm_u : &tm_bank;
         for (int g = 0; g < G; ++g, ++it) {
           const int s8 = it % kNS8;
           if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(full8(s8), kA8Bytes);
-          tma_load_2d(sA8 + s8 * kA8Bytes, mlo, full8(s8), g * kBK8, (int)un.rlo);
-          tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, mhi, full8(s8), g * kBK8, (int)un.rhi);
+          if (un.shared) {
+            tma_load_2d(sA8 + s8 * kA8Bytes, &tm_g, full8(s8), g * kBK8, (int)un.rlo);
+            tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, &tm_u, full8(s8), g * kBK8, (int)un.rhi);
+          } else {
+            // one box for both halves: the bank viewed as [2E][I][K], box 2 x 64 x 128 B at
+            // (expert's gate half, 64 rows of block nb): the gate rows, then the up rows
+            tma_load_3d(sA8 + s8 * kA8Bytes, &tm_bank, full8(s8), g * kBK8, un.nb * 64, 2 * un.expert);
+          }
         }
       }
       for (int k = max(0, it - kNS8); k < it; ++k) mbar_wait_drain(full8(k % kNS8), (k / kNS8) & 1, p.err);
@@ -253,15 +261,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!get_unit(p, u, nblocks, un)) break;
         // boxes of 32 route rows covering the tile; rows past the tile are read
         // (other tiles' rows, or zeros past the tensor) but never stored
-        const int nbox = (un.count + kBoxRows - 1) / kBoxRows;
+        // a full-height tile takes one 128-row box (larger boxes stream faster),
+        // a smaller one the 32-row boxes covering its routes
+        const bool big = un.count > 3 * kBoxRows;
+        const int nbox = big ? 1 : (un.count + kBoxRows - 1) / kBoxRows;
+        const uint32_t bytes = big ? (uint32_t)kBBytes : (uint32_t)(nbox * kBoxRows * kBKB * 2);
         for (int g = 0; g < G && ok; ++g) {
           for (int h = 0; h < 2; ++h, ++ib) {
             const int s = ib % kNSB;
             if (!mbar_wait(emptyB(s), ((ib / kNSB) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-            mbar_arrive_expect_tx(fullB(s), (uint32_t)(nbox * kBoxRows * kBKB * 2));
-            for (int i = 0; i < nbox; ++i)
-              tma_load_2d(sB + s * kBBytes + i * (kBoxRows * kBKB * 2), &tm_x, fullB(s), (g * 2 + h) * kBKB,
-                          un.start + kBoxRows * i);
+            mbar_arrive_expect_tx(fullB(s), bytes);
+            if (big) {
+              tma_load_2d(sB + s * kBBytes, &tm_x128, fullB(s), (g * 2 + h) * kBKB, un.start);
+            } else {
+              for (int i = 0; i < nbox; ++i)
+                tma_load_2d(sB + s * kBBytes + i * (kBoxRows * kBKB * 2), &tm_x, fullB(s), (g * 2 + h) * kBKB,
+                            un.start + kBoxRows * i);
+            }
           }
         }
       }
@@ -421,14 +437,15 @@ int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st) {
   if (L.K % kGroup || L.K <= 0 || L.inter % 64 || L.inter <= 0 || L.N != 2 * L.inter) return LMOE_ERR_INVALID;
   if ((L.ldy % 8) != 0 || (((uintptr_t)L.y) & 15)) return LMOE_ERR_INVALID;
   if (L.grid_tiles <= 0) return LMOE_OK;
-  CUtensorMap tb, tg, tu, tx;
-  int rc = make_int8_map(&tb, L.q_bank, L.experts * L.N, L.K);
+  CUtensorMap tb, tg, tu, tx, tx128;
+  int rc = make_int8_pair_map(&tb, L.q_bank, L.experts, L.inter, L.K);
   if (rc) return rc;
   tg = tb;
   tu = tb;
   if (L.q_lo && (rc = make_int8_map(&tg, L.q_lo, L.rows_lo, L.K))) return rc;
   if (L.q_hi && (rc = make_int8_map(&tu, L.q_hi, L.rows_hi, L.K))) return rc;
   if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype, ts::kBoxRows))) return rc;
+  if ((rc = make_act_map(&tx128, L.x, L.x_rows, L.K, L.dtype, kTileRoutes))) return rc;
   ts::Params p = {};
   p.K = L.K;
   p.inter = L.inter;
@@ -450,11 +467,11 @@ int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st) {
   if (L.dtype == LMOE_BF16) {
     auto k = ts::gate_up_ts_kernel<LMOE_BF16>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, p);
+    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, tx128, p);
   } else if (L.dtype == LMOE_F16) {
     auto k = ts::gate_up_ts_kernel<LMOE_F16>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, p);
+    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, tx128, p);
   } else {
     return LMOE_ERR_INVALID;
   }

@@ -518,6 +518,22 @@ int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K) {
   return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
 }
 
+// gate_up bank [E, 2I, K] int8 viewed as [2E][I][K]: box 2 x 64 rows x 128 bytes, 128-byte
+// swizzle -- the 64 gate rows and the matching 64 up rows of one output block in one copy
+int make_int8_pair_map(CUtensorMap* m, const int8_t* base, int64_t experts, int64_t inter, int64_t K) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LMOE_ERR_CUDA;
+  if (((uintptr_t)base & 15) || (K % 16) || experts <= 0 || inter <= 0) return LMOE_ERR_INVALID;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)inter, (cuuint64_t)(2 * experts)};
+  cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)(inter * K)};
+  cuuint32_t box[3] = {(cuuint32_t)kBK8, 64, 2};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)base, dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
+}
+
 // activations [rows, K] 16-bit, box of 64 rows x 64 elements (8 KB) with the
 // 128-byte swizzle: the B operand's K-major UMMA layout
 int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int dtype, int box_rows) {

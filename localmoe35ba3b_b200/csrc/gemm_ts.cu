@@ -15,8 +15,9 @@
 //      bf16              dequant warps -> tensor memory (tcgen05.st): the MMA's
 //                        A operand, 64 columns per stage, 4 slots; weights never
 //                        pass through shared memory in 16-bit form
-//   X  bf16 [N x 64]     TMA boxes of 32 route rows -> 128B-swizzled smem ring:
-//                        the MMA's B operand
+//   X  bf16 [N x 128]    two 64-column chunks per stage, one barrier per stage
+//                        (TMA boxes of 32 route rows, or 128 for a full tile)
+//                        -> 128B-swizzled smem ring: the MMA's B operand
 //   D  fp32 [128 lanes x 128 columns] in tensor memory, two buffers
 // Shared-memory traffic per MAC is therefore the int8 tile (TMA write + one
 // read) and the route rows (TMA write + the MMA's read), about half of what an
@@ -39,14 +40,16 @@ namespace ts {
 constexpr int kBM = 128;       // weight rows per unit: MMA M
 constexpr int kBK8 = 128;      // int8 stage K (one scale group)
 constexpr int kNS8 = 6;        // int8 stages
-constexpr int kBKB = 64;       // activation stage K (one 128-byte swizzle atom)
-constexpr int kNSB = 6;        // activation stages
+constexpr int kBKB = 64;       // activation chunk K (one 128-byte swizzle atom)
+constexpr int kBChunks = kBK8 / kBKB;  // chunks per activation stage: one stage per int8 stage
+constexpr int kNSB = 3;        // activation stages
 constexpr int kNA = 4;         // tensor-memory A slots
 constexpr int kBoxRows = 32;   // activation TMA box rows
 constexpr int kThreads = 512;
 constexpr int kConvWarps = 8;
 constexpr int kA8Bytes = kBM * kBK8;              // 16 KB
-constexpr int kBBytes = kTileRoutes * kBKB * 2;   // 16 KB
+constexpr int kBBytes = kTileRoutes * kBKB * 2;   // 16 KB per chunk
+constexpr int kBStage = kBChunks * kBBytes;       // 32 KB per activation stage
 constexpr int kAccCols = kTileRoutes;             // fp32 accumulator columns per buffer
 constexpr int kACol0 = 2 * kAccCols;              // A slots follow the two accumulators
 constexpr int kASlotCols = kBK8 / 2;              // 64 columns hold 128 16-bit K values
@@ -59,7 +62,7 @@ static_assert(kACol0 + kNA * kASlotCols <= kTmemCols, "tensor memory budget");
 struct Smem {
   static constexpr int a8 = 0;
   static constexpr int b = a8 + kNS8 * kA8Bytes;
-  static constexpr int u = b + kNSB * kBBytes;
+  static constexpr int u = b + kNSB * kBStage;
   static constexpr int h = u + 2 * kUBytes;
   static constexpr int bars = h + 2 * kHBytes;
   // full8, empty8 (kNS8 each); fullA, emptyA (kNA each); fullB, emptyB (kNSB each); tfull, tempty (2 each); drain
@@ -228,19 +231,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int g = 0; g < G && ok; ++g, ++ia) {
           const int a = ia % kNA;
           if (!mbar_wait(fullA(a), (ia / kNA) & 1, sAbort, p.err)) { ok = false; break; }
-          for (int h = 0; h < 2; ++h, ++ib) {
-            const int s = ib % kNSB;
-            if (!mbar_wait(fullB(s), (ib / kNSB) & 1, sAbort, p.err)) { ok = false; break; }
-            tc_fence_after();
-            const uint64_t bd = sdesc_k_sw128(sB + s * kBBytes);
+          const int s = ib % kNSB;
+          if (!mbar_wait(fullB(s), (ib / kNSB) & 1, sAbort, p.err)) { ok = false; break; }
+          ++ib;
+          tc_fence_after();
+#pragma unroll
+          for (int h = 0; h < kBChunks; ++h) {
+            const uint64_t bd = sdesc_k_sw128(sB + s * kBStage + h * kBBytes);
             const uint32_t acol = tmem + (uint32_t)(kACol0 + a * kASlotCols + h * 32);
 #pragma unroll
             for (int kk = 0; kk < kBKB / 16; ++kk)
               mma_f16_ts(dt, acol + (uint32_t)(kk * 8), bd + (uint64_t)(kk * 2), idesc, (g | h | kk) != 0);
-            mma_commit(emptyB(s));
-            issued = true;
           }
-          if (ok) mma_commit(emptyA(a));
+          mma_commit(emptyB(s));
+          mma_commit(emptyA(a));
+          issued = true;
         }
         // also after an abort, so the epilogue's wait ends
         if (issued) mma_commit(tfull(b));
@@ -263,20 +268,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (other tiles' rows, or zeros past the tensor) but never stored
         // a full-height tile takes one 128-row box (larger boxes stream faster),
         // a smaller one the 32-row boxes covering its routes
+        // one barrier per stage: a warp's bulk copies stream at about one barrier
+        // stage per 0.4 us whatever their size, so both K chunks of the int8 stage
+        // land on the same barrier
         const bool big = un.count > 3 * kBoxRows;
         const int nbox = big ? 1 : (un.count + kBoxRows - 1) / kBoxRows;
-        const uint32_t bytes = big ? (uint32_t)kBBytes : (uint32_t)(nbox * kBoxRows * kBKB * 2);
-        for (int g = 0; g < G && ok; ++g) {
-          for (int h = 0; h < 2; ++h, ++ib) {
-            const int s = ib % kNSB;
-            if (!mbar_wait(emptyB(s), ((ib / kNSB) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-            mbar_arrive_expect_tx(fullB(s), bytes);
+        const uint32_t bytes = kBChunks * (big ? (uint32_t)kBBytes : (uint32_t)(nbox * kBoxRows * kBKB * 2));
+        for (int g = 0; g < G; ++g, ++ib) {
+          const int s = ib % kNSB;
+          if (!mbar_wait(emptyB(s), ((ib / kNSB) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(fullB(s), bytes);
+          for (int h = 0; h < kBChunks; ++h) {
+            const uint32_t dst = sB + s * kBStage + h * kBBytes;
+            const int kx = (g * kBChunks + h) * kBKB;
             if (big) {
-              tma_load_2d(sB + s * kBBytes, &tm_x128, fullB(s), (g * 2 + h) * kBKB, un.start);
+              tma_load_2d(dst, &tm_x128, fullB(s), kx, un.start);
             } else {
               for (int i = 0; i < nbox; ++i)
-                tma_load_2d(sB + s * kBBytes + i * (kBoxRows * kBKB * 2), &tm_x, fullB(s), (g * 2 + h) * kBKB,
-                            un.start + kBoxRows * i);
+                tma_load_2d(dst + i * (kBoxRows * kBKB * 2), &tm_x, fullB(s), kx, un.start + kBoxRows * i);
             }
           }
         }

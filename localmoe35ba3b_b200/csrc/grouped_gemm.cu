@@ -17,8 +17,10 @@
 //      bf16 [128 x 64]  dequant warps -> 128B-swizzled K-major smem (4 slots,
 //                       filled in pairs: one int8 stage = two MMA stages); the
 //                       MMA's B operand
-//   X  bf16 [128 x 64]  TMA tiles of 128 consecutive route rows -> same layout
-//                       (the MMA's A operand)
+//   X  bf16 [128 x 128] per stage, two 64-column chunks of 32-row TMA boxes
+//                       covering the tile's routes, on one barrier (a warp's
+//                       bulk copies stream at about one barrier stage per 0.4 us
+//                       whatever their size) -> same layout (the MMA's A operand)
 //   D  fp32 [128 token lanes x 128 weight columns] in tensor memory, 4 buffers
 // so an epilogue thread owns one route row and finds that row's output
 // columns contiguous in its tensor-memory lane: it stores 16-byte vectors,
@@ -47,13 +49,15 @@ constexpr int kBK = 64;    // MMA stage: one 128-byte swizzle atom of 16-bit K v
 constexpr int kBK8 = 128;  // int8 stage: one scale group
 constexpr int kNS8 = 4;    // int8 weight stages
 constexpr int kNA = 4;     // bf16 weight slots (two pairs)
-constexpr int kNS = 6;     // activation stages
+constexpr int kNS = 3;     // activation stages (one per int8 stage: K 128)
 constexpr int kGemmThreads = 512;
 constexpr int kDeqWarp0 = 4, kDeqWarps = 8;
 constexpr int kEpiWarp0 = 12;
 constexpr int kA8Bytes = kBM * kBK8;
 constexpr int kA16Bytes = kBM * kBK * 2;
-constexpr int kBBytes = kTileRoutes * kBK * 2;
+constexpr int kBBytes = kTileRoutes * kBK * 2;    // one 64-column chunk
+constexpr int kBChunks = kBK8 / kBK;              // chunks per activation stage
+constexpr int kBStage = kBChunks * kBBytes;
 constexpr int kXBoxRows = 32;  // activation TMA box rows: a tile loads only the boxes covering its routes
 constexpr int kTmemBufs = 4;                 // accumulator buffers
 constexpr int kTmemCols = kTmemBufs * kBM;   // 4 x 128 fp32 columns
@@ -83,7 +87,7 @@ struct GemmSmem {
   static constexpr int a8 = 0;
   static constexpr int a16 = a8 + kNS8 * kA8Bytes;
   static constexpr int b = a16 + kNA * kA16Bytes;
-  static constexpr int bars = b + kNS * kBBytes;
+  static constexpr int bars = b + kNS * kBStage;
   // full8, empty8 (kNS8 each); fullA, emptyA (one per slot pair); fullB, emptyB (kNS each);
   // tfull, tempty (kTmemBufs each); drain
   static constexpr int nbars = 2 * kNS8 + 2 * (kNA / 2) + 2 * kNS + 2 * kTmemBufs + 1;
@@ -91,8 +95,6 @@ struct GemmSmem {
   static constexpr int bytes = misc + 64;
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
 };
-static_assert(GemmSmem::alloc <= 232448, "shared memory per block");
-
 static_assert(GemmSmem::alloc <= 232448, "shared memory per block");
 
 // A work unit: one tile of routes of one expert x one block of output columns.
@@ -252,20 +254,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // one int8 stage = the A slot pair (2q, 2q + 1) = MMA stages kb and kb + 1
           const int q = ia % kPairs;
           if (!mbar_wait(fullA(q), (ia / kPairs) & 1, sAbort, p.err)) { ok = false; break; }
-          for (int h = 0; h < 2; ++h, ++it) {
-            const int s = it % kNS;
-            if (!mbar_wait(fullB(s), (it / kNS) & 1, sAbort, p.err)) { ok = false; break; }
-            tc_fence_after();
+          const int s = it % kNS;
+          if (!mbar_wait(fullB(s), (it / kNS) & 1, sAbort, p.err)) { ok = false; break; }
+          ++it;
+          tc_fence_after();
+#pragma unroll
+          for (int h = 0; h < kBChunks; ++h) {
             // A = the route rows (activations), B = the dequantised weight rows
             const uint64_t wd = sdesc_k_sw128(sA16 + (2 * q + h) * kA16Bytes);
-            const uint64_t xd = sdesc_k_sw128(sB + s * kBBytes);
+            const uint64_t xd = sdesc_k_sw128(sB + s * kBStage + h * kBBytes);
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
               mma_f16(dt, xd + (uint64_t)(kk * 2), wd + (uint64_t)(kk * 2), idesc, ((kb + h) | kk) != 0);
-            mma_commit(emptyB(s));
-            issued = true;
           }
-          if (ok) mma_commit(emptyA(q));
+          mma_commit(emptyB(s));
+          mma_commit(emptyA(q));
+          issued = true;
         }
         // also after an abort, so the epilogue's wait ends (a commit with no
         // MMA issued before it is not relied on to arrive)
@@ -286,7 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int u = blockIdx.x; ok; u += stride) {
         Unit un;
         if (!get_unit(p, u, nblocks, un)) break;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb8 = 0; kb8 < KB8; ++kb8, ++it) {
           const int s = it % kNS;
           if (!mbar_wait(emptyB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           // boxes of 32 route rows covering the tile: the bytes moved from L2 bind this
@@ -294,10 +298,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // those boxes keep older data and rows past the tile belong to other tiles
           // (or read as zeros past the tensor); none of them is ever stored.
           const int nbox = (un.count + kXBoxRows - 1) / kXBoxRows;
-          mbar_arrive_expect_tx(fullB(s), (uint32_t)(nbox * kXBoxRows * kBK * 2));
-          for (int i = 0; i < nbox; ++i)
-            tma_load_2d(sB + s * kBBytes + i * (kXBoxRows * kBK * 2), &tm_x, fullB(s), kb * kBK,
-                        un.start + kXBoxRows * i);
+          mbar_arrive_expect_tx(fullB(s), (uint32_t)(kBChunks * nbox * kXBoxRows * kBK * 2));
+          for (int h = 0; h < kBChunks; ++h)
+            for (int i = 0; i < nbox; ++i)
+              tma_load_2d(sB + s * kBStage + h * kBBytes + i * (kXBoxRows * kBK * 2), &tm_x, fullB(s),
+                          (kb8 * kBChunks + h) * kBK, un.start + kXBoxRows * i);
         }
       }
       for (int k = max(0, it - kNS); k < it; ++k) mbar_wait_drain(fullB(k % kNS), (k / kNS) & 1, p.err);

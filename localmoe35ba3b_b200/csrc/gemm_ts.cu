@@ -11,23 +11,27 @@
 // Layout: the MMA's M side is 128 weight rows of one expert (64 gate rows and
 // the matching 64 up rows), its N side is a tile of <= 128 routes rounded up to
 // 16, K streams in 128-wide int8 stages (one scale group).
-//   W  int8 [128 x 128]  TMA -> 128B-swizzled smem ring
+//   W  int8 [128 x 128]  TMA -> 128B-swizzled smem ring (4 stages, two
+//                        producer warps)
 //      bf16              dequant warps -> tensor memory (tcgen05.st): the MMA's
-//                        A operand, 64 columns per stage, 4 slots; weights never
-//                        pass through shared memory in 16-bit form
-//   X  bf16 [N x 128]    two 64-column chunks per stage, one barrier per stage
-//                        (TMA boxes of 32 route rows, or 128 for a full tile)
-//                        -> 128B-swizzled smem ring: the MMA's B operand
+//                        A operand, 64 columns per stage; weights never pass
+//                        through shared memory in 16-bit form
+//   X  bf16 [N x 128]    two 64-column chunks per stage (TMA boxes of 32 route
+//                        rows, or 128 for a full tile) -> 128B-swizzled smem:
+//                        the MMA's B operand
+//   MMA stage s (4 of them) = A slot s + X stage s, with one "ready" barrier
+//   (dequantisers + the activation bytes) and one "freed" barrier (the MMAs'
+//   commit), so the single MMA-issuing thread waits and commits once per stage
 //   D  fp32 [128 lanes x 128 columns] in tensor memory, two buffers
 // Shared-memory traffic per MAC is therefore the int8 tile (TMA write + one
 // read) and the route rows (TMA write + the MMA's read), about half of what an
 // MMA with both operands in shared memory needs; with N <= 128 the MMA time
 // scales with the tile's routes, so small experts cost little beyond their
 // weight stream.
-// Warp roles (512 threads): w0 weight TMA, w1 TMEM owner + MMA issuer,
-// w2 activation TMA, w3 idle, w4-11 dequantisers (warp w writes TMEM lanes of
-// quadrant w % 4, K half (w - 4) / 4), w12-15 epilogue (quadrant w % 4; gate
-// rows in w12-13, up rows in w14-15).
+// Warp roles (512 threads): w0 + w3 weight TMA (alternate stages), w1 TMEM
+// owner + MMA issuer, w2 activation TMA, w4-11 dequantisers (warp w writes
+// TMEM lanes of quadrant w % 4, K half (w - 4) / 4), w12-15 epilogue
+// (quadrant w % 4; gate rows in w12-13, up rows in w14-15).
 // Every wait is bounded (LMOE_WAIT_NS); a timeout raises the CTA abort flag and
 // the caller's error word, every role drains and the CTA exits.
 #include "common.cuh"
@@ -39,11 +43,10 @@ namespace ts {
 
 constexpr int kBM = 128;       // weight rows per unit: MMA M
 constexpr int kBK8 = 128;      // int8 stage K (one scale group)
-constexpr int kNS8 = 6;        // int8 stages
+constexpr int kNS8 = 4;        // int8 stages
 constexpr int kBKB = 64;       // activation chunk K (one 128-byte swizzle atom)
 constexpr int kBChunks = kBK8 / kBKB;  // chunks per activation stage: one stage per int8 stage
-constexpr int kNSB = 3;        // activation stages
-constexpr int kNA = 4;         // tensor-memory A slots
+constexpr int kNA = 4;         // MMA stages: tensor-memory A slot + shared-memory activation stage
 constexpr int kBoxRows = 32;   // activation TMA box rows
 constexpr int kThreads = 512;
 constexpr int kConvWarps = 8;
@@ -58,15 +61,16 @@ constexpr int kUPitch = 80;                       // bytes per up row in the exc
 constexpr int kUBytes = 64 * kUPitch;             // [64 rows][32 routes] 16-bit, padded rows
 constexpr int kHBytes = 32 * 64 * 2;              // [32 routes][64 columns] 16-bit
 static_assert(kACol0 + kNA * kASlotCols <= kTmemCols, "tensor memory budget");
+static_assert(kNS8 % 2 == 0, "two weight producers own alternate stages");
 
 struct Smem {
   static constexpr int a8 = 0;
   static constexpr int b = a8 + kNS8 * kA8Bytes;
-  static constexpr int u = b + kNSB * kBStage;
+  static constexpr int u = b + kNA * kBStage;
   static constexpr int h = u + 2 * kUBytes;
   static constexpr int bars = h + 2 * kHBytes;
-  // full8, empty8 (kNS8 each); fullA, emptyA (kNA each); fullB, emptyB (kNSB each); tfull, tempty (2 each); drain
-  static constexpr int nbars = 2 * kNS8 + 2 * kNA + 2 * kNSB + 4 + 1;
+  // full8, empty8 (kNS8 each); ready, freed (kNA each); tfull, tempty (2 each); drain
+  static constexpr int nbars = 2 * kNS8 + 2 * kNA + 4 + 1;
   static constexpr int misc = bars + nbars * 8;
   static constexpr int bytes = misc + 64;
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
@@ -137,13 +141,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   auto full8 = [&](int s) { return bar0 + 8u * s; };
   auto empty8 = [&](int s) { return bar0 + 8u * (kNS8 + s); };
-  auto fullA = [&](int s) { return bar0 + 8u * (2 * kNS8 + s); };
-  auto emptyA = [&](int s) { return bar0 + 8u * (2 * kNS8 + kNA + s); };
-  auto fullB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + s); };
-  auto emptyB = [&](int s) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + kNSB + s); };
-  auto tfull = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 * kNSB + b); };
-  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 * kNSB + 2 + b); };
-  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 * kNSB + 4);
+  // MMA stage s: ready(s) completes when the 8 dequantiser warps have written A slot s
+  // and the activation stage s has landed; freed(s) when the MMAs reading both are done
+  auto ready = [&](int s) { return bar0 + 8u * (2 * kNS8 + s); };
+  auto freed = [&](int s) { return bar0 + 8u * (2 * kNS8 + kNA + s); };
+  auto tfull = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + b); };
+  auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (2 * kNS8 + 2 * kNA + 4);
 
   const int nblocks = (int)(p.inter / 64);
   const int G = (int)(p.K / kBK8);
@@ -155,12 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(empty8(s), kConvWarps);
     }
     for (int s = 0; s < kNA; ++s) {
-      mbar_init(fullA(s), kConvWarps);
-      mbar_init(emptyA(s), 1);
-    }
-    for (int s = 0; s < kNSB; ++s) {
-      mbar_init(fullB(s), 1);
-      mbar_init(emptyB(s), 1);
+      mbar_init(ready(s), kConvWarps + 1);  // + the activation producer's expect-tx arrival
+      mbar_init(freed(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull(b), 1);
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *sAbort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  if ((warp == 0 || warp == 3) && lane == 0) {
     prefetch_tmap(&tm_bank);
     prefetch_tmap(&tm_g);
     prefetch_tmap(&tm_u);
@@ -189,15 +189,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *sTmem;
   const int stride = gridDim.x;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 3) {
     // ------------------------------------------------------------ weight TMA
+    // two producer warps take alternate stages: one warp's bulk copies on
+    // different barriers complete one after another (about one HBM latency
+    // each), so a second warp doubles the weight stream; stage s always
+    // belongs to warp (s & 1) since kNS8 is even
     if (lane == 0) {
+      const int mine = warp == 3 ? 1 : 0;
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok; u += stride) {
         Unit un;
         if (!get_unit(p, u, nblocks, un)) break;
         for (int g = 0; g < G; ++g, ++it) {
+          if ((it & 1) != mine) continue;
           const int s8 = it % kNS8;
           if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(full8(s8), kA8Bytes);
@@ -211,14 +217,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      for (int k = max(0, it - kNS8); k < it; ++k) mbar_wait_drain(full8(k % kNS8), (k / kNS8) & 1, p.err);
+      for (int k = max(0, it - kNS8); k < it; ++k)
+        if ((k & 1) == mine) mbar_wait_drain(full8(k % kNS8), (k / kNS8) & 1, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int ia = 0, ib = 0, ui = 0;
+      // one thread issues every MMA: the issue path (about 70-90 cycles per MMA
+      // plus each wait and commit) is this kernel's critical path, so a stage
+      // costs one wait, 8 MMAs and one commit
+      int it = 0, ui = 0;
       bool ok = true, issued = false;
+      const uint64_t bd0 = sdesc_k_sw128(sB);
       for (int u = blockIdx.x; ok; u += stride, ++ui) {
         Unit un;
         if (!get_unit(p, u, nblocks, un)) break;
@@ -228,23 +239,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(tempty(b), ((ui >> 1) & 1) ^ 1, sAbort, p.err)) break;
         tc_fence_after();
         const uint32_t dt = tmem + (uint32_t)(b * kAccCols);
-        for (int g = 0; g < G && ok; ++g, ++ia) {
-          const int a = ia % kNA;
-          if (!mbar_wait(fullA(a), (ia / kNA) & 1, sAbort, p.err)) { ok = false; break; }
-          const int s = ib % kNSB;
-          if (!mbar_wait(fullB(s), (ib / kNSB) & 1, sAbort, p.err)) { ok = false; break; }
-          ++ib;
+        for (int g = 0; g < G; ++g, ++it) {
+          const int s = it % kNA;
+          if (!mbar_wait(ready(s), (it / kNA) & 1, sAbort, p.err)) { ok = false; break; }
           tc_fence_after();
+          const uint32_t acol = tmem + (uint32_t)(kACol0 + s * kASlotCols);
+          const uint64_t bd = bd0 + (uint64_t)((s * kBStage) >> 4);
 #pragma unroll
-          for (int h = 0; h < kBChunks; ++h) {
-            const uint64_t bd = sdesc_k_sw128(sB + s * kBStage + h * kBBytes);
-            const uint32_t acol = tmem + (uint32_t)(kACol0 + a * kASlotCols + h * 32);
+          for (int h = 0; h < kBChunks; ++h)
 #pragma unroll
             for (int kk = 0; kk < kBKB / 16; ++kk)
-              mma_f16_ts(dt, acol + (uint32_t)(kk * 8), bd + (uint64_t)(kk * 2), idesc, (g | h | kk) != 0);
-          }
-          mma_commit(emptyB(s));
-          mma_commit(emptyA(a));
+              mma_f16_ts(dt, acol + (uint32_t)(h * 32 + kk * 8), bd + (uint64_t)(((h * kBBytes) >> 4) + kk * 2), idesc,
+                         (g | h | kk) != 0);
+          mma_commit(freed(s));
           issued = true;
         }
         // also after an abort, so the epilogue's wait ends
@@ -275,22 +282,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nbox = big ? 1 : (un.count + kBoxRows - 1) / kBoxRows;
         const uint32_t bytes = kBChunks * (big ? (uint32_t)kBBytes : (uint32_t)(nbox * kBoxRows * kBKB * 2));
         for (int g = 0; g < G; ++g, ++ib) {
-          const int s = ib % kNSB;
-          if (!mbar_wait(emptyB(s), ((ib / kNSB) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-          mbar_arrive_expect_tx(fullB(s), bytes);
+          const int s = ib % kNA;
+          if (!mbar_wait(freed(s), ((ib / kNA) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(ready(s), bytes);
           for (int h = 0; h < kBChunks; ++h) {
             const uint32_t dst = sB + s * kBStage + h * kBBytes;
             const int kx = (g * kBChunks + h) * kBKB;
             if (big) {
-              tma_load_2d(dst, &tm_x128, fullB(s), kx, un.start);
+              tma_load_2d(dst, &tm_x128, ready(s), kx, un.start);
             } else {
               for (int i = 0; i < nbox; ++i)
-                tma_load_2d(dst + i * (kBoxRows * kBKB * 2), &tm_x, fullB(s), kx, un.start + kBoxRows * i);
+                tma_load_2d(dst + i * (kBoxRows * kBKB * 2), &tm_x, ready(s), kx, un.start + kBoxRows * i);
             }
           }
         }
       }
-      for (int k = max(0, ib - kNSB); k < ib; ++k) mbar_wait_drain(fullB(k % kNSB), (k / kNSB) & 1, p.err);
+      // never leave a bulk copy in flight into shared memory that is about to be
+      // released: the last stages' ready phases also need the dequantisers'
+      // arrivals, which come within microseconds (or, after an abort, the bounded
+      // wait runs out)
+      for (int k = max(0, ib - kNA); k < ib; ++k) mbar_wait_drain(ready(k % kNA), (k / kNA) & 1, p.err);
     }
     __syncwarp();
   } else if (warp >= 4 && warp < 4 + kConvWarps) {
@@ -323,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4 v[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = lds128(a8 + (uint32_t)(((kh * 4 + j) ^ (r & 7)) << 4));
-        if (!warp_wait(emptyA(a), ((it8 / kNA) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
+        if (!warp_wait(freed(a), ((it8 / kNA) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
         uint32_t o[32];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -341,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(fullA(a));
+          mbar_arrive(ready(a));
           mbar_arrive(empty8(s8));
         }
         sc = sn;

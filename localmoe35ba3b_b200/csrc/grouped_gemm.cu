@@ -28,8 +28,8 @@
 // The kernel is persistent: one CTA per SM walks the (tile, column-block)
 // work units in a fixed stride, so the epilogue of one unit overlaps the main
 // loop of the next ones.
-// Warp roles (512 threads): w0 weight TMA, w1 TMEM owner + MMA issuer,
-// w2 activation TMA, w3 idle, w4-11 dequantisers, w12-15 epilogue.
+// Warp roles (512 threads): w0 + w3 weight TMA (alternate stages), w1 TMEM
+// owner + MMA issuer, w2 activation TMA, w4-11 dequantisers, w12-15 epilogue.
 // Epilogue modes: PLAIN (y = round(acc)), SWIGLU (gate columns 0-63 and up
 // columns 64-127 of the unit give hidden = round(round(silu(g)) * u), the
 // reference's gpu_routes.py:74-75), WEIGHTED (v = round(round(acc) * w_route),
@@ -96,6 +96,7 @@ struct GemmSmem {
   static constexpr int alloc = bytes + 1024;  // slack for 1024-byte alignment
 };
 static_assert(GemmSmem::alloc <= 232448, "shared memory per block");
+static_assert(kNS8 % 2 == 0, "two weight producers own alternate stages");
 
 // A work unit: one tile of routes of one expert x one block of output columns.
 struct Unit {
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     *sAbort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  if ((warp == 0 || warp == 3) && lane == 0) {
     prefetch_tmap(&tm_bank);
     prefetch_tmap(&tm_lo);
     prefetch_tmap(&tm_hi);
@@ -213,9 +214,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = *sTmem;
   const int stride = gridDim.x;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 3) {
     // ------------------------------------------------------------ weight TMA
+    // two producer warps take alternate stages (one warp's bulk copies on
+    // different barriers complete one after another); stage s always belongs
+    // to warp (s & 1) since kNS8 is even
     if (lane == 0) {
+      const int mine = warp == 3 ? 1 : 0;
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok; u += stride) {
@@ -226,6 +231,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const CUtensorMap* mlo = un.shared ? &tm_lo : &tm_bank;
         const CUtensorMap* mhi = un.shared ? (swiglu ? &tm_hi : &tm_lo) : &tm_bank;
         for (int kb = 0; kb < KB8; ++kb, ++it) {
+          if ((it & 1) != mine) continue;
           const int s8 = it % kNS8;
           if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(full8(s8), kA8Bytes);
@@ -234,7 +240,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       // never leave a bulk copy in flight into shared memory that is about to be released
-      for (int k = max(0, it - kNS8); k < it; ++k) mbar_wait_drain(full8(k % kNS8), (k / kNS8) & 1, p.err);
+      for (int k = max(0, it - kNS8); k < it; ++k)
+        if ((k & 1) == mine) mbar_wait_drain(full8(k % kNS8), (k / kNS8) & 1, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {

@@ -145,7 +145,7 @@ template <int DT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tm_bank, const __grid_constant__ CUtensorMap tm_lo,
                               const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_x,
-                              const GemmParams p) {
+                              const __grid_constant__ CUtensorMap tm_x128, const GemmParams p) {
   using A = Act<DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -203,7 +203,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tm_lo);
     prefetch_tmap(&tm_hi);
   }
-  if (warp == 2 && lane == 0) prefetch_tmap(&tm_x);
+  if (warp == 2 && lane == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_x128);
+  }
   if (warp == 1) {
     tmem_alloc(smem_u32(sTmem), kTmemCols);
     tmem_relinquish();
@@ -300,16 +303,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb8 = 0; kb8 < KB8; ++kb8, ++it) {
           const int s = it % kNS;
           if (!mbar_wait(emptyB(s), ((it / kNS) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
-          // boxes of 32 route rows covering the tile: the bytes moved from L2 bind this
-          // kernel, so a small tile does not load 128 rows.  Rows of the MMA tile past
-          // those boxes keep older data and rows past the tile belong to other tiles
-          // (or read as zeros past the tensor); none of them is ever stored.
-          const int nbox = (un.count + kXBoxRows - 1) / kXBoxRows;
-          mbar_arrive_expect_tx(fullB(s), (uint32_t)(kBChunks * nbox * kXBoxRows * kBK * 2));
-          for (int h = 0; h < kBChunks; ++h)
-            for (int i = 0; i < nbox; ++i)
-              tma_load_2d(sB + s * kBStage + h * kBBytes + i * (kXBoxRows * kBK * 2), &tm_x, fullB(s),
-                          (kb8 * kBChunks + h) * kBK, un.start + kXBoxRows * i);
+          // boxes of 32 route rows covering the tile: a small tile does not load 128
+          // rows.  Rows of the MMA tile past those boxes keep older data and rows past
+          // the tile belong to other tiles (or read as zeros past the tensor); none of
+          // them is ever stored.  A nearly full tile takes one 128-row box per chunk
+          // instead of four: a warp's bulk copies cost about the same per copy
+          // whatever their size.
+          const bool big = un.count > 3 * kXBoxRows;
+          const int nbox = big ? 1 : (un.count + kXBoxRows - 1) / kXBoxRows;
+          const uint32_t chunk_bytes = big ? (uint32_t)kBBytes : (uint32_t)(nbox * kXBoxRows * kBK * 2);
+          mbar_arrive_expect_tx(fullB(s), kBChunks * chunk_bytes);
+          for (int h = 0; h < kBChunks; ++h) {
+            const uint32_t dst = sB + s * kBStage + h * kBBytes;
+            const int kx = (kb8 * kBChunks + h) * kBK;
+            if (big) {
+              tma_load_2d(dst, &tm_x128, fullB(s), kx, un.start);
+            } else {
+              for (int i = 0; i < nbox; ++i)
+                tma_load_2d(dst + i * (kXBoxRows * kBK * 2), &tm_x, fullB(s), kx, un.start + kXBoxRows * i);
+            }
+          }
         }
       }
       for (int k = max(0, it - kNS); k < it; ++k) mbar_wait_drain(fullB(k % kNS), (k / kNS) & 1, p.err);
@@ -572,7 +585,7 @@ int sm_count() {
 int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st) {
   if (L.K % kGroup || L.K <= 0) return LMOE_ERR_INVALID;
   if (L.grid_tiles <= 0) return LMOE_OK;
-  CUtensorMap tb, tl, th, tx;
+  CUtensorMap tb, tl, th, tx, tx128;
   int rc = make_int8_map(&tb, L.q_bank, L.experts * L.N, L.K);
   if (rc) return rc;
   tl = tb;
@@ -580,6 +593,7 @@ int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st) {
   if (L.q_lo && (rc = make_int8_map(&tl, L.q_lo, L.rows_lo, L.K))) return rc;
   if (L.q_hi && (rc = make_int8_map(&th, L.q_hi, L.rows_hi, L.K))) return rc;
   if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype, kXBoxRows))) return rc;
+  if ((rc = make_act_map(&tx128, L.x, L.x_rows, L.K, L.dtype, kTileRoutes))) return rc;
   GemmParams p = {};
   p.K = L.K;
   p.tiles = L.tiles;
@@ -608,11 +622,11 @@ int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st) {
   if (L.dtype == LMOE_BF16) {
     auto k = grouped_gemm_w8a16_kernel<LMOE_BF16>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<(unsigned)ctas, kGemmThreads, smem, st>>>(tb, tl, th, tx, p);
+    k<<<(unsigned)ctas, kGemmThreads, smem, st>>>(tb, tl, th, tx, tx128, p);
   } else if (L.dtype == LMOE_F16) {
     auto k = grouped_gemm_w8a16_kernel<LMOE_F16>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<(unsigned)ctas, kGemmThreads, smem, st>>>(tb, tl, th, tx, p);
+    k<<<(unsigned)ctas, kGemmThreads, smem, st>>>(tb, tl, th, tx, tx128, p);
   } else {
     return LMOE_ERR_INVALID;
   }

@@ -37,14 +37,16 @@ HIDDEN, INTER, EXPERTS, TOP = 2048, 512, 256, 8
 EXPERT_BYTES = 3 * INTER * HIDDEN + 3 * INTER * HIDDEN // 128 * 4  # 3,244,032
 METRIC = 'expert-FFN prefill tok/s (2048-chunk x 40 layers, W8A16)'
 UNIT = 'tok/s'
-# Kernels launched per layer of the step: route_kernel, permute_rows_kernel, grouped GEMM
-# (gate_up), grouped GEMM (down), moe_combine_kernel.
-LAUNCHES_PER_LAYER = 5
+# Kernels launched per layer of the step: meta_count_kernel, meta_scan_kernel,
+# meta_place_kernel (routing metadata), permute_rows_kernel, gate_up_ts_kernel (gate_up +
+# SwiGLU), grouped_gemm_w8a16_kernel (down + routing weight), moe_combine_kernel.
+LAUNCHES_PER_LAYER = 7
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
 # `ncu --set full` capture of layer 0 (`python bench.py --layers 2 --steps 1 --warmup 1
-# --no-cpu-baseline`, -k regex:grouped_gemm -s 4 -c 2): gate_up 429.1 MB + down 253.6 MB.
-# Per-layer work does not depend on the layer count, so no scaling is applied.
-NCU_TRAFFIC_PER_LAYER = 682.7e6
+# --no-cpu-baseline --no-extra`, -k "regex:gate_up_ts|grouped_gemm" -s 2 -c 2):
+# gate_up 404.6 MB + down 246.0 MB.  Per-layer work does not depend on the layer count, so
+# no scaling is applied.
+NCU_TRAFFIC_PER_LAYER = 650.6e6
 NCU_TRAFFIC_SOURCE = ('ncu dram__bytes_read.sum + dram__bytes_write.sum, gate_up + down launches of one '
                       '2048-token layer; bytes per layer like alg_bytes_per_layer')
 

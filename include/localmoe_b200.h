@@ -165,6 +165,17 @@ LMOE_API int lmoe_decode_moe(const void* x, const float* weights, const int64_t*
                              const void* residual, void* out, int dtype, int w8a8, void* ws, int* err,
                              void* stream);
 
+/* Router tail of the sparse-MoE block: replaces the HF Qwen3_5MoeTopKRouter.forward tail
+ * (transformers qwen3_5_moe/modeling_qwen3_5_moe.py:765-769) that the reference drives
+ * unchanged (qwen35_deploy/model.py:57-68 swaps only the experts and the linears).
+ * logits [tokens, experts] in the activation dtype (the block's F.linear(x, gate.weight));
+ * weights [tokens, top] fp32 = topk(softmax(float(logits))) / their sum, ids [tokens, top]
+ * int64 in descending probability, ties to the lower expert id; probs (nullable)
+ * [tokens, experts] fp32 = the softmax (HF returns it as router_logits).  experts must be
+ * 32, 64, 128, 256 or 512 (else LMOE_ERR_UNSUPPORTED); 1 <= top <= min(32, experts). */
+LMOE_API int lmoe_router_topk(const void* logits, int64_t tokens, int64_t experts, int64_t top, float* weights,
+                              int64_t* ids, float* probs, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

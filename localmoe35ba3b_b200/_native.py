@@ -43,6 +43,7 @@ SIGNATURES = {
     'lmoe_decode_workspace_size': (_I64, [_I64, _I64, _I64]),
     'lmoe_decode_moe': (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64,
                              _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
+    'lmoe_router_topk': (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _I, _P]),
 }
 
 _lib = None

@@ -60,3 +60,48 @@ def rel_maxabs(got, ref):
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def write_conversion(root, layers, E, H, I, seed=0):
+    """A small converted checkpoint in the reference converter's output format
+    (convert.py:60-118: per-tensor safetensors files, per-record size and
+    SHA-256, manifest.json with complete=True) holding the MoE tensors of
+    ``layers`` layers.  Returns {layer: {name suffix: numpy arrays}}."""
+    import hashlib
+    import json
+    import os
+    from safetensors.torch import save_file
+    r = rng(seed)
+    records, truth = [], {}
+
+    def put(name, values, fmt):
+        key = hashlib.sha256(name.encode()).hexdigest()[:24]
+        path = os.path.join(root, key + '.safetensors')
+        save_file({k: torch.from_numpy(np.ascontiguousarray(v)) if isinstance(v, np.ndarray) else v
+                   for k, v in values.items()}, path)
+        with open(path, 'rb') as f:
+            digest = hashlib.sha256(f.read()).hexdigest()
+        first = next(iter(values.values()))
+        records.append({'name': name, 'shape': list(first.shape), 'file': key + '.safetensors', 'sha256': digest,
+                        'bytes': os.path.getsize(path), 'format': fmt})
+
+    for layer in range(layers):
+        p = f'model.language_model.layers.{layer}.mlp.'
+        t = {}
+        t['gate_up'] = rand_q(r, (E, 2 * I, H))
+        t['down'] = rand_q(r, (E, H, I))
+        t['shared'] = [rand_q(r, (I, H)), rand_q(r, (I, H)), rand_q(r, (H, I))]
+        t['shared_gate'] = act(r, (1, H), BF16, 0.02)
+        t['router'] = act(r, (E, H), BF16, 0.05)
+        put(p + 'experts.gate_up_proj', {'q': t['gate_up'][0], 'scale': t['gate_up'][1]}, 'int8_g128_fp32scale')
+        put(p + 'experts.down_proj', {'q': t['down'][0], 'scale': t['down'][1]}, 'int8_g128_fp32scale')
+        for n, (q, s) in zip(('gate_proj', 'up_proj', 'down_proj'), t['shared']):
+            put(p + f'shared_expert.{n}.weight', {'q': q, 'scale': s}, 'int8_g128_fp32scale')
+        put(p + 'shared_expert_gate.weight', {'weight': torch.from_numpy(t['shared_gate']).to(torch.bfloat16)},
+            'original')
+        put(p + 'gate.weight', {'weight': torch.from_numpy(t['router']).to(torch.bfloat16)}, 'original')
+        truth[layer] = t
+    with open(os.path.join(root, 'manifest.json'), 'w') as f:
+        json.dump({'identity': {'format': 'q36-w8a16-g128-rtn-fp32scale-v1'}, 'records': records, 'complete': True,
+                   'bytes': sum(x['bytes'] for x in records)}, f)
+    return truth

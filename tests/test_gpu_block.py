@@ -134,3 +134,26 @@ def test_sparse_moe_block_router_outputs():
     assert scores.shape == (2 * T, top) and scores.dtype == torch.float32
     assert ids.shape == (2 * T, top) and ids.dtype == torch.int64
     assert torch.allclose(scores.sum(-1), torch.ones(2 * T, device='cuda'), atol=1e-6)
+
+
+def test_blocks_from_converted_checkpoint(tmp_path):
+    """A conversion in the reference's format loads straight onto the GPU and
+    the blocks built from it match the oracle on the same tensors."""
+    from helpers import write_conversion
+    from localmoe35ba3b_b200.runtime import checkpoint
+    E, H, I, top, T = 32, 512, 256, 4, 40
+    truth = write_conversion(str(tmp_path), layers=2, E=E, H=H, I=I, seed=21)
+    blocks = checkpoint.load_blocks(tmp_path, top_k=top, device='cuda', activation='w8a16')
+    assert len(blocks) == 2 and blocks[0].bank0.is_cuda
+    r = rng(22)
+    x = act(r, (T, H), BF16)
+    for layer, blk in enumerate(blocks):
+        t = truth[layer]
+        xd = to_dev(x, BF16)
+        out = blk(xd)
+        torch.cuda.synchronize()
+        logits = to_np(F.linear(xd, blk.gate.weight))
+        ids, w = O.route(logits, top)
+        bank = (t['gate_up'][0], t['gate_up'][1], t['down'][0], t['down'][1])
+        ref = O.moe_block(x, w, ids, bank, t['shared'], t['shared_gate'], BF16)
+        assert rel_maxabs(to_np(out), ref) < 1e-2

@@ -81,6 +81,39 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& f0, float& f1, fl
   f3 = __uint_as_float(m3) - magic;
 }
 
+// Dequantise one int8 word with packed f32x2 arithmetic: lo / hi = the packed
+// 16-bit pairs round_dtype(float(q_j) * s) for bytes j = 0,1 / 2,3.  Each lane of
+// sub.rn.f32x2 and mul.rn.f32x2 is the IEEE round-to-nearest operation of the
+// scalar path (i8x4_to_f32, __fmul_rn, Act::pack), so the results are the same bit
+// for bit with half the floating-point instructions.  s2 = splat2(scale).
+__device__ __forceinline__ uint64_t splat2(float s) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "r"(__float_as_uint(s)));
+  return r;
+}
+template <int DT>
+__device__ __forceinline__ void deq4(uint32_t w, uint64_t s2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  uint32_t m0, m1, m2, m3;
+  asm("prmt.b32 %0, %1, %2, 0x7650;" : "=r"(m0) : "r"(u), "r"(0x4B000000u));
+  asm("prmt.b32 %0, %1, %2, 0x7651;" : "=r"(m1) : "r"(u), "r"(0x4B000000u));
+  asm("prmt.b32 %0, %1, %2, 0x7652;" : "=r"(m2) : "r"(u), "r"(0x4B000000u));
+  asm("prmt.b32 %0, %1, %2, 0x7653;" : "=r"(m3) : "r"(u), "r"(0x4B000000u));
+  uint64_t a, b;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "r"(m0), "r"(m1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "r"(m2), "r"(m3));
+  const uint64_t magic2 = 0x4B0000804B000080ull;  // (2^23 + 128) in both lanes
+  asm("sub.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(magic2));
+  asm("sub.rn.f32x2 %0, %0, %1;" : "+l"(b) : "l"(magic2));
+  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(s2));
+  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(b) : "l"(s2));
+  uint32_t a0, a1, b0, b1;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a0), "=r"(a1) : "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(b0), "=r"(b1) : "l"(b));
+  lo = Act<DT>::pack(__uint_as_float(a0), __uint_as_float(a1));
+  hi = Act<DT>::pack(__uint_as_float(b0), __uint_as_float(b1));
+}
+
 // ---------------------------------------------------------------- timing
 __device__ __forceinline__ uint64_t gtime_ns() {
   uint64_t t;

@@ -336,16 +336,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 4; ++j) v[j] = lds128(a8 + (uint32_t)(((kh * 4 + j) ^ (r & 7)) << 4));
         if (!warp_wait(freed(a), ((it8 / kNA) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
         uint32_t o[32];
+        const uint64_t sc2 = splat2(sc);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint32_t wv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
 #pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            float f0, f1, f2, f3;
-            i8x4_to_f32(wv[m], f0, f1, f2, f3);
-            o[j * 8 + 2 * m] = A::pack(__fmul_rn(f0, sc), __fmul_rn(f1, sc));
-            o[j * 8 + 2 * m + 1] = A::pack(__fmul_rn(f2, sc), __fmul_rn(f3, sc));
-          }
+          for (int m = 0; m < 4; ++m) deq4<DT>(wv[m], sc2, o[j * 8 + 2 * m], o[j * 8 + 2 * m + 1]);
         }
         tmem_st32(tl + (uint32_t)(kACol0 + a * kASlotCols + kh * 32), o);
         tmem_st_wait();

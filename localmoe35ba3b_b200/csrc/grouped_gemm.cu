@@ -395,13 +395,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int r = rb + 4 * i;
           const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
           uint32_t o[8];
+          const uint64_t sc2 = splat2(sc[i]);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float f0, f1, f2, f3;
-            i8x4_to_f32(wv[j], f0, f1, f2, f3);
-            o[2 * j] = A::pack(__fmul_rn(f0, sc[i]), __fmul_rn(f1, sc[i]));
-            o[2 * j + 1] = A::pack(__fmul_rn(f2, sc[i]), __fmul_rn(f3, sc[i]));
-          }
+          for (int j = 0; j < 4; ++j) deq4<DT>(wv[j], sc2, o[2 * j], o[2 * j + 1]);
           const uint4 lo = make_uint4(o[0], o[1], o[2], o[3]), hi = make_uint4(o[4], o[5], o[6], o[7]);
           const uint32_t d0 = a16 + sw128_off(r, 2 * cc), d1 = a16 + sw128_off(r, 2 * cc + 1);
           // selects, not a branch: a divergent branch would issue each store twice

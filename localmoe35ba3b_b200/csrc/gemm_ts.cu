@@ -31,7 +31,8 @@
 // Warp roles (512 threads): w0 + w3 weight TMA (alternate stages), w1 TMEM
 // owner + MMA issuer, w2 activation TMA, w4-11 dequantisers (warp w writes
 // TMEM lanes of quadrant w % 4, K half (w - 4) / 4), w12-15 epilogue
-// (quadrant w % 4; gate rows in w12-13, up rows in w14-15).
+// (quadrant w % 4; up rows in w12-13, gate rows and the SiLU math in w14-15,
+// on other SMSPs than the MMA issuer w1).
 // Every wait is bounded (LMOE_WAIT_NS); a timeout raises the CTA abort flag and
 // the caller's error word, every role drains and the CTA exits.
 #include "common.cuh"
@@ -318,8 +319,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; ok; u += stride) {
       Unit un;
       if (!get_unit(p, u, nblocks, un)) break;
-      const bool up = r >= 64;
-      const int64_t grow = (up ? un.rhi : un.rlo) + (r & 63);
+      // TMEM lanes 0-63 take the up rows (shared-memory rows 64-127 of the stage),
+      // lanes 64-127 the gate rows (rows 0-63): the epilogue's SiLU work then runs
+      // in warps 14-15, away from the MMA issuer's SMSP
+      const int srow = r ^ 64;
+      const bool up = srow >= 64;
+      const int64_t grow = (up ? un.rhi : un.rlo) + (srow & 63);
       const int64_t rmax = un.shared ? p.rows_sh : p.rows_bank;
       const float* sp = (un.shared ? (up ? p.s_u : p.s_g) : p.s_bank) + grow * G;
       const bool valid = grow < rmax;
@@ -330,10 +335,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s8 = it8 % kNS8;
         const int a = it8 % kNA;
         if (!warp_wait(full8(s8), (it8 / kNS8) & 1, sAbort, p.err)) { ok = false; break; }
-        const uint32_t a8 = sA8 + s8 * kA8Bytes + r * 128;
+        const uint32_t a8 = sA8 + s8 * kA8Bytes + srow * 128;
         uint4 v[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = lds128(a8 + (uint32_t)(((kh * 4 + j) ^ (r & 7)) << 4));
+        for (int j = 0; j < 4; ++j) v[j] = lds128(a8 + (uint32_t)(((kh * 4 + j) ^ (srow & 7)) << 4));
         if (!warp_wait(freed(a), ((it8 / kNA) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
         uint32_t o[32];
         const uint64_t sc2 = splat2(sc);
@@ -358,10 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 12) {
     // ------------------------------------------------------------ epilogue
-    // per 32-route chunk: the up warps (q = 2, 3) hand their rounded values to
-    // the gate warps (q = 0, 1; same lane = same hidden column) through shared
-    // memory; the gate warps form hidden, transpose it through shared memory to
-    // [route][column] and store 16-byte row pieces
+    // per 32-route chunk: the up warps (q = 0, 1: TMEM lanes 0-63) hand their
+    // rounded values to the gate warps (q = 2, 3; same lane = same hidden column)
+    // through shared memory; the gate warps form hidden, transpose it through
+    // shared memory to [route][column] and store 16-byte row pieces
     const int q = warp - 12;
     const int row = q * 32 + lane;
     typename A::T* y = (typename A::T*)p.y;
@@ -393,20 +398,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!have) continue;
         uint8_t* ub = ubase + (chunk & 1) * kUBytes;
         uint8_t* hb = hbase + (chunk & 1) * kHBytes;
-        if (q >= 2) {
+        const int hc = row & 63;  // hidden column of this lane
+        if (q < 2) {
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) pk[j] = A::pack(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1]));
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            sts128(smem_u32(ub + (row - 64) * kUPitch + k * 16), make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]));
+            sts128(smem_u32(ub + hc * kUPitch + k * 16), make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]));
         }
         named_barrier(2 + (q & 1), 64);
-        if (q < 2) {
+        if (q >= 2) {
           uint32_t uu[16];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint4 t = lds128(smem_u32(ub + row * kUPitch + k * 16));
+            const uint4 t = lds128(smem_u32(ub + hc * kUPitch + k * 16));
             uu[4 * k] = t.x;
             uu[4 * k + 1] = t.y;
             uu[4 * k + 2] = t.z;
@@ -418,11 +424,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float gv = A::round(__uint_as_float(acc[jj]));
             const float upv = (jj & 1) ? A::hi_f(uu[jj >> 1]) : A::lo_f(uu[jj >> 1]);
             const float sl = A::round(silu_exact(gv));
-            hrow[jj * 64 + row] = A::bits(__fmul_rn(sl, upv));
+            hrow[jj * 64 + hc] = A::bits(__fmul_rn(sl, upv));
           }
           named_barrier(4, 64);
           // 64 threads: route e >> 1, columns (e & 1) * 32 .. + 31
-          const int e = q * 32 + lane;
+          const int e = (q - 2) * 32 + lane;
           const int tok = e >> 1, half = e & 1;
           const int ntok = min(32, un.count - c * 32);
           if (tok < ntok) {

@@ -38,8 +38,8 @@ EXPERT_BYTES = 3 * INTER * HIDDEN + 3 * INTER * HIDDEN // 128 * 4  # 3,244,032
 METRIC = 'expert-FFN prefill tok/s (2048-chunk x 40 layers, W8A16)'
 UNIT = 'tok/s'
 # Kernels launched per layer of the step: meta_count_kernel, meta_scan_kernel,
-# meta_place_kernel (routing metadata), permute_rows_kernel, gate_up_ts_kernel (gate_up +
-# SwiGLU), grouped_gemm_w8a16_kernel (down + routing weight), moe_combine_kernel.
+# meta_place_kernel (routing metadata), permute_rows_kernel, grouped_ts_kernel<.., false>
+# (gate_up + SwiGLU), grouped_ts_kernel<.., true> (down + routing weight), moe_combine_kernel.
 LAUNCHES_PER_LAYER = 7
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
 # `ncu --set full` capture of layer 0 (`python bench.py --layers 2 --steps 1 --warmup 1

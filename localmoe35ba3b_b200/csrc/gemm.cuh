@@ -35,8 +35,10 @@ struct GemmLaunch {
 };
 
 int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st);
-// gate_up with the SwiGLU epilogue on the TMEM-operand kernel (gemm_ts.cu)
+// gate_up with the SwiGLU epilogue / down with the routing-weight epilogue on the
+// TMEM-operand kernel (gemm_ts.cu)
 int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st);
+int launch_down_ts(const GemmLaunch& L, cudaStream_t st);
 
 // tensor maps (grouped_gemm.cu): int8 [rows, K] with a 64-row x 128-byte, 128B-swizzled box;
 // 16-bit activations [rows, K] with a box_rows x 64-element, 128B-swizzled box

@@ -61,6 +61,8 @@ constexpr int kTmemCols = 512;
 constexpr int kUPitch = 80;                       // bytes per up row in the exchange buffer
 constexpr int kUBytes = 64 * kUPitch;             // [64 rows][32 routes] 16-bit, padded rows
 constexpr int kHBytes = 32 * 64 * 2;              // [32 routes][64 columns] 16-bit
+constexpr int kDStageBytes = 32 * 128 * 2;        // down: [32 routes][128 columns] 16-bit
+static_assert(2 * kDStageBytes <= 2 * kUBytes + 2 * kHBytes, "down staging fits the gate_up exchange area");
 static_assert(kACol0 + kNA * kASlotCols <= kTmemCols, "tensor memory budget");
 static_assert(kNS8 % 2 == 0, "two weight producers own alternate stages");
 
@@ -79,17 +81,19 @@ struct Smem {
 static_assert(Smem::alloc <= 232448, "shared memory per block");
 
 struct Params {
-  int64_t K;               // hidden
-  int64_t inter;           // I: bank rows [0, I) gate, [I, 2I) up
+  int64_t K;               // gate_up: hidden; down: I
+  int64_t inter;           // gate_up: I (bank rows [0, I) gate, [I, 2I) up)
+  int64_t rows_e;          // rows of one expert's weight: gate_up 2I, down hidden
   const Tile* tiles;
   const int32_t* hdr;
-  int64_t rows_bank;       // experts * 2I
-  int64_t rows_sh;         // rows of the shared gate / up tensors (I)
-  const float* s_bank;     // [experts * 2I, K/128]
-  const float* s_g;        // shared gate scales [I, K/128]
+  int64_t rows_bank;       // experts * rows_e
+  int64_t rows_sh;         // rows of the shared expert's tensor(s): I (gate, up) or hidden (down)
+  const float* s_bank;     // [experts * rows_e, K/128]
+  const float* s_g;        // shared gate (down: the shared down) scales
   const float* s_u;        // shared up scales
+  const float* rweight;    // down: routing weight of each route row
   int experts;             // tiles with expert == experts are the shared expert
-  void* y;                 // hidden [rows, I]
+  void* y;                 // gate_up: hidden [rows, I]; down: weighted rows [rows, hidden]
   int64_t ldy;
   int* err;
 };
@@ -97,9 +101,13 @@ struct Params {
 struct Unit {
   int start, count, nb, expert;
   bool shared;
-  int64_t rlo, rhi;  // tensor-map rows of the gate and up halves
+  int64_t rlo, rhi;  // tensor-map rows of the unit's two 64-row halves (gate_up: gate, up)
 };
 
+// Unit u = (route tile u / nblocks, output block u % nblocks): gate_up blocks are 64
+// hidden columns (64 gate + the matching 64 up rows), down blocks 128 output columns
+// (128 consecutive rows of the expert's down weight).
+template <bool DOWN>
 __device__ __forceinline__ bool get_unit(const Params& p, int u, int nblocks, Unit& o) {
   const int t = u / nblocks;
   if (t >= p.hdr[kHdrNumTiles]) return false;
@@ -109,10 +117,15 @@ __device__ __forceinline__ bool get_unit(const Params& p, int u, int nblocks, Un
   o.start = tl.start;
   o.count = tl.count;
   o.shared = tl.expert == p.experts;
-  const int64_t col = (int64_t)o.nb * 64;
-  const int64_t ebase = o.shared ? 0 : (int64_t)tl.expert * 2 * p.inter;
-  o.rlo = ebase + col;
-  o.rhi = (o.shared ? 0 : ebase + p.inter) + col;
+  const int64_t ebase = o.shared ? 0 : (int64_t)tl.expert * p.rows_e;
+  if (DOWN) {
+    o.rlo = ebase + (int64_t)o.nb * 128;
+    o.rhi = o.rlo + 64;
+  } else {
+    const int64_t col = (int64_t)o.nb * 64;
+    o.rlo = ebase + col;
+    o.rhi = (o.shared ? 0 : ebase + p.inter) + col;
+  }
   return o.count > 0;
 }
 
@@ -124,9 +137,10 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 
 __device__ __forceinline__ float silu_exact(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
-template <int DT>
+// DOWN = false: gate_up + SwiGLU; DOWN = true: down + routing weight.
+template <int DT, bool DOWN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gate_up_ts_kernel(const __grid_constant__ CUtensorMap tm_bank, const __grid_constant__ CUtensorMap tm_g,
+    grouped_ts_kernel(const __grid_constant__ CUtensorMap tm_bank, const __grid_constant__ CUtensorMap tm_g,
                       const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_x,
                       const __grid_constant__ CUtensorMap tm_x128, const Params p) {
   using A = Act<DT>;
@@ -150,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tempty = [&](int b) { return bar0 + 8u * (2 * kNS8 + 2 * kNA + 2 + b); };
   const uint32_t drain = bar0 + 8u * (2 * kNS8 + 2 * kNA + 4);
 
-  const int nblocks = (int)(p.inter / 64);
+  const int nblocks = DOWN ? (int)(p.rows_e / 128) : (int)(p.inter / 64);
   const int G = (int)(p.K / kBK8);
   const int warp = warp_id(), lane = lane_id();
 
@@ -202,13 +216,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok; u += stride) {
         Unit un;
-        if (!get_unit(p, u, nblocks, un)) break;
+        if (!get_unit<DOWN>(p, u, nblocks, un)) break;
         for (int g = 0; g < G; ++g, ++it) {
           if ((it & 1) != mine) continue;
           const int s8 = it % kNS8;
           if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(full8(s8), kA8Bytes);
-          if (un.shared) {
+          if (DOWN) {
+            // 128 consecutive rows of one down weight: two 64-row boxes
+            const CUtensorMap* m = un.shared ? &tm_g : &tm_bank;
+            tma_load_2d(sA8 + s8 * kA8Bytes, m, full8(s8), g * kBK8, (int)un.rlo);
+            tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, m, full8(s8), g * kBK8, (int)un.rhi);
+          } else if (un.shared) {
             tma_load_2d(sA8 + s8 * kA8Bytes, &tm_g, full8(s8), g * kBK8, (int)un.rlo);
             tma_load_2d(sA8 + s8 * kA8Bytes + kA8Bytes / 2, &tm_u, full8(s8), g * kBK8, (int)un.rhi);
           } else {
@@ -233,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t bd0 = sdesc_k_sw128(sB);
       for (int u = blockIdx.x; ok; u += stride, ++ui) {
         Unit un;
-        if (!get_unit(p, u, nblocks, un)) break;
+        if (!get_unit<DOWN>(p, u, nblocks, un)) break;
         const int NT = (un.count + 15) & ~15;
         const uint32_t idesc = idesc_f16(DT == LMOE_BF16 ? 1 : 0, kBM, NT);
         const int b = ui & 1;
@@ -271,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok; u += stride) {
         Unit un;
-        if (!get_unit(p, u, nblocks, un)) break;
+        if (!get_unit<DOWN>(p, u, nblocks, un)) break;
         // boxes of 32 route rows covering the tile; rows past the tile are read
         // (other tiles' rows, or zeros past the tensor) but never stored
         // a full-height tile takes one 128-row box (larger boxes stream faster),
@@ -318,13 +337,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int u = blockIdx.x; ok; u += stride) {
       Unit un;
-      if (!get_unit(p, u, nblocks, un)) break;
+      if (!get_unit<DOWN>(p, u, nblocks, un)) break;
       // TMEM lanes 0-63 take the up rows (shared-memory rows 64-127 of the stage),
       // lanes 64-127 the gate rows (rows 0-63): the epilogue's SiLU work then runs
       // in warps 14-15, away from the MMA issuer's SMSP
-      const int srow = r ^ 64;
-      const bool up = srow >= 64;
-      const int64_t grow = (up ? un.rhi : un.rlo) + (srow & 63);
+      // (down: TMEM lane r = row r of the unit)
+      const int srow = DOWN ? r : (r ^ 64);
+      const bool up = !DOWN && srow >= 64;
+      const int64_t grow = DOWN ? un.rlo + r : (up ? un.rhi : un.rlo) + (srow & 63);
       const int64_t rmax = un.shared ? p.rows_sh : p.rows_bank;
       const float* sp = (un.shared ? (up ? p.s_u : p.s_g) : p.s_bank) + grow * G;
       const bool valid = grow < rmax;
@@ -375,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int ui = 0, chunk = 0;
     for (int u = blockIdx.x;; u += stride, ++ui) {
       Unit un;
-      if (!get_unit(p, u, nblocks, un)) break;
+      if (!get_unit<DOWN>(p, u, nblocks, un)) break;
       const int b = ui & 1;
       if (q == 0 && lane == 0) *sHave = mbar_wait_drain(tfull(b), (ui >> 1) & 1, p.err) ? 1u : 0u;
       named_barrier(1, 128);
@@ -385,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int NT = (un.count + 15) & ~15;
       const int nch = (NT + 31) / 32;
       const uint32_t taddr = tmem + (uint32_t)(b * kAccCols) + ((uint32_t)(q * 32) << 16);
-      const int64_t col0 = (int64_t)un.nb * 64;
+      const int64_t col0 = (int64_t)un.nb * (DOWN ? 128 : 64);
       for (int c = 0; c < nch; ++c, ++chunk) {
         uint32_t acc[32];
         tmem_ld32(taddr + (uint32_t)(c * 32), acc);
@@ -396,6 +416,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(tempty(b));
         }
         if (!have) continue;
+        if constexpr (DOWN) {
+          // lane = output column col0 + row of the unit; per route j of the chunk
+          // v = round(round(acc) * w_route) (shared-expert rows: round(acc)), written
+          // transposed to a [32 routes][128 columns] 16-bit stage, then 16-byte row
+          // pieces: 128 threads = 32 routes x 4 pieces of 64 bytes
+          uint16_t* st = reinterpret_cast<uint16_t*>(ubase + (chunk & 1) * kDStageBytes);
+          const int ntok = min(32, un.count - c * 32);
+          // the chunk's 32 routing weights first, all loads before any store (the
+          // stores go through a generic pointer the loads could alias)
+          const float* wp = p.rweight + un.start + c * 32;
+          float w[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) w[jj] = (!un.shared && jj < ntok) ? __ldg(wp + jj) : 1.f;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            float v = A::round(__uint_as_float(acc[jj]));
+            if (!un.shared) v = __fmul_rn(v, w[jj]);
+            st[jj * 128 + row] = A::bits(v);
+          }
+          named_barrier(2, 128);
+          const int tok = row >> 2, piece = row & 3;
+          if (tok < ntok) {
+            typename A::T* dst = y + (int64_t)(un.start + c * 32 + tok) * p.ldy + col0 + piece * 32;
+            const uint32_t src = smem_u32(st) + (uint32_t)(tok * 256 + piece * 64);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) reinterpret_cast<uint4*>(dst)[k] = lds128(src + k * 16);
+          }
+          continue;
+        }
         uint8_t* ub = ubase + (chunk & 1) * kUBytes;
         uint8_t* hb = hbase + (chunk & 1) * kHBytes;
         const int hc = row & 63;  // hidden column of this lane
@@ -454,44 +503,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace ts
 
-int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st) {
-  if (L.mode != kSwiGLU || L.tiles == nullptr) return LMOE_ERR_INVALID;
-  if (L.K % kGroup || L.K <= 0 || L.inter % 64 || L.inter <= 0 || L.N != 2 * L.inter) return LMOE_ERR_INVALID;
+template <bool DOWN>
+static int launch_ts(const GemmLaunch& L, cudaStream_t st) {
   if ((L.ldy % 8) != 0 || (((uintptr_t)L.y) & 15)) return LMOE_ERR_INVALID;
   if (L.grid_tiles <= 0) return LMOE_OK;
   CUtensorMap tb, tg, tu, tx, tx128;
-  int rc = make_int8_pair_map(&tb, L.q_bank, L.experts, L.inter, L.K);
+  int rc = DOWN ? make_int8_map(&tb, L.q_bank, L.experts * L.N, L.K)
+                : make_int8_pair_map(&tb, L.q_bank, L.experts, L.inter, L.K);
   if (rc) return rc;
   tg = tb;
   tu = tb;
   if (L.q_lo && (rc = make_int8_map(&tg, L.q_lo, L.rows_lo, L.K))) return rc;
-  if (L.q_hi && (rc = make_int8_map(&tu, L.q_hi, L.rows_hi, L.K))) return rc;
+  if (!DOWN && L.q_hi && (rc = make_int8_map(&tu, L.q_hi, L.rows_hi, L.K))) return rc;
   if ((rc = make_act_map(&tx, L.x, L.x_rows, L.K, L.dtype, ts::kBoxRows))) return rc;
   if ((rc = make_act_map(&tx128, L.x, L.x_rows, L.K, L.dtype, kTileRoutes))) return rc;
   ts::Params p = {};
   p.K = L.K;
-  p.inter = L.inter;
+  p.inter = DOWN ? 0 : L.inter;
+  p.rows_e = L.N;
   p.tiles = L.tiles;
   p.hdr = L.hdr;
   p.rows_bank = L.experts * L.N;
   p.rows_sh = L.q_lo ? L.rows_lo : 0;
   p.s_bank = L.s_bank;
   p.s_g = L.s_lo;
-  p.s_u = L.s_hi;
+  p.s_u = DOWN ? nullptr : L.s_hi;
+  p.rweight = L.rweight;
   p.experts = (int)L.experts;
   p.y = L.y;
   p.ldy = L.ldy;
   p.err = L.err;
-  const int64_t units = (L.inter / 64) * L.grid_tiles;
+  const int64_t units = (DOWN ? L.N / 128 : L.inter / 64) * L.grid_tiles;
   const int64_t sms = sm_count();
   const int64_t ctas = units < sms ? units : sms;
   const size_t smem = ts::Smem::alloc;
   if (L.dtype == LMOE_BF16) {
-    auto k = ts::gate_up_ts_kernel<LMOE_BF16>;
+    auto k = ts::grouped_ts_kernel<LMOE_BF16, DOWN>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, tx128, p);
   } else if (L.dtype == LMOE_F16) {
-    auto k = ts::gate_up_ts_kernel<LMOE_F16>;
+    auto k = ts::grouped_ts_kernel<LMOE_F16, DOWN>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, tx128, p);
   } else {
@@ -499,6 +550,18 @@ int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st) {
   }
   LMOE_CUDA_CHECK(cudaGetLastError());
   return LMOE_OK;
+}
+
+int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st) {
+  if (L.mode != kSwiGLU || L.tiles == nullptr) return LMOE_ERR_INVALID;
+  if (L.K % kGroup || L.K <= 0 || L.inter % 64 || L.inter <= 0 || L.N != 2 * L.inter) return LMOE_ERR_INVALID;
+  return launch_ts<false>(L, st);
+}
+
+int launch_down_ts(const GemmLaunch& L, cudaStream_t st) {
+  if (L.mode != kWeighted || L.tiles == nullptr || L.rweight == nullptr) return LMOE_ERR_INVALID;
+  if (L.K % kGroup || L.K <= 0 || L.N % 128 || L.N <= 0) return LMOE_ERR_INVALID;
+  return launch_ts<true>(L, st);
 }
 
 }  // namespace lmoe

@@ -203,7 +203,7 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   d.ldy = hidden;
   d.rweight = (const float*)(meta + ML.off_rweight);
   d.mode = kWeighted;
-  if ((rc = launch_grouped_gemm(d, st))) return rc;
+  if ((rc = launch_down_ts(d, st))) return rc;
   if ((rc = mark(3))) return rc;
 
   const int32_t* ordered = (const int32_t*)(meta + ML.off_ordered);

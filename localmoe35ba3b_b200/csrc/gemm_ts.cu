@@ -61,7 +61,8 @@ constexpr int kTmemCols = 512;
 constexpr int kUPitch = 80;                       // bytes per up row in the exchange buffer
 constexpr int kUBytes = 64 * kUPitch;             // [64 rows][32 routes] 16-bit, padded rows
 constexpr int kHBytes = 32 * 64 * 2;              // [32 routes][64 columns] 16-bit
-constexpr int kDStageBytes = 32 * 128 * 2;        // down: [32 routes][128 columns] 16-bit
+constexpr int kDPitch = 136;                      // down stage row: 128 columns + 8 of padding (16-bit)
+constexpr int kDStageBytes = 32 * kDPitch * 2;    // down: [32 routes][136] 16-bit
 static_assert(2 * kDStageBytes <= 2 * kUBytes + 2 * kHBytes, "down staging fits the gate_up exchange area");
 static_assert(kACol0 + kNA * kASlotCols <= kTmemCols, "tensor memory budget");
 static_assert(kNS8 % 2 == 0, "two weight producers own alternate stages");
@@ -71,7 +72,8 @@ struct Smem {
   static constexpr int b = a8 + kNS8 * kA8Bytes;
   static constexpr int u = b + kNA * kBStage;
   static constexpr int h = u + 2 * kUBytes;
-  static constexpr int bars = h + 2 * kHBytes;
+  static constexpr int wts = h + 2 * kHBytes;   // down: the unit's 128 routing weights (fp32)
+  static constexpr int bars = wts + 128 * 4;
   // full8, empty8 (kNS8 each); ready, freed (kNA each); tfull, tempty (2 each); drain
   static constexpr int nbars = 2 * kNS8 + 2 * kNA + 4 + 1;
   static constexpr int misc = bars + nbars * 8;
@@ -397,9 +399,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       Unit un;
       if (!get_unit<DOWN>(p, u, nblocks, un)) break;
       const int b = ui & 1;
+      // down: this thread's route weight loads before the accumulator wait, so its
+      // latency overlaps it (shared-expert rows are not weighted)
+      float wrow = 1.f;
+      if (DOWN && !un.shared && row < un.count) wrow = __ldg(p.rweight + un.start + row);
       if (q == 0 && lane == 0) *sHave = mbar_wait_drain(tfull(b), (ui >> 1) & 1, p.err) ? 1u : 0u;
       named_barrier(1, 128);
       const bool have = *sHave != 0;
+      if (DOWN) reinterpret_cast<float*>(smem + Smem::wts)[row] = wrow;  // the previous unit's reads are done
       named_barrier(1, 128);
       tc_fence_after();
       const int NT = (un.count + 15) & ~15;
@@ -423,23 +430,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           // pieces: 128 threads = 32 routes x 4 pieces of 64 bytes
           uint16_t* st = reinterpret_cast<uint16_t*>(ubase + (chunk & 1) * kDStageBytes);
           const int ntok = min(32, un.count - c * 32);
-          // the chunk's 32 routing weights first, all loads before any store (the
-          // stores go through a generic pointer the loads could alias)
-          const float* wp = p.rweight + un.start + c * 32;
+          // the chunk's 32 routing weights from the unit's shared copy (broadcast reads)
           float w[32];
+          const uint32_t wsrc = smem_u32(smem + Smem::wts) + (uint32_t)(c * 32 * 4);
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) w[jj] = (!un.shared && jj < ntok) ? __ldg(wp + jj) : 1.f;
+          for (int jj = 0; jj < 32; jj += 4) {
+            const uint4 t = lds128(wsrc + jj * 4);
+            w[jj] = __uint_as_float(t.x);
+            w[jj + 1] = __uint_as_float(t.y);
+            w[jj + 2] = __uint_as_float(t.z);
+            w[jj + 3] = __uint_as_float(t.w);
+          }
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
             float v = A::round(__uint_as_float(acc[jj]));
             if (!un.shared) v = __fmul_rn(v, w[jj]);
-            st[jj * 128 + row] = A::bits(v);
+            st[jj * kDPitch + row] = A::bits(v);
           }
           named_barrier(2, 128);
           const int tok = row >> 2, piece = row & 3;
           if (tok < ntok) {
             typename A::T* dst = y + (int64_t)(un.start + c * 32 + tok) * p.ldy + col0 + piece * 32;
-            const uint32_t src = smem_u32(st) + (uint32_t)(tok * 256 + piece * 64);
+            const uint32_t src = smem_u32(st) + (uint32_t)(tok * kDPitch * 2 + piece * 64);
 #pragma unroll
             for (int k = 0; k < 4; ++k) reinterpret_cast<uint4*>(dst)[k] = lds128(src + k * 16);
           }

@@ -42,11 +42,10 @@ UNIT = 'tok/s'
 # (gate_up + SwiGLU), grouped_ts_kernel<.., true> (down + routing weight), moe_combine_kernel.
 LAUNCHES_PER_LAYER = 7
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
-# `ncu --set full` capture of layer 0 (`python bench.py --layers 2 --steps 1 --warmup 1
-# --no-cpu-baseline --no-extra`, -k "regex:gate_up_ts|grouped_gemm" -s 2 -c 2):
-# gate_up 404.6 MB + down 246.0 MB.  Per-layer work does not depend on the layer count, so
-# no scaling is applied.
-NCU_TRAFFIC_PER_LAYER = 650.6e6
+# `ncu --set full` capture (`python bench.py --layers 2 --steps 1 --warmup 1 --no-cpu-baseline
+# --no-extra`, -k regex:grouped_ts -s 2 -c 2): gate_up 404.2 MB + down 244.1 MB.  Per-layer
+# work does not depend on the layer count, so no scaling is applied.
+NCU_TRAFFIC_PER_LAYER = 648.3e6
 NCU_TRAFFIC_SOURCE = ('ncu dram__bytes_read.sum + dram__bytes_write.sum, gate_up + down launches of one '
                       '2048-token layer; bytes per layer like alg_bytes_per_layer')
 

@@ -1,43 +1,39 @@
 // One-token MoE decode: the reference's Int8Experts decode branch
 // (qwen35_deploy/operators/int8.py:158-187) with the gated HF shared expert
-// (modeling_qwen3_5_moe.py:781-790), as a short chain of launches on the
-// caller's stream with no host synchronisation (so it can be captured in a
-// CUDA graph):
-//   1. decode_table_kernel   ids -> the [top (+2), 5] descriptor table in
-//                            ascending expert order (int8.py:170-179), built on
-//                            the device instead of after an ids.cpu() sync
-//   2. grouped GEMV          gate_up of the routed experts (W8A8 or W8A16) and,
-//                            with a shared expert, its gate/up rows (W8A16, the
-//                            Int8Linear path)
-//   3. silu_rows_kernel      hidden = round(round(silu(g)) * u) (int8.py:182-184)
-//   4. grouped GEMV          down of the routed experts and of the shared expert
-//   5. reduce_combine_kernel the ordered combine of _ordered_reduce
-//                            (int8.py:240-250), then + round(sigmoid(x.gate) *
-//                            shared), then + residual
+// (modeling_qwen3_5_moe.py:781-790), in two launches on the caller's stream with
+// no host synchronisation (so it can be captured in a CUDA graph):
+//   1. decode_gate_up_kernel  one warp per (expert, hidden column): the gate and
+//      up rows' dot products (W8A8 or W8A16 routed, W8A16 shared), then
+//      hidden = round(round(silu(g)) * u) (int8.py:182-184)
+//   2. decode_down_kernel     one warp per output column: the down rows of every
+//      selected expert, folded as they finish into the ordered combine of
+//      _ordered_reduce (int8.py:240-250), then + round(sigmoid(x.gate) * shared),
+//      then + residual
+// Each block rebuilds the experts' ascending order from the router's ids
+// (int8.py:170-179's table, without the ids.cpu() sync and the upload), issues its
+// weight rows' loads, and only then (while they are in flight) quantises the
+// activation rows it reads for W8A8 (w8a8._quant).  The per-row arithmetic is the
+// grouped GEMV's (gemv.cuh), step for step.
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemv.cuh"
 
 namespace lmoe {
 
-int lmoe_grouped_launch(bool w8a8, const void* x, const int64_t* table, void* y, int64_t experts, int64_t n,
-                        int64_t k, int field, int shared, int dtype, cudaStream_t st);
-
 constexpr int kDecodeMaxTop = 32;
+constexpr int kDecWarps = 8;
+constexpr int kDecBatch = 8;  // down rows whose loads are in flight together
 
-// Table row r (r-th smallest expert id; ties by slot) = (gate_up.q, gate_up.scale,
-// down.q, down.scale, slot).  Shared expert rows follow: (gate.q, gate.s, down.q,
-// down.s, 0) and (up.q, up.s, 0, 0, 0).  An id outside [0, E) raises
-// LMOE_DEVERR_BAD_EXPERT and is replaced by expert 0, so no read leaves the bank.
-__global__ void decode_table_kernel(const int64_t* __restrict__ ids, int top, int64_t E, const int8_t* qg,
-                                    const float* sg, const int8_t* qd, const float* sd, int64_t H, int64_t I,
-                                    const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu,
-                                    const float* sh_su, const int8_t* sh_qd, const float* sh_sd,
-                                    int64_t* __restrict__ table, int* err) {
-  const int lane = threadIdx.x;
+// Warp 0: s_eid[r] = the r-th smallest expert id (ties by slot), s_slot[r] its slot.
+// An id outside [0, E) becomes expert 0 (no read leaves the bank) and, when
+// `report`, raises LMOE_DEVERR_BAD_EXPERT.
+__device__ __forceinline__ void expert_ranks(const int64_t* ids, int top, int64_t E, int64_t* s_eid, int* s_slot,
+                                             int* err, bool report) {
+  const int lane = lane_id();
   int64_t e = lane < top ? ids[lane] : INT64_MAX;
   if (lane < top && (e < 0 || e >= E)) {
-    raise_error(err, LMOE_DEVERR_BAD_EXPERT);
+    if (report) raise_error(err, LMOE_DEVERR_BAD_EXPERT);
     e = 0;
   }
   int rank = 0;
@@ -46,111 +42,198 @@ __global__ void decode_table_kernel(const int64_t* __restrict__ ids, int top, in
     rank += (o < e || (o == e && j < lane)) ? 1 : 0;
   }
   if (lane < top) {
-    int64_t* row = table + (int64_t)rank * 5;
-    row[0] = (int64_t)(qg + e * 2 * I * H);
-    row[1] = (int64_t)(sg + e * 2 * I * (H / kGroup));
-    row[2] = (int64_t)(qd + e * H * I);
-    row[3] = (int64_t)(sd + e * H * (I / kGroup));
-    row[4] = lane;
-  }
-  if (lane == 0 && sh_qg != nullptr) {
-    int64_t* row = table + (int64_t)top * 5;
-    row[0] = (int64_t)sh_qg;
-    row[1] = (int64_t)sh_sg;
-    row[2] = (int64_t)sh_qd;
-    row[3] = (int64_t)sh_sd;
-    row[4] = 0;
-    row[5] = (int64_t)sh_qu;
-    row[6] = (int64_t)sh_su;
-    row[7] = 0;
-    row[8] = 0;
-    row[9] = 0;
+    s_eid[rank] = e;
+    if (s_slot) s_slot[rank] = lane;
   }
 }
 
 __device__ __forceinline__ float silu_exact(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
-// rows 0..top-1: gate/up halves of the routed gate_up rows [top, 2I];
-// row top (when gsh != nullptr): the shared expert's gate and up rows [2, I]
-template <int DT>
-__global__ void silu_rows_kernel(const typename Act<DT>::T* __restrict__ gu, const typename Act<DT>::T* __restrict__ gsh,
-                                 int top, int64_t I, typename Act<DT>::T* __restrict__ h,
-                                 typename Act<DT>::T* __restrict__ hsh) {
+// rows 0..top-1: the routed experts in ascending id order; row top: the shared
+// expert (when sh_qg != nullptr).  hid [rows, I].
+template <int DT, bool W8A8>
+__global__ void __launch_bounds__(kDecWarps * 32)
+    decode_gate_up_kernel(const typename Act<DT>::T* __restrict__ x, const int64_t* __restrict__ ids, int top,
+                          int64_t E, const int8_t* __restrict__ qg, const float* __restrict__ sg, int64_t H, int64_t I,
+                          const int8_t* __restrict__ sh_qg, const float* __restrict__ sh_sg,
+                          const int8_t* __restrict__ sh_qu, const float* __restrict__ sh_su,
+                          typename Act<DT>::T* __restrict__ hid, int* err) {
   using A = Act<DT>;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int rows = top + (gsh != nullptr ? 1 : 0);
-  if (idx >= rows * I) return;
-  const int64_t r = idx / I, c = idx % I;
-  float g, u;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int64_t s_eid[kDecodeMaxTop];
+  const int lane = lane_id(), warp = warp_id();
+  const int groups = (int)(H / kGroup);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem);                   // [H]
+  float* xs = reinterpret_cast<float*>(smem + ((H + 15) & ~15));  // [H / 128]
+  if (warp == 0) expert_ranks(ids, top, E, s_eid, nullptr, err, blockIdx.x == 0);
+  __syncthreads();
+  // the rows' loads go out first; the activation quantisation overlaps them
+  const int rows = top + (sh_qg != nullptr ? 1 : 0);
+  const int64_t flat = (int64_t)blockIdx.x * kDecWarps + warp;
+  const bool live = flat < rows * I;
+  const int r = live ? (int)(flat / I) : 0;
+  const int64_t c = live ? flat % I : 0;
+  const int8_t *gq, *uq;
+  const float *gs, *us;
   if (r < top) {
-    g = A::to_f(gu[r * 2 * I + c]);
-    u = A::to_f(gu[r * 2 * I + I + c]);
+    const int64_t e = s_eid[r];
+    gq = qg + (e * 2 * I + c) * H;
+    uq = qg + (e * 2 * I + I + c) * H;
+    gs = sg + (e * 2 * I + c) * groups;
+    us = sg + (e * 2 * I + I + c) * groups;
   } else {
-    g = A::to_f(gsh[c]);
-    u = A::to_f(gsh[I + c]);
+    gq = sh_qg + c * H;
+    uq = sh_qu + c * H;
+    gs = sh_sg + c * groups;
+    us = sh_su + c * groups;
   }
-  const float v = __fmul_rn(A::round(silu_exact(g)), u);
-  if (r < top)
-    h[r * I + c] = A::from_f(v);
-  else
-    hsh[c] = A::from_f(v);
+  const int chunks = (int)(H / 16);
+  uint4 wg[kMaxChunksPerLane], wu[kMaxChunksPerLane];
+  if (live) {
+    row_load(gq, chunks, lane, wg);
+    row_load(uq, chunks, lane, wu);
+  }
+  if (W8A8)
+    for (int g = warp; g < groups; g += kDecWarps) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
+  __syncthreads();
+  if (!live) return;
+  float g, u;
+  if (W8A8 && r < top) {
+    g = row_dot_w8a8(wg, gs, xq, xs, chunks, lane);
+    u = row_dot_w8a8(wu, us, xq, xs, chunks, lane);
+  } else {  // W8A16 routed experts, and the shared expert (Int8Linear arithmetic)
+    g = row_dot_w16<DT>(wg, gs, x, chunks, lane);
+    u = row_dot_w16<DT>(wu, us, x, chunks, lane);
+  }
+  if (lane == 0) hid[(int64_t)r * I + c] = A::from_f(__fmul_rn(A::round(silu_exact(A::round(g))), A::round(u)));
 }
 
-constexpr int kCombineThreadsDec = 256;
-
-// out[c] = ordered combine of the routed rows (+ gated shared row) (+ residual)
-template <int DT>
-__global__ void __launch_bounds__(kCombineThreadsDec) reduce_combine_kernel(
-    const typename Act<DT>::T* __restrict__ v, const int64_t* __restrict__ table, const float* __restrict__ w, int top,
-    int64_t H, const typename Act<DT>::T* __restrict__ vsh, const typename Act<DT>::T* __restrict__ x,
-    const typename Act<DT>::T* __restrict__ gate_w, const typename Act<DT>::T* __restrict__ residual,
-    typename Act<DT>::T* __restrict__ out) {
+// out[n] = ordered combine over the routed experts of round(round(v) * w_slot),
+// + round(sig * round(v_shared)) with sig = round(sigmoid(round(x . gate))), + residual.
+template <int DT, bool W8A8, int MAXI>
+__global__ void __launch_bounds__(kDecWarps * 32)
+    decode_down_kernel(const typename Act<DT>::T* __restrict__ x, const float* __restrict__ weights,
+                       const int64_t* __restrict__ ids, int top, int64_t E, const int8_t* __restrict__ qd,
+                       const float* __restrict__ sd, int64_t H, int64_t I, const int8_t* __restrict__ sh_qd,
+                       const float* __restrict__ sh_sd, const typename Act<DT>::T* __restrict__ gate_w,
+                       const typename Act<DT>::T* __restrict__ residual, const typename Act<DT>::T* __restrict__ hid,
+                       typename Act<DT>::T* __restrict__ out, int* err) {
   using A = Act<DT>;
-  __shared__ float red[kCombineThreadsDec / 32];
-  float sig = 1.f;
-  if (vsh != nullptr && gate_w != nullptr) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int64_t s_eid[kDecodeMaxTop];
+  __shared__ int s_slot[kDecodeMaxTop];
+  __shared__ float red[kDecWarps];
+  const int lane = lane_id(), warp = warp_id();
+  const int gI = (int)(I / kGroup);
+  int8_t* hq = reinterpret_cast<int8_t*>(smem);                         // [top, I]
+  float* hs = reinterpret_cast<float*>(smem + ((top * I + 15) & ~15));  // [top, I / 128]
+  if (warp == 0) expert_ranks(ids, top, E, s_eid, s_slot, err, false);
+  __syncthreads();
+  // this column's weight rows go out first (the shared row and the first batch of
+  // routed rows); the hidden rows' quantisation and the gate's dot product overlap them
+  const int64_t n = (int64_t)blockIdx.x * kDecWarps + warp;
+  const bool live = n < H;
+  const int chunks = (int)(I / 16);
+  constexpr int BATCH = MAXI == 1 ? kDecBatch : 2;  // rows in flight together, within the register budget
+  const bool with_shared = sh_qd != nullptr;
+  const bool gated = with_shared && gate_w != nullptr;
+  uint4 wsh[MAXI];
+  uint4 w[BATCH][MAXI];
+  if (live) {
+    if (with_shared) row_load(sh_qd + n * I, chunks, lane, wsh);
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j)
+      if (j < top) row_load(qd + (s_eid[j] * H + n) * I, chunks, lane, w[j]);
+  }
+  if (W8A8)
+    for (int t = warp; t < top * gI; t += kDecWarps) {
+      const int r = t / gI, g = t % gI;
+      quant_group<DT>(hid + (int64_t)r * I + g * kGroup, hq + (int64_t)r * I + g * kGroup, hs + r * gI + g, lane);
+    }
+  if (gated) {
     float part = 0.f;
-    for (int64_t c = threadIdx.x; c < H; c += kCombineThreadsDec) part = fmaf(A::to_f(x[c]), A::to_f(gate_w[c]), part);
+    for (int64_t c = threadIdx.x; c < H; c += kDecWarps * 32) part = fmaf(A::to_f(x[c]), A::to_f(gate_w[c]), part);
 #pragma unroll
     for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (lane_id() == 0) red[warp_id()] = part;
-    __syncthreads();
+    if (lane == 0) red[warp] = part;
+  }
+  __syncthreads();
+  if (!live) return;
+  float sig = 1.f;
+  if (gated) {
     float tot = 0.f;
 #pragma unroll
-    for (int i = 0; i < kCombineThreadsDec / 32; ++i) tot += red[i];
-    const float logit = A::round(tot);
-    sig = A::round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-logit))));
+    for (int i = 0; i < kDecWarps; ++i) tot += red[i];
+    sig = A::round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-A::round(tot)))));
   }
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= H) return;
   float acc = 0.f;
-  for (int i = 0; i < top; ++i) {
-    const float wt = w[table[i * 5 + 4]];
-    acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::to_f(v[(int64_t)i * H + c]), wt))));
+  for (int r0 = 0; r0 < top; r0 += BATCH) {
+    if (r0 > 0) {
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j)
+        if (r0 + j < top) row_load(qd + (s_eid[r0 + j] * H + n) * I, chunks, lane, w[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const int r = r0 + j;
+      if (r >= top) break;
+      const float* srow = sd + (s_eid[r] * H + n) * gI;
+      const float v = W8A8 ? row_dot_w8a8(w[j], srow, hq + (int64_t)r * I, hs + r * gI, chunks, lane)
+                           : row_dot_w16<DT>(w[j], srow, hid + (int64_t)r * I, chunks, lane);
+      acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::round(v), weights[s_slot[r]]))));
+    }
   }
-  if (vsh != nullptr) {
-    const float s = A::to_f(vsh[c]);
-    acc = A::round(__fadd_rn(acc, gate_w != nullptr ? A::round(__fmul_rn(sig, s)) : s));
+  if (with_shared) {
+    const float s = A::round(row_dot_w16<DT>(wsh, sh_sd + n * gI, hid + (int64_t)top * I, chunks, lane));
+    acc = A::round(__fadd_rn(acc, gated ? A::round(__fmul_rn(sig, s)) : s));
   }
-  if (residual != nullptr) acc = A::round(__fadd_rn(A::to_f(residual[c]), acc));
-  out[c] = A::from_f(acc);
+  if (residual != nullptr) acc = A::round(__fadd_rn(A::to_f(residual[n]), acc));
+  if (lane == 0) out[n] = A::from_f(acc);
 }
 
 struct DecodeWs {
-  int64_t off_table, off_gu, off_gsh, off_h, off_hsh, off_v, off_vsh, bytes;
+  int64_t off_h, bytes;
   static int64_t align(int64_t v) { return (v + 255) & ~int64_t(255); }
   DecodeWs(int64_t top, int64_t H, int64_t I) {
-    int64_t o = 0;
-    off_table = o;  o = align(o + (top + 2) * 5 * 8);
-    off_gu = o;     o = align(o + top * 2 * I * 2);
-    off_gsh = o;    o = align(o + 2 * I * 2);
-    off_h = o;      o = align(o + top * I * 2);
-    off_hsh = o;    o = align(o + I * 2);
-    off_v = o;      o = align(o + top * H * 2);
-    off_vsh = o;    o = align(o + H * 2);
-    bytes = o;
+    (void)H;
+    off_h = 0;
+    bytes = align((top + 1) * I * 2);  // hidden rows: routed + shared
   }
 };
+
+template <int DT, bool W8A8>
+static int launch_decode(const void* x, const float* weights, const int64_t* ids, int top, const int8_t* qg,
+                         const float* sg, const int8_t* qd, const float* sd, int64_t E, int64_t H, int64_t I,
+                         const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu, const float* sh_su,
+                         const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w, const void* residual,
+                         void* out, void* hid, int* err, cudaStream_t st) {
+  using T = typename Act<DT>::T;
+  const int rows = top + (sh_qg != nullptr ? 1 : 0);
+  const unsigned b1 = (unsigned)((rows * I + kDecWarps - 1) / kDecWarps);
+  const size_t sm1 = (size_t)((H + 15) & ~15) + (size_t)(H / kGroup) * 4;
+  decode_gate_up_kernel<DT, W8A8><<<b1, kDecWarps * 32, sm1, st>>>(
+      (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid, err);
+  LMOE_CUDA_CHECK(cudaGetLastError());
+  const unsigned b2 = (unsigned)((H + kDecWarps - 1) / kDecWarps);
+  const size_t sm2 = W8A8 ? (size_t)((top * I + 15) & ~15) + (size_t)top * (I / kGroup) * 4 : 16;
+  if (sm2 > 227 * 1024) return LMOE_ERR_UNSUPPORTED;
+  if (sm2 > 48 * 1024) {
+    LMOE_CUDA_CHECK(cudaFuncSetAttribute(decode_down_kernel<DT, W8A8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sm2));
+    LMOE_CUDA_CHECK(cudaFuncSetAttribute(decode_down_kernel<DT, W8A8, kMaxChunksPerLane>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
+  }
+  if (I <= 512)
+    decode_down_kernel<DT, W8A8, 1><<<b2, kDecWarps * 32, sm2, st>>>(
+        (const T*)x, weights, ids, top, E, qd, sd, H, I, sh_qd, sh_sd, (const T*)sh_gate_w, (const T*)residual,
+        (const T*)hid, (T*)out, err);
+  else
+    decode_down_kernel<DT, W8A8, kMaxChunksPerLane><<<b2, kDecWarps * 32, sm2, st>>>(
+        (const T*)x, weights, ids, top, E, qd, sd, H, I, sh_qd, sh_sd, (const T*)sh_gate_w, (const T*)residual,
+        (const T*)hid, (T*)out, err);
+  LMOE_CUDA_CHECK(cudaGetLastError());
+  return LMOE_OK;
+}
 
 }  // namespace lmoe
 
@@ -171,47 +254,16 @@ extern "C" int lmoe_decode_moe(const void* x, const float* weights, const int64_
   if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_ERR_INVALID;
   const bool with_shared = sh_qg != nullptr;
   if (with_shared && (!sh_sg || !sh_qu || !sh_su || !sh_qd || !sh_sd)) return LMOE_ERR_INVALID;
-  const DecodeWs L(top, H, I);
-  uint8_t* base = (uint8_t*)ws;
-  int64_t* table = (int64_t*)(base + L.off_table);
-  void* gu = base + L.off_gu;
-  void* gsh = base + L.off_gsh;
-  void* h = base + L.off_h;
-  void* hsh = base + L.off_hsh;
-  void* v = base + L.off_v;
-  void* vsh = base + L.off_vsh;
+  if (H > 16 * 32 * kMaxChunksPerLane || I > 16 * 32 * kMaxChunksPerLane) return LMOE_ERR_UNSUPPORTED;
+  const int t = (int)top;
   cudaStream_t st = (cudaStream_t)stream;
-
-  decode_table_kernel<<<1, 32, 0, st>>>(ids, (int)top, E, qg, sg, qd, sd, H, I, sh_qg, sh_sg, sh_qu, sh_su, sh_qd,
-                                        sh_sd, table, err);
-  LMOE_CUDA_CHECK(cudaGetLastError());
-  int rc;
-  // gate_up: routed rows share x; the shared expert's gate/up rows use the W8A16 arithmetic
-  if ((rc = lmoe_grouped_launch(w8a8 != 0, x, table, gu, top, 2 * I, H, 0, 1, dtype, st))) return rc;
-  if (with_shared && (rc = lmoe_grouped_launch(false, x, table + top * 5, gsh, 2, I, H, 0, 1, dtype, st))) return rc;
-  const int64_t n_silu = (top + (with_shared ? 1 : 0)) * I;
-  const unsigned sb = (unsigned)((n_silu + 255) / 256);
   if (dtype == LMOE_BF16)
-    silu_rows_kernel<LMOE_BF16><<<sb, 256, 0, st>>>((const __nv_bfloat16*)gu,
-                                                    with_shared ? (const __nv_bfloat16*)gsh : nullptr, (int)top, I,
-                                                    (__nv_bfloat16*)h, (__nv_bfloat16*)hsh);
-  else
-    silu_rows_kernel<LMOE_F16><<<sb, 256, 0, st>>>((const __half*)gu, with_shared ? (const __half*)gsh : nullptr,
-                                                   (int)top, I, (__half*)h, (__half*)hsh);
-  LMOE_CUDA_CHECK(cudaGetLastError());
-  // down: routed row e reads hidden row e; the shared expert reads its own hidden row
-  if ((rc = lmoe_grouped_launch(w8a8 != 0, h, table, v, top, H, I, 2, 0, dtype, st))) return rc;
-  if (with_shared && (rc = lmoe_grouped_launch(false, hsh, table + top * 5, vsh, 1, H, I, 2, 1, dtype, st))) return rc;
-  const unsigned cb = (unsigned)((H + kCombineThreadsDec - 1) / kCombineThreadsDec);
-  if (dtype == LMOE_BF16)
-    reduce_combine_kernel<LMOE_BF16><<<cb, kCombineThreadsDec, 0, st>>>(
-        (const __nv_bfloat16*)v, table, weights, (int)top, H, with_shared ? (const __nv_bfloat16*)vsh : nullptr,
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)sh_gate_w, (const __nv_bfloat16*)residual,
-        (__nv_bfloat16*)out);
-  else
-    reduce_combine_kernel<LMOE_F16><<<cb, kCombineThreadsDec, 0, st>>>(
-        (const __half*)v, table, weights, (int)top, H, with_shared ? (const __half*)vsh : nullptr, (const __half*)x,
-        (const __half*)sh_gate_w, (const __half*)residual, (__half*)out);
-  LMOE_CUDA_CHECK(cudaGetLastError());
-  return LMOE_OK;
+    return w8a8 ? launch_decode<LMOE_BF16, true>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu, sh_su,
+                                                 sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st)
+                : launch_decode<LMOE_BF16, false>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu,
+                                                  sh_su, sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st);
+  return w8a8 ? launch_decode<LMOE_F16, true>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu, sh_su,
+                                              sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st)
+              : launch_decode<LMOE_F16, false>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu, sh_su,
+                                               sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st);
 }

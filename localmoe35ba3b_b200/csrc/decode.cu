@@ -24,6 +24,8 @@ namespace lmoe {
 constexpr int kDecodeMaxTop = 32;
 constexpr int kDecWarps = 8;
 constexpr int kDecBatch = 8;  // down rows whose loads are in flight together
+constexpr int kDecMaxGroups = 32;  // K <= 4096
+constexpr int kDecScPerLane = 4;   // down: prefetched scales per lane (rows x groups <= 128)
 
 // Warp 0: s_eid[r] = the r-th smallest expert id (ties by slot), s_slot[r] its slot.
 // An id outside [0, E) becomes expert 0 (no read leaves the bank) and, when
@@ -51,7 +53,7 @@ __device__ __forceinline__ float silu_exact(float g) { return __fdiv_rn(g, __fad
 
 // rows 0..top-1: the routed experts in ascending id order; row top: the shared
 // expert (when sh_qg != nullptr).  hid [rows, I].
-template <int DT, bool W8A8>
+template <int DT, bool W8A8, int MAXI>
 __global__ void __launch_bounds__(kDecWarps * 32)
     decode_gate_up_kernel(const typename Act<DT>::T* __restrict__ x, const int64_t* __restrict__ ids, int top,
                           int64_t E, const int8_t* __restrict__ qg, const float* __restrict__ sg, int64_t H, int64_t I,
@@ -61,6 +63,7 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   using A = Act<DT>;
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ int64_t s_eid[kDecodeMaxTop];
+  __shared__ float s_sc[kDecWarps * 2 * kDecMaxGroups];
   const int lane = lane_id(), warp = warp_id();
   const int groups = (int)(H / kGroup);
   int8_t* xq = reinterpret_cast<int8_t*>(smem);                   // [H]
@@ -88,22 +91,30 @@ __global__ void __launch_bounds__(kDecWarps * 32)
     us = sh_su + c * groups;
   }
   const int chunks = (int)(H / 16);
-  uint4 wg[kMaxChunksPerLane], wu[kMaxChunksPerLane];
+  uint4 wg[MAXI], wu[MAXI];  // MAXI = H / 512 chunks per lane: fewer registers, more resident warps
+  // the two rows' group scales travel with the weights (lane i < groups: gate scale i,
+  // groups <= i < 2 * groups: up scale i - groups), so the dots wait on no second load
+  float sc0 = 0.f, sc1 = 0.f;
   if (live) {
     row_load(gq, chunks, lane, wg);
     row_load(uq, chunks, lane, wu);
+    if (lane < 2 * groups) sc0 = lane < groups ? gs[lane] : us[lane - groups];
+    if (lane + 32 < 2 * groups) sc1 = lane + 32 < groups ? gs[lane + 32] : us[lane + 32 - groups];
   }
   if (W8A8)
     for (int g = warp; g < groups; g += kDecWarps) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
+  float* wsc = s_sc + warp * 2 * kDecMaxGroups;  // [gate groups][up groups]
+  if (lane < 2 * groups) wsc[lane] = sc0;
+  if (lane + 32 < 2 * groups) wsc[lane + 32] = sc1;
   __syncthreads();
   if (!live) return;
   float g, u;
   if (W8A8 && r < top) {
-    g = row_dot_w8a8(wg, gs, xq, xs, chunks, lane);
-    u = row_dot_w8a8(wu, us, xq, xs, chunks, lane);
+    g = row_dot_w8a8(wg, wsc, xq, xs, chunks, lane);
+    u = row_dot_w8a8(wu, wsc + groups, xq, xs, chunks, lane);
   } else {  // W8A16 routed experts, and the shared expert (Int8Linear arithmetic)
-    g = row_dot_w16<DT>(wg, gs, x, chunks, lane);
-    u = row_dot_w16<DT>(wu, us, x, chunks, lane);
+    g = row_dot_w16<DT>(wg, wsc, x, chunks, lane);
+    u = row_dot_w16<DT>(wu, wsc + groups, x, chunks, lane);
   }
   if (lane == 0) hid[(int64_t)r * I + c] = A::from_f(__fmul_rn(A::round(silu_exact(A::round(g))), A::round(u)));
 }
@@ -123,6 +134,7 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   __shared__ int64_t s_eid[kDecodeMaxTop];
   __shared__ int s_slot[kDecodeMaxTop];
   __shared__ float red[kDecWarps];
+  __shared__ float s_sc[kDecWarps * 32 * kDecScPerLane];
   const int lane = lane_id(), warp = warp_id();
   const int gI = (int)(I / kGroup);
   int8_t* hq = reinterpret_cast<int8_t*>(smem);                         // [top, I]
@@ -139,11 +151,27 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   const bool gated = with_shared && gate_w != nullptr;
   uint4 wsh[MAXI];
   uint4 w[BATCH][MAXI];
+  // every row's group scales travel with the first weights (entry i = row i / gI,
+  // group i % gI; the shared row last) into the warp's shared buffer, so the dots
+  // wait on no second load; too many to prefetch: the dots read them from memory
+  const int nsc = (top + (with_shared ? 1 : 0)) * gI;
+  const bool pre = nsc <= 32 * kDecScPerLane;
+  float scv[kDecScPerLane];
   if (live) {
     if (with_shared) row_load(sh_qd + n * I, chunks, lane, wsh);
 #pragma unroll
     for (int j = 0; j < BATCH; ++j)
       if (j < top) row_load(qd + (s_eid[j] * H + n) * I, chunks, lane, w[j]);
+    if (pre) {
+#pragma unroll
+      for (int k = 0; k < kDecScPerLane; ++k) {
+        const int i = lane + 32 * k;
+        if (i < nsc) {
+          const int r = i / gI, g = i % gI;
+          scv[k] = r < top ? sd[(s_eid[r] * H + n) * gI + g] : sh_sd[n * gI + g];
+        }
+      }
+    }
   }
   if (W8A8)
     for (int t = warp; t < top * gI; t += kDecWarps) {
@@ -156,6 +184,12 @@ __global__ void __launch_bounds__(kDecWarps * 32)
 #pragma unroll
     for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     if (lane == 0) red[warp] = part;
+  }
+  float* wsc = s_sc + warp * 32 * kDecScPerLane;
+  if (live && pre) {
+#pragma unroll
+    for (int k = 0; k < kDecScPerLane; ++k)
+      if (lane + 32 * k < nsc) wsc[lane + 32 * k] = scv[k];
   }
   __syncthreads();
   if (!live) return;
@@ -177,14 +211,15 @@ __global__ void __launch_bounds__(kDecWarps * 32)
     for (int j = 0; j < BATCH; ++j) {
       const int r = r0 + j;
       if (r >= top) break;
-      const float* srow = sd + (s_eid[r] * H + n) * gI;
+      const float* srow = pre ? wsc + r * gI : sd + (s_eid[r] * H + n) * gI;
       const float v = W8A8 ? row_dot_w8a8(w[j], srow, hq + (int64_t)r * I, hs + r * gI, chunks, lane)
                            : row_dot_w16<DT>(w[j], srow, hid + (int64_t)r * I, chunks, lane);
       acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::round(v), weights[s_slot[r]]))));
     }
   }
   if (with_shared) {
-    const float s = A::round(row_dot_w16<DT>(wsh, sh_sd + n * gI, hid + (int64_t)top * I, chunks, lane));
+    const float s = A::round(row_dot_w16<DT>(wsh, pre ? wsc + top * gI : sh_sd + n * gI, hid + (int64_t)top * I,
+                                             chunks, lane));
     acc = A::round(__fadd_rn(acc, gated ? A::round(__fmul_rn(sig, s)) : s));
   }
   if (residual != nullptr) acc = A::round(__fadd_rn(A::to_f(residual[n]), acc));
@@ -211,8 +246,12 @@ static int launch_decode(const void* x, const float* weights, const int64_t* ids
   const int rows = top + (sh_qg != nullptr ? 1 : 0);
   const unsigned b1 = (unsigned)((rows * I + kDecWarps - 1) / kDecWarps);
   const size_t sm1 = (size_t)((H + 15) & ~15) + (size_t)(H / kGroup) * 4;
-  decode_gate_up_kernel<DT, W8A8><<<b1, kDecWarps * 32, sm1, st>>>(
-      (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid, err);
+  if (H <= 2048)
+    decode_gate_up_kernel<DT, W8A8, 4><<<b1, kDecWarps * 32, sm1, st>>>(
+        (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid, err);
+  else
+    decode_gate_up_kernel<DT, W8A8, kMaxChunksPerLane><<<b1, kDecWarps * 32, sm1, st>>>(
+        (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid, err);
   LMOE_CUDA_CHECK(cudaGetLastError());
   const unsigned b2 = (unsigned)((H + kDecWarps - 1) / kDecWarps);
   const size_t sm2 = W8A8 ? (size_t)((top * I + 15) & ~15) + (size_t)top * (I / kGroup) * 4 : 16;

@@ -56,7 +56,8 @@ __device__ __forceinline__ void row_load(const int8_t* wrow, int chunks, int lan
 
 // W8A8 (w8a8._linear, operators/w8a8.py:25-41): exact int32 dot per 128-group, then
 // acc = acc + (float(dot) * xs[g]) * ws[g] in group order.  xq / xs: the quantised
-// activation row and its group scales.  Every lane returns acc.
+// activation row and its group scales; srow: the weight row's scales (global or
+// shared memory).  Every lane returns acc.
 template <int MAXI>
 __device__ __forceinline__ float row_dot_w8a8(const uint4 (&w)[MAXI], const float* srow, const int8_t* xq,
                                               const float* xs, int chunks, int lane) {
@@ -79,7 +80,7 @@ __device__ __forceinline__ float row_dot_w8a8(const uint4 (&w)[MAXI], const floa
     d += __shfl_xor_sync(0xffffffffu, d, 4);
     const int g = c >> 3;  // group of this lane's chunk
     float t = 0.f;
-    if (c < chunks) t = __fmul_rn(__fmul_rn((float)d, xs[g]), __ldg(srow + g));
+    if (c < chunks) t = __fmul_rn(__fmul_rn((float)d, xs[g]), srow[g]);
     // lanes 0, 8, 16, 24 hold groups 4i .. 4i+3; add them in order
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -103,7 +104,7 @@ __device__ __forceinline__ float row_dot_w16(const uint4 (&w)[MAXI], const float
     if (i >= iters) break;
     const int c = lane + 32 * i;
     if (c >= chunks) continue;
-    const float sc = __ldg(srow + (c >> 3));
+    const float sc = srow[c >> 3];
     const uint4 xa = *reinterpret_cast<const uint4*>(xv + c * 16);
     const uint4 xb = *reinterpret_cast<const uint4*>(xv + c * 16 + 8);
     const uint32_t wv[4] = {w[i].x, w[i].y, w[i].z, w[i].w};

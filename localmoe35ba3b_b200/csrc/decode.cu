@@ -51,6 +51,13 @@ __device__ __forceinline__ void expert_ranks(const int64_t* ids, int top, int64_
 
 __device__ __forceinline__ float silu_exact(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
+// Programmatic dependent launch: the down kernel is launched so that it may start
+// while the gate_up kernel is still running; it waits here (griddepcontrol.wait, a
+// no-op without such a launch) before its first read of the gate_up kernel's output.
+// The gate_up kernel lets it launch once its own loads are out.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // rows 0..top-1: the routed experts in ascending id order; row top: the shared
 // expert (when sh_qg != nullptr).  hid [rows, I].
 template <int DT, bool W8A8, int MAXI>
@@ -101,6 +108,7 @@ __global__ void __launch_bounds__(kDecWarps * 32)
     if (lane < 2 * groups) sc0 = lane < groups ? gs[lane] : us[lane - groups];
     if (lane + 32 < 2 * groups) sc1 = lane + 32 < groups ? gs[lane + 32] : us[lane + 32 - groups];
   }
+  grid_dep_launch();
   if (W8A8)
     for (int g = warp; g < groups; g += kDecWarps) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
   float* wsc = s_sc + warp * 2 * kDecMaxGroups;  // [gate groups][up groups]
@@ -173,11 +181,6 @@ __global__ void __launch_bounds__(kDecWarps * 32)
       }
     }
   }
-  if (W8A8)
-    for (int t = warp; t < top * gI; t += kDecWarps) {
-      const int r = t / gI, g = t % gI;
-      quant_group<DT>(hid + (int64_t)r * I + g * kGroup, hq + (int64_t)r * I + g * kGroup, hs + r * gI + g, lane);
-    }
   if (gated) {
     float part = 0.f;
     for (int64_t c = threadIdx.x; c < H; c += kDecWarps * 32) part = fmaf(A::to_f(x[c]), A::to_f(gate_w[c]), part);
@@ -185,6 +188,14 @@ __global__ void __launch_bounds__(kDecWarps * 32)
     for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     if (lane == 0) red[warp] = part;
   }
+  // everything above reads only what existed before the gate_up kernel started; the
+  // hidden rows below are its output
+  grid_dep_wait();
+  if (W8A8)
+    for (int t = warp; t < top * gI; t += kDecWarps) {
+      const int r = t / gI, g = t % gI;
+      quant_group<DT>(hid + (int64_t)r * I + g * kGroup, hq + (int64_t)r * I + g * kGroup, hs + r * gI + g, lane);
+    }
   float* wsc = s_sc + warp * 32 * kDecScPerLane;
   if (live && pre) {
 #pragma unroll
@@ -262,14 +273,24 @@ static int launch_decode(const void* x, const float* weights, const int64_t* ids
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(decode_down_kernel<DT, W8A8, kMaxChunksPerLane>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
   }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(b2);
+  cfg.blockDim = dim3(kDecWarps * 32);
+  cfg.dynamicSmemBytes = sm2;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (I <= 512)
-    decode_down_kernel<DT, W8A8, 1><<<b2, kDecWarps * 32, sm2, st>>>(
-        (const T*)x, weights, ids, top, E, qd, sd, H, I, sh_qd, sh_sd, (const T*)sh_gate_w, (const T*)residual,
-        (const T*)hid, (T*)out, err);
+    LMOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_down_kernel<DT, W8A8, 1>, (const T*)x, weights, ids, top, E, qd,
+                                       sd, H, I, sh_qd, sh_sd, (const T*)sh_gate_w, (const T*)residual,
+                                       (const T*)hid, (T*)out, err));
   else
-    decode_down_kernel<DT, W8A8, kMaxChunksPerLane><<<b2, kDecWarps * 32, sm2, st>>>(
-        (const T*)x, weights, ids, top, E, qd, sd, H, I, sh_qd, sh_sd, (const T*)sh_gate_w, (const T*)residual,
-        (const T*)hid, (T*)out, err);
+    LMOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_down_kernel<DT, W8A8, kMaxChunksPerLane>, (const T*)x, weights,
+                                       ids, top, E, qd, sd, H, I, sh_qd, sh_sd, (const T*)sh_gate_w,
+                                       (const T*)residual, (const T*)hid, (T*)out, err));
   LMOE_CUDA_CHECK(cudaGetLastError());
   return LMOE_OK;
 }

@@ -191,6 +191,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with cudaLaunchAttributeProgrammaticStreamSerialization may start
+// before the previous kernel in its stream has finished: grid_dep_wait blocks until
+// that kernel has completed and its writes are visible (a no-op for a normal
+// launch); grid_dep_launch lets this kernel's own dependent start early.  Only reads
+// of the previous kernel's output must come after grid_dep_wait: data written by
+// earlier work is complete, since the previous kernel itself started after it.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA / cp.async
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
   asm volatile(

@@ -52,11 +52,9 @@ __device__ __forceinline__ void expert_ranks(const int64_t* ids, int top, int64_
 __device__ __forceinline__ float silu_exact(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
 // Programmatic dependent launch: the down kernel is launched so that it may start
-// while the gate_up kernel is still running; it waits here (griddepcontrol.wait, a
-// no-op without such a launch) before its first read of the gate_up kernel's output.
-// The gate_up kernel lets it launch once its own loads are out.
-__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// while the gate_up kernel is still running; it waits (grid_dep_wait) before its first
+// read of the gate_up kernel's output, and the gate_up kernel lets it launch once its
+// own loads are out (grid_dep_launch).
 
 // rows 0..top-1: the routed experts in ascending id order; row top: the shared
 // expert (when sh_qg != nullptr).  hid [rows, I].

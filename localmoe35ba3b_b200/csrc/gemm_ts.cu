@@ -203,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   tc_fence_after();
+  grid_dep_launch();  // the next kernel's CTAs may take each SM as this kernel's CTA leaves it
   const uint32_t tmem = *sTmem;
   const int stride = gridDim.x;
 
@@ -287,6 +288,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 2) {
     // ------------------------------------------------------------ activation TMA
+    // the activation rows are the previous kernel's output (permute_rows_kernel for
+    // gate_up, the gate_up kernel for down): this kernel may be launched before that
+    // kernel ends, and only this role reads its output
+    grid_dep_wait();
     if (lane == 0) {
       int ib = 0;
       bool ok = true;
@@ -549,14 +554,26 @@ static int launch_ts(const GemmLaunch& L, cudaStream_t st) {
   const int64_t sms = sm_count();
   const int64_t ctas = units < sms ? units : sms;
   const size_t smem = ts::Smem::alloc;
+  // programmatic dependent launch: CTAs may start on SMs that the previous kernel's
+  // CTAs have left (their weight streams start at once; the activation producer waits)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(ts::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (L.dtype == LMOE_BF16) {
     auto k = ts::grouped_ts_kernel<LMOE_BF16, DOWN>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, tx128, p);
+    LMOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, tb, tg, tu, tx, tx128, p));
   } else if (L.dtype == LMOE_F16) {
     auto k = ts::grouped_ts_kernel<LMOE_F16, DOWN>;
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<(unsigned)ctas, ts::kThreads, smem, st>>>(tb, tg, tu, tx, tx128, p);
+    LMOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, tb, tg, tu, tx, tx128, p));
   } else {
     return LMOE_ERR_INVALID;
   }

@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_rows_kernel(const uin
                                                                       const int32_t* __restrict__ pos,
                                                                       uint4* __restrict__ out, int64_t rows,
                                                                       int64_t vec_per_row) {
+  grid_dep_launch();  // the gate_up kernel may take SMs as this kernel's blocks leave them
   const int64_t r = (int64_t)blockIdx.x * kPermWarps + warp_id();
   if (r >= rows) return;
   const int64_t src = pos[r];

@@ -50,6 +50,10 @@ __global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(
     const float logit = A::round(tot);
     sig = A::round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-logit))));
   }
+  // the shared gate above reads only the block's input; the rows below are the down
+  // kernel's output
+  grid_dep_wait();
+  grid_dep_launch();
   for (int64_t c = threadIdx.x * 8; c < H; c += kCombineThreads * 8) {
     float acc[8];
 #pragma unroll
@@ -208,14 +212,15 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
 
   const int32_t* ordered = (const int32_t*)(meta + ML.off_ordered);
   if (dtype == LMOE_BF16)
-    moe_combine_kernel<LMOE_BF16><<<(unsigned)tokens, kCombineThreads, 0, st>>>(
-        (const __nv_bfloat16*)dn, ordered, (int)top, hidden, R, (const __nv_bfloat16*)x,
-        (const __nv_bfloat16*)sh_gate_w, with_shared ? 1 : 0, (const __nv_bfloat16*)residual, (__nv_bfloat16*)out);
+    LMOE_CUDA_CHECK(launch_pdl(moe_combine_kernel<LMOE_BF16>, dim3((unsigned)tokens), dim3(kCombineThreads), 0, st,
+                               (const __nv_bfloat16*)dn, ordered, (int)top, hidden, R, (const __nv_bfloat16*)x,
+                               (const __nv_bfloat16*)sh_gate_w, with_shared ? 1 : 0,
+                               (const __nv_bfloat16*)residual, (__nv_bfloat16*)out));
   else
-    moe_combine_kernel<LMOE_F16><<<(unsigned)tokens, kCombineThreads, 0, st>>>(
-        (const __half*)dn, ordered, (int)top, hidden, R, (const __half*)x, (const __half*)sh_gate_w,
-        with_shared ? 1 : 0, (const __half*)residual, (__half*)out);
-  LMOE_CUDA_CHECK(cudaGetLastError());
+    LMOE_CUDA_CHECK(launch_pdl(moe_combine_kernel<LMOE_F16>, dim3((unsigned)tokens), dim3(kCombineThreads), 0, st,
+                               (const __half*)dn, ordered, (int)top, hidden, R, (const __half*)x,
+                               (const __half*)sh_gate_w, with_shared ? 1 : 0, (const __half*)residual,
+                               (__half*)out));
   return mark(4);
 }
 

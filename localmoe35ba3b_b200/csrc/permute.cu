@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_rows_kernel(const uin
                                                                       const int32_t* __restrict__ pos,
                                                                       uint4* __restrict__ out, int64_t rows,
                                                                       int64_t vec_per_row) {
+  grid_dep_wait();    // pos is the previous kernel's output
   grid_dep_launch();  // the gate_up kernel may take SMs as this kernel's blocks leave them
   const int64_t r = (int64_t)blockIdx.x * kPermWarps + warp_id();
   if (r >= rows) return;
@@ -29,8 +30,8 @@ int launch_permute_rows(const void* x, const int32_t* pos, void* out, int64_t ro
   if (rows <= 0) return LMOE_OK;
   if (k % 8 || ((uintptr_t)x & 15) || ((uintptr_t)out & 15)) return LMOE_ERR_INVALID;
   const unsigned blocks = (unsigned)((rows + kPermWarps - 1) / kPermWarps);
-  permute_rows_kernel<<<blocks, kPermWarps * 32, 0, st>>>((const uint4*)x, pos, (uint4*)out, rows, k / 8);
-  LMOE_CUDA_CHECK(cudaGetLastError());
+  LMOE_CUDA_CHECK(launch_pdl(permute_rows_kernel, dim3(blocks), dim3(kPermWarps * 32), 0, st, (const uint4*)x, pos,
+                             (uint4*)out, rows, k / 8));
   return LMOE_OK;
 }
 

@@ -276,6 +276,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
 __global__ void __launch_bounds__(kMetaChunk) meta_count_kernel(const int64_t* __restrict__ ids, int R, int E,
                                                                 int32_t* __restrict__ cc, int* err) {
   extern __shared__ int h[];  // [E + 1]
+  grid_dep_wait();  // ids may be the previous kernel's output (the router)
+  grid_dep_launch();
   for (int i = threadIdx.x; i <= E; i += kMetaChunk) h[i] = 0;
   __syncthreads();
   const int f = blockIdx.x * kMetaChunk + threadIdx.x;
@@ -288,6 +290,8 @@ __global__ void __launch_bounds__(kRouteThreads) meta_scan_kernel(RouteArgs a, i
                                                                   int nchunks) {
   __shared__ int warp_tot[32];
   __shared__ int s_first[1025];
+  grid_dep_wait();  // the chunk counts of meta_count_kernel
+  grid_dep_launch();
   const int E = a.E, R = a.T * a.top;
   const int e = threadIdx.x;
   int count = 0;
@@ -318,6 +322,8 @@ __global__ void __launch_bounds__(kRouteThreads) meta_scan_kernel(RouteArgs a, i
 
 __global__ void __launch_bounds__(kMetaChunk) meta_place_kernel(RouteArgs a, const int32_t* __restrict__ cc) {
   extern __shared__ int wc[];  // [kMetaChunk / 32][E + 1] per-warp counts, then first slots
+  grid_dep_wait();  // the offsets of meta_scan_kernel
+  grid_dep_launch();
   constexpr int kW = kMetaChunk / 32;
   const int E = a.E, R = a.T * a.top;
   const int lane = lane_id(), warp = warp_id();
@@ -436,16 +442,14 @@ int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t token
   const size_t hsm = (size_t)(experts + 1) * sizeof(int);
   const size_t wsm = (size_t)(kMetaChunk / 32) * (experts + 1) * sizeof(int);
   if (nchunks > 0) {
-    meta_count_kernel<<<nchunks, kMetaChunk, hsm, st>>>(ids, R, (int)experts, cc, err);
-    LMOE_CUDA_CHECK(cudaGetLastError());
+    LMOE_CUDA_CHECK(launch_pdl(meta_count_kernel, dim3(nchunks), dim3(kMetaChunk), hsm, st, ids, R, (int)experts, cc,
+                               err));
   }
-  meta_scan_kernel<<<1, kRouteThreads, 0, st>>>(a, cc, nchunks);
-  LMOE_CUDA_CHECK(cudaGetLastError());
+  LMOE_CUDA_CHECK(launch_pdl(meta_scan_kernel, dim3(1), dim3(kRouteThreads), 0, st, a, cc, nchunks));
   if (nchunks > 0) {
     if (wsm > 48 * 1024)
       LMOE_CUDA_CHECK(cudaFuncSetAttribute(meta_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsm));
-    meta_place_kernel<<<nchunks, kMetaChunk, wsm, st>>>(a, cc);
-    LMOE_CUDA_CHECK(cudaGetLastError());
+    LMOE_CUDA_CHECK(launch_pdl(meta_place_kernel, dim3(nchunks), dim3(kMetaChunk), wsm, st, a, cc));
   }
   return LMOE_OK;
 }

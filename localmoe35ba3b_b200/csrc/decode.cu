@@ -73,6 +73,9 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   const int groups = (int)(H / kGroup);
   int8_t* xq = reinterpret_cast<int8_t*>(smem);                   // [H]
   float* xs = reinterpret_cast<float*>(smem + ((H + 15) & ~15));  // [H / 128]
+  // launched so that it may start before the previous kernel ends: the ids, x and the
+  // hidden buffer (which the previous call's down kernel reads) all wait for it
+  grid_dep_wait();
   if (warp == 0) expert_ranks(ids, top, E, s_eid, nullptr, err, blockIdx.x == 0);
   __syncthreads();
   // the rows' loads go out first; the activation quantisation overlaps them
@@ -189,6 +192,7 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   // everything above reads only what existed before the gate_up kernel started; the
   // hidden rows below are its output
   grid_dep_wait();
+  grid_dep_launch();  // the next call's gate_up kernel may launch (it waits on this one at its start)
   if (W8A8)
     for (int t = warp; t < top * gI; t += kDecWarps) {
       const int r = t / gI, g = t % gI;
@@ -256,11 +260,12 @@ static int launch_decode(const void* x, const float* weights, const int64_t* ids
   const unsigned b1 = (unsigned)((rows * I + kDecWarps - 1) / kDecWarps);
   const size_t sm1 = (size_t)((H + 15) & ~15) + (size_t)(H / kGroup) * 4;
   if (H <= 2048)
-    decode_gate_up_kernel<DT, W8A8, 4><<<b1, kDecWarps * 32, sm1, st>>>(
-        (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid, err);
+    LMOE_CUDA_CHECK(launch_pdl(decode_gate_up_kernel<DT, W8A8, 4>, dim3(b1), dim3(kDecWarps * 32), sm1, st,
+                               (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid, err));
   else
-    decode_gate_up_kernel<DT, W8A8, kMaxChunksPerLane><<<b1, kDecWarps * 32, sm1, st>>>(
-        (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid, err);
+    LMOE_CUDA_CHECK(launch_pdl(decode_gate_up_kernel<DT, W8A8, kMaxChunksPerLane>, dim3(b1), dim3(kDecWarps * 32),
+                               sm1, st, (const T*)x, ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, (T*)hid,
+                               err));
   LMOE_CUDA_CHECK(cudaGetLastError());
   const unsigned b2 = (unsigned)((H + kDecWarps - 1) / kDecWarps);
   const size_t sm2 = W8A8 ? (size_t)((top * I + 15) & ~15) + (size_t)top * (I / kGroup) * 4 : 16;

@@ -1,4 +1,4 @@
-"""Expert parallelism (runtime/ep.py) on CPU ranks over gloo, world size 2.
+"""Expert parallelism (runtime/ep.py) on CPU ranks over gloo, world sizes 2 and 4.
 
 The orchestration -- send plan, all-to-all of counts, rows and route lists,
 route expansion, per-rank ordered pre-reduction, reverse all-to-all, per-token
@@ -18,10 +18,10 @@ import torch.multiprocessing as mp
 
 from oracle import oracle as O
 
-E, H, I, TOP, T, WORLD = 16, 256, 128, 4, 12, 2
+E, H, I, TOP, T = 16, 256, 128, 4, 12
 
 
-def _case():
+def _case(world):
     r = np.random.default_rng(321)
     qg, sg = O.quantize_weight(r.standard_normal((E, 2 * I, H)).astype(np.float32) * 0.02)
     qd, sd = O.quantize_weight(r.standard_normal((E, H, I)).astype(np.float32) * 0.02)
@@ -29,7 +29,7 @@ def _case():
               for s in ((I, H), (I, H), (H, I))]
     gate = O.round_to(r.standard_normal((1, H)).astype(np.float32) * 0.02, 'bf16')
     xs, ids, ws, res = [], [], [], []
-    for _ in range(WORLD):
+    for _ in range(world):
         logits = r.standard_normal((T, E)).astype(np.float32) + O.zipf_bias(E, r)[None]
         i, w = O.route(logits, TOP)
         xs.append(O.round_to(r.standard_normal((T, H)).astype(np.float32), 'bf16'))
@@ -43,14 +43,14 @@ def _bf(a):
     return torch.from_numpy(np.asarray(a, dtype=np.float32)).to(torch.bfloat16)
 
 
-def _worker(rank, port, out_dir):
+def _worker(rank, world, port, out_dir):
     os.environ['MASTER_ADDR'] = '127.0.0.1'
     os.environ['MASTER_PORT'] = str(port)
-    dist.init_process_group('gloo', rank=rank, world_size=WORLD)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
     try:
         from localmoe35ba3b_b200.runtime import ep
-        bank, shared, gate, xs, ids, ws, res = _case()
-        e_loc = E // WORLD
+        bank, shared, gate, xs, ids, ws, res = _case(world)
+        e_loc = E // world
         lb = [b[rank * e_loc:(rank + 1) * e_loc] for b in bank]
 
         def local_moe(x_rows, w, i):
@@ -69,13 +69,13 @@ def _worker(rank, port, out_dir):
         dist.destroy_process_group()
 
 
-def _ep_sequence(x, w, ids, bank, shared, gate, res):
+def _ep_sequence(x, w, ids, bank, shared, gate, res, world):
     """The expert-parallel rounding sequence restated on one process."""
-    e_loc = E // WORLD
+    e_loc = E // world
     out = np.zeros((T, H), dtype=np.float32)
     for t in range(T):
         acc = np.zeros(H, dtype=np.float32)
-        for g in range(WORLD):
+        for g in range(world):
             sel = [k for k in range(TOP) if ids[t, k] // e_loc == g]
             if not sel:
                 continue
@@ -110,14 +110,31 @@ def test_plan_groups_rows_by_rank():
     assert rw[0].tolist() == pytest.approx([.4, 0, .2, 0])
 
 
-def test_expert_parallel_two_ranks_matches_oracle(tmp_path):
+def test_plan_four_ranks():
+    from localmoe35ba3b_b200.runtime import ep
+    ids = torch.tensor([[0, 9, 3, 12], [15, 14, 13, 12], [1, 2, 3, 4]])
+    w = torch.tensor([[.4, .3, .2, .1], [.25, .25, .25, .25], [.1, .2, .3, .4]])
+    tok, counts, rid, rw = ep.plan(ids, w, 16, 4)
+    # 4 experts per rank: token 0 -> ranks {0, 2, 3}, token 1 -> {3}, token 2 -> {0, 1}
+    assert counts.tolist() == [2, 1, 1, 2]
+    assert tok.tolist() == [0, 2, 2, 0, 0, 1]
+    assert rid.tolist() == [[0, -1, 3, -1], [1, 2, 3, -1], [-1, -1, -1, 0],
+                            [-1, 1, -1, -1], [-1, -1, -1, 0], [3, 2, 1, 0]]
+    assert rw[1].tolist() == pytest.approx([.1, .2, .3, 0])
+    assert rw[5].tolist() == pytest.approx([.25] * 4)
+    with pytest.raises(ValueError):
+        ep.plan(ids, w, 16, 3)
+
+
+@pytest.mark.parametrize('world', [2, 4])
+def test_expert_parallel_matches_oracle(tmp_path, world):
     port = _free_port()
-    mp.start_processes(_worker, args=(port, str(tmp_path)), nprocs=WORLD, join=True, start_method='spawn')
-    bank, shared, gate, xs, ids, ws, res = _case()
-    for rank in range(WORLD):
+    mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True, start_method='spawn')
+    bank, shared, gate, xs, ids, ws, res = _case(world)
+    for rank in range(world):
         got = np.load(tmp_path / f'ep{rank}.npy')
         single = O.round_to(res[rank] + O.moe_block(xs[rank], ws[rank], ids[rank], bank, shared, gate, 'bf16'), 'bf16')
         err = np.abs(got - single).max() / np.abs(single).max()
         assert err < 1e-2, err
-        exact = _ep_sequence(xs[rank], ws[rank], ids[rank], bank, shared, gate, res[rank])
+        exact = _ep_sequence(xs[rank], ws[rank], ids[rank], bank, shared, gate, res[rank], world)
         assert np.array_equal(got, exact)

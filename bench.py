@@ -63,6 +63,9 @@ def parse():
     ap.add_argument('--no-extra', action='store_true', help='skip the decode (C3) and dense-sweep (C4) legs')
     ap.add_argument('--ep', action='store_true', help='with --gpus N > 1: expert parallelism (experts sharded, '
                                                       'all-to-all) instead of N data-parallel replicas')
+    ap.add_argument('--ep-wire', choices=('bf16', 'int8'), default='bf16',
+                    help='with --ep: format of the dispatched hidden rows (int8 = W8A8 activation '
+                         'quantisation, 2112 instead of 4096 bytes per row)')
     return ap.parse_args()
 
 
@@ -202,7 +205,7 @@ def run_ours(a, rank, world, local):
         if use_ep:
             # expert parallelism: this rank's experts serve every rank's routes to them
             for l in range(a.layers):
-                x = ep.moe_forward(x, wts[l], ids[l], EXPERTS, fns[l][0], fns[l][1], residual=x)
+                x = ep.moe_forward(x, wts[l], ids[l], EXPERTS, fns[l][0], fns[l][1], residual=x, wire=a.ep_wire)
             return x
         for l, (bank, shared, gate) in enumerate(layers):
             x = gpu_routes.moe_block(x, wts[l], ids[l], bank, shared=shared, shared_gate_weight=gate,
@@ -319,13 +322,15 @@ def run_ours(a, rank, world, local):
         'config': {'workload': f'prefill chunk: {a.tokens} tokens x {a.layers} layers, 256 experts top-8 + shared, '
                                'hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, Zipf(1.1) routing',
                    'tokens_per_gpu': a.tokens, 'layers': a.layers,
-                   'parallelism': (f'ep{world} (experts {e_loc} per GPU, all-to-all over NCCL)' if use_ep
+                   'parallelism': (f'ep{world} (experts {e_loc} per GPU, all-to-all over NCCL, '
+                                   f'{a.ep_wire} dispatch rows)' if use_ep
                                    else (f'dp{world} replicas (full weights per GPU; --ep for expert parallelism)'
                                          if world > 1 else 'single')),
                    'active_experts_mean': round(float(np.mean(active)), 1),
                    'l2': 'inputs larger than L2 (33.2 GB of resident expert weights per GPU)'},
         'roofline': roof, 'cpu_baseline': cpu, 'e2e': e2e,
-        'gpu_launches': (2 if use_ep else 1) * LAUNCHES_PER_LAYER * a.layers * a.steps, 'clocks': clk.summary(),
+        'gpu_launches': ((2 * LAUNCHES_PER_LAYER + (a.ep_wire == 'int8')) if use_ep else LAUNCHES_PER_LAYER)
+                        * a.layers * a.steps, 'clocks': clk.summary(),
     }
     if extra:
         line['extra'] = extra

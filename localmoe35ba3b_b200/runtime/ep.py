@@ -8,8 +8,13 @@ The reference runs on one GPU (its experts stream over PCIe); on B200s the
    that rank becomes one send row -- the token's hidden row plus its routes
    for that rank (local expert ids, routing weights; unused slots -1 / 0).
    Rows are grouped by destination rank, tokens ascending.
-2. ``all_to_all_single`` of the row counts, then of the rows and the route
-   lists (NCCL on GPUs, gloo on CPU).
+2. ``all_to_all_single`` of the row counts, then ONE of the packed send rows
+   (NCCL on GPUs, gloo on CPU).  A packed row is ``[payload | route ids int32
+   x top | route weights fp32 x top]`` as bytes; the payload is the hidden row
+   itself (``wire='bf16'``) or, with ``wire='int8'``, its W8A8 activation
+   quantisation (int8 [H] + fp32 scales [H/128], operators/w8a8.py:8-22):
+   2,112 instead of 4,096 bytes at H = 2048.  The owner dequantises an int8
+   row to ``round_dtype(q * s)`` before its experts read it.
 3. The owner expands its received rows into one row per route and runs the
    routed experts on them (``gpu_routes.moe_block`` with top 1: gate_up +
    SwiGLU, down, ``round(round(v) * w)``), then pre-reduces each received row's
@@ -24,7 +29,9 @@ The rounding sequence equals the reference's single chain
 (int8.py:245-249, prefill.py:44-46) except at the rank boundaries, where a
 pre-reduced partial sum is added instead of its terms one by one; the results
 stay within the 1e-2 bar (tests/test_ep.py checks both the bound and the exact
-EP sequence against the oracle).
+EP sequence against the oracle).  The int8 wire adds the activation
+quantisation error of the routed experts' input (the shared expert reads the
+local bf16 row); the return trip always carries the dtype rows.
 
 The compute is injected (``local_moe(x, weights, ids)`` and
 ``shared_part(x)``), so the same orchestration runs the GPU kernels in the
@@ -98,12 +105,80 @@ def _a2a(out, inp, out_splits, in_splits, group):
     dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits, group=group)
 
 
-def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=None, group=None):
+WIRES = ('bf16', 'int8')
+GROUP = 128
+
+
+def _bytes(t):
+    """A contiguous 2-D tensor's rows as uint8 ``[n, row bytes]``."""
+    return t.contiguous().view(torch.uint8).reshape(t.shape[0], -1)
+
+
+def _field(buf, start, stop, dtype):
+    """Columns ``[start, stop)`` of uint8 rows, reinterpreted as ``dtype`` rows."""
+    return buf[:, start:stop].contiguous().view(dtype)
+
+
+def wire_row_bytes(h, top, wire, itemsize=2):
+    """Bytes of one packed send row: payload + route ids + route weights."""
+    if wire not in WIRES:
+        raise ValueError("wire must be 'bf16' or 'int8'")
+    payload = h + 4 * (h // GROUP) if wire == 'int8' else itemsize * h
+    return payload + 8 * top
+
+
+def pack_rows(rows, route_ids, route_w, wire, quantize=None):
+    """Send rows -> uint8 ``[n, wire_row_bytes]``: ``[payload | ids | weights]``.
+    With ``wire='int8'`` the payload is ``quantize(rows) -> (q int8 [n, H], s fp32
+    [n, H/128])`` (the W8A8 activation quantiser) as bytes."""
+    if wire == 'int8':
+        q, s = quantize(rows)
+        parts = [_bytes(q), _bytes(s)]
+    elif wire == 'bf16':
+        parts = [_bytes(rows)]
+    else:
+        raise ValueError("wire must be 'bf16' or 'int8'")
+    parts += [_bytes(route_ids.to(torch.int32)), _bytes(route_w.to(torch.float32))]
+    return torch.cat(parts, dim=1)
+
+
+def unpack_rows(buf, h, top, wire, dtype):
+    """Received packed rows -> ``(rows dtype [n, H], route ids int32 [n, top],
+    route weights fp32 [n, top])``; int8 payloads become ``round_dtype(float(q) * s)``
+    per 128-column group."""
+    n = buf.shape[0]
+    if wire == 'int8':
+        g = h // GROUP
+        q = _field(buf, 0, h, torch.int8)
+        s = _field(buf, h, h + 4 * g, torch.float32)
+        rows = (q.float().view(n, g, GROUP) * s.view(n, g, 1)).view(n, h).to(dtype)
+        off = h + 4 * g
+    else:
+        off = torch.empty((), dtype=dtype).element_size() * h
+        rows = _field(buf, 0, off, dtype)
+    ids = _field(buf, off, off + 4 * top, torch.int32)
+    w = _field(buf, off + 4 * top, off + 8 * top, torch.float32)
+    return rows.reshape(n, h), ids.reshape(n, top), w.reshape(n, top)
+
+
+def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=None, group=None,
+                wire='bf16', quantize=None):
     """Expert-parallel MoE block for this rank's tokens ``x [T, H]``.
 
     ``local_moe(x_rows, w [R',1], ids [R',1]) -> [R', H]`` runs this rank's
     experts on route rows (local expert ids); ``shared_part(x) -> [T, H]`` is
-    round(sigmoid(gate) * shared_expert(x)) (or None)."""
+    round(sigmoid(gate) * shared_expert(x)) (or None).  ``wire`` is the format
+    of the dispatched hidden rows ('bf16': the rows as they are; 'int8': W8A8
+    activation quantisation through ``quantize``, by default the library's
+    ``operators.w8a8.quantize``)."""
+    if wire not in WIRES:
+        raise ValueError("wire must be 'bf16' or 'int8'")
+    h = x.shape[-1]
+    if wire == 'int8':
+        if h % GROUP:
+            raise ValueError('Expected CUDA rows with K divisible by 128')
+        if quantize is None:
+            from ..operators.w8a8 import quantize
     world = dist.get_world_size(group)
     route_tok, send_counts, route_ids, route_w = plan(ids, weights, experts, world)
     # 1. counts
@@ -111,15 +186,16 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     dist.all_to_all_single(recv_counts, send_counts, group=group)
     sc, rc = send_counts.tolist(), recv_counts.tolist()
     n_recv, top = sum(rc), ids.shape[1]
-    h = x.shape[-1]
-    # 2. rows and their route lists
+    # 2. packed rows: payload, route ids and weights in one exchange
     send_rows = x[route_tok].contiguous()
-    recv_rows = torch.empty((n_recv, h), dtype=x.dtype, device=x.device)
-    _a2a(recv_rows, send_rows, rc, sc, group)
-    recv_ids = torch.empty((n_recv, top), dtype=torch.int32, device=x.device)
-    _a2a(recv_ids, route_ids.contiguous(), rc, sc, group)
-    recv_w = torch.empty((n_recv, top), dtype=torch.float32, device=x.device)
-    _a2a(recv_w, route_w.contiguous(), rc, sc, group)
+    row_bytes = wire_row_bytes(h, top, wire, x.element_size())
+    if send_rows.shape[0]:
+        send_buf = pack_rows(send_rows, route_ids, route_w, wire, quantize)
+    else:
+        send_buf = torch.empty((0, row_bytes), dtype=torch.uint8, device=x.device)
+    recv_buf = torch.empty((n_recv, row_bytes), dtype=torch.uint8, device=x.device)
+    _a2a(recv_buf, send_buf, rc, sc, group)
+    recv_rows, recv_ids, recv_w = unpack_rows(recv_buf, h, top, wire, x.dtype)
     # 3. local experts on one row per route, then the per-row ordered pre-reduction
     partial = torch.zeros((n_recv, h), dtype=x.dtype, device=x.device)
     if n_recv:

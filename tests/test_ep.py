@@ -1,4 +1,5 @@
-"""Expert parallelism (runtime/ep.py) on CPU ranks over gloo, world sizes 2 and 4.
+"""Expert parallelism (runtime/ep.py) on CPU ranks over gloo, world sizes 2 and 4,
+with the bf16 and the int8 (W8A8-quantised) dispatch wire.
 
 The orchestration -- send plan, all-to-all of counts, rows and route lists,
 route expansion, per-rank ordered pre-reduction, reverse all-to-all, per-token
@@ -43,7 +44,12 @@ def _bf(a):
     return torch.from_numpy(np.asarray(a, dtype=np.float32)).to(torch.bfloat16)
 
 
-def _worker(rank, world, port, out_dir):
+def _wire_quantize(rows):
+    q, s = O.quantize_act(rows.float().numpy())
+    return torch.from_numpy(q), torch.from_numpy(s)
+
+
+def _worker(rank, world, wire, port, out_dir):
     os.environ['MASTER_ADDR'] = '127.0.0.1'
     os.environ['MASTER_PORT'] = str(port)
     dist.init_process_group('gloo', rank=rank, world_size=world)
@@ -63,14 +69,16 @@ def _worker(rank, world, port, out_dir):
             return _bf(O.shared_gate_combine(np.zeros_like(xn), sh, xn, gate, 'bf16'))
 
         out = ep.moe_forward(_bf(xs[rank]), torch.from_numpy(ws[rank]), torch.from_numpy(ids[rank]), E, local_moe,
-                             shared_part, residual=_bf(res[rank]))
+                             shared_part, residual=_bf(res[rank]), wire=wire, quantize=_wire_quantize)
         np.save(os.path.join(out_dir, f'ep{rank}.npy'), out.float().numpy())
     finally:
         dist.destroy_process_group()
 
 
-def _ep_sequence(x, w, ids, bank, shared, gate, res, world):
-    """The expert-parallel rounding sequence restated on one process."""
+def _ep_sequence(x, w, ids, bank, shared, gate, res, world, wire='bf16'):
+    """The expert-parallel rounding sequence restated on one process; with the
+    int8 wire the routed experts read round_bf16(q * s) of the W8A8 quantisation."""
+    xr = x if wire == 'bf16' else O.round_to(O.dequant(*O.quantize_act(x)), 'bf16')
     e_loc = E // world
     out = np.zeros((T, H), dtype=np.float32)
     for t in range(T):
@@ -82,7 +90,7 @@ def _ep_sequence(x, w, ids, bank, shared, gate, res, world):
             part = np.zeros(H, dtype=np.float32)
             for k in sorted(sel, key=lambda k: ids[t, k]):
                 e = int(ids[t, k])
-                v = O.routed_moe(x[t:t + 1], w[t:t + 1, k:k + 1], np.array([[0]]),
+                v = O.routed_moe(xr[t:t + 1], w[t:t + 1, k:k + 1], np.array([[0]]),
                                  [b[e:e + 1] for b in bank], 'bf16')[0]
                 part = O.round_to(part + v, 'bf16')
             acc = O.round_to(acc + part, 'bf16')
@@ -126,15 +134,43 @@ def test_plan_four_ranks():
         ep.plan(ids, w, 16, 3)
 
 
+def test_wire_rows_round_trip():
+    from localmoe35ba3b_b200.runtime import ep
+    # H = 2048, top 8: 4096 + 64 bytes on the bf16 wire, 2048 + 64 + 64 on the int8 wire
+    assert ep.wire_row_bytes(2048, 8, 'bf16') == 4160
+    assert ep.wire_row_bytes(2048, 8, 'int8') == 2176
+    with pytest.raises(ValueError):
+        ep.wire_row_bytes(2048, 8, 'fp8')
+    r = np.random.default_rng(5)
+    x = _bf(r.standard_normal((7, H)) * 3)
+    rid = torch.tensor(r.integers(-1, 8, (7, TOP)), dtype=torch.int32)
+    rw = torch.tensor(r.random((7, TOP)), dtype=torch.float32)
+    buf = ep.pack_rows(x, rid, rw, 'bf16')
+    assert buf.dtype == torch.uint8 and buf.shape == (7, ep.wire_row_bytes(H, TOP, 'bf16'))
+    rows, ids, w = ep.unpack_rows(buf, H, TOP, 'bf16', torch.bfloat16)
+    assert torch.equal(rows, x) and torch.equal(ids, rid) and torch.equal(w, rw)
+    buf = ep.pack_rows(x, rid, rw, 'int8', _wire_quantize)
+    assert buf.shape == (7, ep.wire_row_bytes(H, TOP, 'int8'))
+    rows, ids, w = ep.unpack_rows(buf, H, TOP, 'int8', torch.bfloat16)
+    want = O.round_to(O.dequant(*O.quantize_act(x.float().numpy())), 'bf16')
+    assert np.array_equal(rows.float().numpy(), want)
+    assert torch.equal(ids, rid) and torch.equal(w, rw)
+    empty = torch.empty((0, ep.wire_row_bytes(H, TOP, 'int8')), dtype=torch.uint8)
+    rows, ids, w = ep.unpack_rows(empty, H, TOP, 'int8', torch.bfloat16)
+    assert rows.shape == (0, H) and ids.shape == (0, TOP) and w.shape == (0, TOP)
+
+
+@pytest.mark.parametrize('wire', ['bf16', 'int8'])
 @pytest.mark.parametrize('world', [2, 4])
-def test_expert_parallel_matches_oracle(tmp_path, world):
+def test_expert_parallel_matches_oracle(tmp_path, world, wire):
     port = _free_port()
-    mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True, start_method='spawn')
+    mp.start_processes(_worker, args=(world, wire, port, str(tmp_path)), nprocs=world, join=True,
+                       start_method='spawn')
     bank, shared, gate, xs, ids, ws, res = _case(world)
     for rank in range(world):
         got = np.load(tmp_path / f'ep{rank}.npy')
         single = O.round_to(res[rank] + O.moe_block(xs[rank], ws[rank], ids[rank], bank, shared, gate, 'bf16'), 'bf16')
         err = np.abs(got - single).max() / np.abs(single).max()
         assert err < 1e-2, err
-        exact = _ep_sequence(xs[rank], ws[rank], ids[rank], bank, shared, gate, res[rank], world)
+        exact = _ep_sequence(xs[rank], ws[rank], ids[rank], bank, shared, gate, res[rank], world, wire)
         assert np.array_equal(got, exact)

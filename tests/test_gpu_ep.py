@@ -52,7 +52,16 @@ def test_shared_only_block_matches_oracle():
     assert rel_maxabs(to_np(out), ref) < 1e-2
 
 
-def test_expert_parallel_world1_matches_oracle():
+def _wire_ref(x, ids, w, bank, shared, gate, res, wire):
+    """The block with the routed experts reading the dispatched rows: x itself on
+    the bf16 wire, round_bf16(q * s) of its W8A8 quantisation on the int8 wire."""
+    xr = x if wire == 'bf16' else O.round_to(O.dequant(*O.quantize_act(x)), BF16)
+    routed = O.routed_moe(xr, w, ids, bank, BF16)
+    return O.round_to(res + O.shared_gate_combine(routed, O.shared_expert(x, shared, BF16), x, gate, BF16), BF16)
+
+
+@pytest.mark.parametrize('wire', ['bf16', 'int8'])
+def test_expert_parallel_world1_matches_oracle(wire):
     import torch.distributed as dist
     from localmoe35ba3b_b200.runtime import ep
     x, ids, w, bank, shared, gate, res = _case()
@@ -68,15 +77,14 @@ def test_expert_parallel_world1_matches_oracle():
         sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
         out = ep.moe_forward(to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(), bank[0].shape[0],
                              ep.gpu_local_moe(bd), ep.gpu_shared_part(bd, sh, to_dev(gate, BF16)),
-                             residual=to_dev(res, BF16))
+                             residual=to_dev(res, BF16), wire=wire)
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
-    ref = O.round_to(res + O.moe_block(x, w, ids, bank, shared, gate, BF16), BF16)
-    assert rel_maxabs(to_np(out), ref) < 1e-2
+    assert rel_maxabs(to_np(out), _wire_ref(x, ids, w, bank, shared, gate, res, wire)) < 1e-2
 
 
-def _ep2_worker(rank, port, out_dir):
+def _ep2_worker(rank, wire, port, out_dir):
     import torch.distributed as dist
     from localmoe35ba3b_b200.runtime import ep, gpu_routes
     os.environ['MASTER_ADDR'] = '127.0.0.1'
@@ -92,7 +100,7 @@ def _ep2_worker(rank, port, out_dir):
         sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
         out = ep.moe_forward(to_dev(x[sl], BF16), torch.from_numpy(w[sl]).cuda(), torch.from_numpy(ids[sl]).cuda(),
                              bank[0].shape[0], ep.gpu_local_moe(lb), ep.gpu_shared_part(lb, sh, to_dev(gate, BF16)),
-                             residual=to_dev(res[sl], BF16))
+                             residual=to_dev(res[sl], BF16), wire=wire)
         torch.cuda.synchronize()
         np.save(os.path.join(out_dir, f'ep2_{rank}.npy'), to_np(out))
     finally:
@@ -100,14 +108,15 @@ def _ep2_worker(rank, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
-def test_expert_parallel_two_gpus_matches_oracle(tmp_path):
+@pytest.mark.parametrize('wire', ['bf16', 'int8'])
+def test_expert_parallel_two_gpus_matches_oracle(tmp_path, wire):
     import torch.multiprocessing as mp
     s = socket.socket()
     s.bind(('127.0.0.1', 0))
     port = s.getsockname()[1]
     s.close()
-    mp.start_processes(_ep2_worker, args=(port, str(tmp_path)), nprocs=2, join=True, start_method='spawn')
+    mp.start_processes(_ep2_worker, args=(wire, port, str(tmp_path)), nprocs=2, join=True, start_method='spawn')
     x, ids, w, bank, shared, gate, res = _case()
-    ref = O.round_to(res + O.moe_block(x, w, ids, bank, shared, gate, BF16), BF16)
+    ref = _wire_ref(x, ids, w, bank, shared, gate, res, wire)
     got = np.concatenate([np.load(tmp_path / f'ep2_{r}.npy') for r in range(2)])
     assert rel_maxabs(got, ref) < 1e-2

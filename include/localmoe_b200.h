@@ -41,6 +41,7 @@ extern "C" {
 
 #define LMOE_DEVERR_TIMEOUT 1
 #define LMOE_DEVERR_BAD_EXPERT 2 /* an expert id outside [0, experts): read as expert 0 */
+#define LMOE_DEVERR_BAD_INDEX 4  /* a row index outside its buffer: that row is written as zeros */
 #define LMOE_ERR_TIMEOUT LMOE_DEVERR_TIMEOUT
 
 #define LMOE_BF16 0
@@ -177,6 +178,34 @@ LMOE_API int lmoe_decode_moe(const void* x, const float* weights, const int64_t*
  * 32, 64, 128, 256 or 512 (else LMOE_ERR_UNSUPPORTED); 1 <= top <= min(32, experts). */
 LMOE_API int lmoe_router_topk(const void* logits, int64_t tokens, int64_t experts, int64_t top, float* weights,
                               int64_t* ids, float* probs, int dtype, void* stream);
+
+/* Expert-parallel dispatch rows.  The reference runs the block on one GPU, so these
+ * replace no reference call: they pack and unpack the rows that the sharded block
+ * exchanges over all_to_all before the owner's routed experts (gpu_routes.routed_moe,
+ * runtime/gpu_routes.py:66-82) read them.  A packed row is
+ *   [payload | route ids int32 x top | route weights fp32 x top]
+ * with payload = the hidden row in the activation dtype (wire LMOE_WIRE_DTYPE) or its
+ * W8A8 activation quantisation, int8 [hidden] then fp32 scales [hidden/128], exactly as
+ * lmoe_quantize_rows (w8a8.quantize, operators/w8a8.py:8-22) computes it (LMOE_WIRE_INT8).
+ * hidden % 128 == 0, 0 <= top <= 32. */
+#define LMOE_WIRE_DTYPE 0
+#define LMOE_WIRE_INT8 1
+/* Bytes of one packed row, or LMOE_ERR_INVALID. */
+LMOE_API int64_t lmoe_ep_row_bytes(int64_t hidden, int64_t top, int wire, int dtype);
+/* out [rows, lmoe_ep_row_bytes] row r = pack(x[tok[r]], route_ids[r], route_w[r]);
+ * x [tokens, hidden], tok [rows] int64, route_ids [rows, top] int32, route_w [rows, top]
+ * fp32.  A tok outside [0, tokens) writes a zero payload and sets LMOE_DEVERR_BAD_INDEX.
+ * x 8-byte aligned; out 4-byte (int8 wire) or 8-byte aligned. */
+LMOE_API int lmoe_ep_pack_rows(const void* x, int64_t tokens, const int64_t* tok, const int32_t* route_ids,
+                               const float* route_w, int64_t rows, int64_t hidden, int64_t top, int wire,
+                               void* out, int dtype, int* err, void* stream);
+/* y [routes, hidden] row r = the payload of packed row row_of[r] (row r when row_of is
+ * NULL) of buf [rows, lmoe_ep_row_bytes], an int8 payload as round_dtype(float(q) * s)
+ * per 128-column group.  A row_of outside [0, rows) writes zeros and sets
+ * LMOE_DEVERR_BAD_INDEX.  y 8-byte aligned; buf 4-byte (int8 wire) or 8-byte aligned. */
+LMOE_API int lmoe_ep_unpack_rows(const void* buf, int64_t rows, const int64_t* row_of, int64_t routes,
+                                 int64_t hidden, int64_t top, int wire, void* y, int dtype, int* err,
+                                 void* stream);
 
 #ifdef __cplusplus
 }

@@ -16,6 +16,8 @@ BF16, F16 = 0, 1
 ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED = -1, -2, -3
 DEVERR_TIMEOUT = 1
 DEVERR_BAD_EXPERT = 2
+DEVERR_BAD_INDEX = 4
+WIRE_DTYPE, WIRE_INT8 = 0, 1
 
 _P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
 
@@ -44,6 +46,9 @@ SIGNATURES = {
     'lmoe_decode_moe': (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64,
                              _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
     'lmoe_router_topk': (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _I, _P]),
+    'lmoe_ep_row_bytes': (_I64, [_I64, _I64, _I, _I]),
+    'lmoe_ep_pack_rows': (_I, [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I, _P, _I, _P, _P]),
+    'lmoe_ep_unpack_rows': (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _I, _P, _P]),
 }
 
 _lib = None
@@ -117,7 +122,7 @@ def check_device_errors(device=None, reset=True):
         w.zero_()
     if v:
         raise NativeError(f'device-side error bits 0x{v:x} (1 = a bounded wait timed out, '
-                          '2 = an expert id out of range)')
+                          '2 = an expert id out of range, 4 = a row index out of range)')
     return 0
 
 

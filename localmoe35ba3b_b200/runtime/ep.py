@@ -142,6 +142,15 @@ def pack_rows(rows, route_ids, route_w, wire, quantize=None):
     return torch.cat(parts, dim=1)
 
 
+def route_fields(buf, h, top, wire, dtype):
+    """Route ids int32 ``[n, top]`` and weights fp32 ``[n, top]`` of packed rows."""
+    n = buf.shape[0]
+    off = wire_row_bytes(h, top, wire, torch.empty((), dtype=dtype).element_size()) - 8 * top
+    ids = _field(buf, off, off + 4 * top, torch.int32)
+    w = _field(buf, off + 4 * top, off + 8 * top, torch.float32)
+    return ids.reshape(n, top), w.reshape(n, top)
+
+
 def unpack_rows(buf, h, top, wire, dtype):
     """Received packed rows -> ``(rows dtype [n, H], route ids int32 [n, top],
     route weights fp32 [n, top])``; int8 payloads become ``round_dtype(float(q) * s)``
@@ -152,13 +161,40 @@ def unpack_rows(buf, h, top, wire, dtype):
         q = _field(buf, 0, h, torch.int8)
         s = _field(buf, h, h + 4 * g, torch.float32)
         rows = (q.float().view(n, g, GROUP) * s.view(n, g, 1)).view(n, h).to(dtype)
-        off = h + 4 * g
     else:
-        off = torch.empty((), dtype=dtype).element_size() * h
-        rows = _field(buf, 0, off, dtype)
-    ids = _field(buf, off, off + 4 * top, torch.int32)
-    w = _field(buf, off + 4 * top, off + 8 * top, torch.float32)
-    return rows.reshape(n, h), ids.reshape(n, top), w.reshape(n, top)
+        rows = _field(buf, 0, torch.empty((), dtype=dtype).element_size() * h, dtype)
+    return (rows.reshape(n, h), *route_fields(buf, h, top, wire, dtype))
+
+
+def _wire_code(wire):
+    from .. import _native as N
+    return N.WIRE_INT8 if wire == 'int8' else N.WIRE_DTYPE
+
+
+def pack_rows_gpu(x, tok, route_ids, route_w, wire):
+    """``pack_rows(x[tok], ...)`` in one kernel (``lmoe_ep_pack_rows``): gather, W8A8
+    quantisation on the int8 wire, route ids and weights."""
+    from .. import _native as N
+    x, tok = x.contiguous(), tok.to(torch.int64).contiguous()
+    route_ids = route_ids.to(torch.int32).contiguous()
+    route_w = route_w.to(torch.float32).contiguous()
+    n, top = route_ids.shape
+    h = x.shape[-1]
+    out = torch.empty((n, wire_row_bytes(h, top, wire, x.element_size())), dtype=torch.uint8, device=x.device)
+    N.call('lmoe_ep_pack_rows', N.ptr(x), x.shape[0], N.ptr(tok), N.ptr(route_ids), N.ptr(route_w), n, h, top,
+           _wire_code(wire), N.ptr(out), N.dtype_code(x.dtype), N.ptr(N.error_word(x.device)), N.stream(x.device))
+    return out
+
+
+def unpack_rows_gpu(buf, row_of, h, top, wire, dtype):
+    """Payload of packed row ``row_of[r]`` as activation row r, in one kernel
+    (``lmoe_ep_unpack_rows``; the int8 wire dequantised to ``round_dtype(q * s)``)."""
+    from .. import _native as N
+    row_of = row_of.to(torch.int64).contiguous()
+    y = torch.empty((row_of.numel(), h), dtype=dtype, device=buf.device)
+    N.call('lmoe_ep_unpack_rows', N.ptr(buf.contiguous()), buf.shape[0], N.ptr(row_of), row_of.numel(), h, top,
+           _wire_code(wire), N.ptr(y), N.dtype_code(dtype), N.ptr(N.error_word(buf.device)), N.stream(buf.device))
+    return y
 
 
 def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=None, group=None,
@@ -169,16 +205,16 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     experts on route rows (local expert ids); ``shared_part(x) -> [T, H]`` is
     round(sigmoid(gate) * shared_expert(x)) (or None).  ``wire`` is the format
     of the dispatched hidden rows ('bf16': the rows as they are; 'int8': W8A8
-    activation quantisation through ``quantize``, by default the library's
-    ``operators.w8a8.quantize``)."""
+    activation quantisation).  CUDA tensors pack and unpack through the library
+    kernels; CPU ranks (gloo) pack with torch and quantise through ``quantize``
+    (``rows -> (q int8 [n, H], s fp32 [n, H/128])``)."""
     if wire not in WIRES:
         raise ValueError("wire must be 'bf16' or 'int8'")
     h = x.shape[-1]
-    if wire == 'int8':
-        if h % GROUP:
-            raise ValueError('Expected CUDA rows with K divisible by 128')
-        if quantize is None:
-            from ..operators.w8a8 import quantize
+    if h % GROUP:
+        raise ValueError('Expected CUDA rows with K divisible by 128')
+    if wire == 'int8' and not x.is_cuda and quantize is None:
+        raise ValueError('the int8 wire on CPU ranks needs a quantize function')
     world = dist.get_world_size(group)
     route_tok, send_counts, route_ids, route_w = plan(ids, weights, experts, world)
     # 1. counts
@@ -186,26 +222,32 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     dist.all_to_all_single(recv_counts, send_counts, group=group)
     sc, rc = send_counts.tolist(), recv_counts.tolist()
     n_recv, top = sum(rc), ids.shape[1]
-    # 2. packed rows: payload, route ids and weights in one exchange
-    send_rows = x[route_tok].contiguous()
+    # 2. packed rows: payload, route ids and weights in one exchange (on the GPU one
+    #    kernel gathers, quantises and packs; CPU ranks pack with torch byte views)
+    n_send = route_tok.numel()
     row_bytes = wire_row_bytes(h, top, wire, x.element_size())
-    if send_rows.shape[0]:
-        send_buf = pack_rows(send_rows, route_ids, route_w, wire, quantize)
+    if x.is_cuda:
+        send_buf = pack_rows_gpu(x, route_tok, route_ids, route_w, wire)
+    elif n_send:
+        send_buf = pack_rows(x[route_tok].contiguous(), route_ids, route_w, wire, quantize)
     else:
         send_buf = torch.empty((0, row_bytes), dtype=torch.uint8, device=x.device)
     recv_buf = torch.empty((n_recv, row_bytes), dtype=torch.uint8, device=x.device)
     _a2a(recv_buf, send_buf, rc, sc, group)
-    recv_rows, recv_ids, recv_w = unpack_rows(recv_buf, h, top, wire, x.dtype)
+    recv_ids, recv_w = route_fields(recv_buf, h, top, wire, x.dtype)
     # 3. local experts on one row per route, then the per-row ordered pre-reduction
     partial = torch.zeros((n_recv, h), dtype=x.dtype, device=x.device)
     if n_recv:
         row, expert, weight, rank, max_routes = expand_routes(recv_ids, recv_w)
         if row.numel():
-            out_routes = local_moe(recv_rows[row].contiguous(), weight[:, None].contiguous(),
-                                   expert[:, None].contiguous())
-            partial = prereduce(out_routes, row, rank, n_recv, max_routes, recv_rows)
+            if x.is_cuda:
+                x_routes = unpack_rows_gpu(recv_buf, row, h, top, wire, x.dtype)
+            else:
+                x_routes = unpack_rows(recv_buf, h, top, wire, x.dtype)[0][row].contiguous()
+            out_routes = local_moe(x_routes, weight[:, None].contiguous(), expert[:, None].contiguous())
+            partial = prereduce(out_routes, row, rank, n_recv, max_routes, x)
     # 4. partial rows back to their tokens' ranks
-    back = torch.empty((send_rows.shape[0], h), dtype=x.dtype, device=x.device)
+    back = torch.empty((n_send, h), dtype=x.dtype, device=x.device)
     _a2a(back, partial, sc, rc, group)
     # 5. per token: ascending rank order, then the gated shared expert, then the residual
     out = torch.zeros_like(x)

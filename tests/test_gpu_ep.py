@@ -120,3 +120,49 @@ def test_expert_parallel_two_gpus_matches_oracle(tmp_path, wire):
     ref = _wire_ref(x, ids, w, bank, shared, gate, res, wire)
     got = np.concatenate([np.load(tmp_path / f'ep2_{r}.npy') for r in range(2)])
     assert rel_maxabs(got, ref) < 1e-2
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize('wire', ['bf16', 'int8'])
+def test_pack_and_unpack_kernels_match_torch_packing(wire, dtype):
+    """lmoe_ep_pack_rows == the torch byte packing of the gathered rows (with the
+    library's W8A8 quantiser on the int8 wire), byte for byte; lmoe_ep_unpack_rows ==
+    the torch unpacking gathered per route, bit for bit."""
+    from localmoe35ba3b_b200.operators.w8a8 import quantize
+    from localmoe35ba3b_b200.runtime import ep
+    g = torch.Generator(device='cpu').manual_seed(9)
+    T, H, top, n = 40, 1024, 8, 77
+    x = (torch.randn((T, H), generator=g) * 3).to(dtype).cuda()
+    x[3, 128:256] = 0  # an all-zero group: the scale floor
+    tok = torch.randint(0, T, (n,), generator=g).cuda()
+    rid = torch.randint(-1, 16, (n, top), generator=g, dtype=torch.int32).cuda()
+    rw = torch.rand((n, top), generator=g).cuda()
+    got = ep.pack_rows_gpu(x, tok, rid, rw, wire)
+    want = ep.pack_rows(x[tok].contiguous(), rid, rw, wire, quantize)
+    torch.cuda.synchronize()
+    assert got.shape == (n, ep.wire_row_bytes(H, top, wire)) and torch.equal(got, want)
+    row_of = torch.randint(0, n, (200,), generator=g).cuda()
+    rows = ep.unpack_rows_gpu(got, row_of, H, top, wire, dtype)
+    ref_rows, ids, w = ep.unpack_rows(want, H, top, wire, dtype)
+    torch.cuda.synchronize()
+    assert torch.equal(rows.view(torch.int16), ref_rows[row_of].view(torch.int16))
+    assert torch.equal(ids, rid) and torch.equal(w, rw)
+
+
+def test_pack_kernel_flags_a_token_index_out_of_range():
+    """The kernel checks each token index before it reads x: an index outside
+    [0, tokens) writes zeros and sets LMOE_DEVERR_BAD_INDEX (4)."""
+    from localmoe35ba3b_b200 import _native
+    from localmoe35ba3b_b200.runtime import ep
+    _native.check_device_errors()
+    x = torch.ones((4, 256), dtype=torch.bfloat16, device='cuda')
+    tok = torch.tensor([0, 4, 2], device='cuda')
+    rid = torch.zeros((3, 2), dtype=torch.int32, device='cuda')
+    rw = torch.ones((3, 2), device='cuda')
+    buf = ep.pack_rows_gpu(x, tok, rid, rw, 'int8')
+    rows = ep.unpack_rows_gpu(buf, torch.tensor([0, 1, 2, 3], device='cuda'), 256, 2, 'int8', torch.bfloat16)
+    torch.cuda.synchronize()
+    assert int(_native.error_word('cuda').item()) == _native.DEVERR_BAD_INDEX
+    _native.error_word('cuda').zero_()
+    assert torch.all(rows[1] == 0) and torch.all(rows[3] == 0)
+    assert torch.all(rows[0] == 1) and torch.all(rows[2] == 1)

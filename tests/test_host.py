@@ -64,6 +64,31 @@ def test_c_abi_rejects_bad_geometry_without_launching():
                                None, None) == _native.ERR_INVALID
 
 
+def test_ep_wire_row_bytes_and_validation():
+    """The dispatch-row size agrees with the Python packer; bad geometry, a null
+    pointer or a misaligned buffer is refused before any launch."""
+    from localmoe35ba3b_b200 import _native
+    from localmoe35ba3b_b200.runtime import ep
+    lib = _native.lib()
+    for h, top in ((2048, 8), (128, 1), (4096, 32), (256, 0)):
+        for wire, code in (('bf16', _native.WIRE_DTYPE), ('int8', _native.WIRE_INT8)):
+            assert lib.lmoe_ep_row_bytes(h, top, code, _native.BF16) == ep.wire_row_bytes(h, top, wire)
+    assert lib.lmoe_ep_row_bytes(2048, 8, _native.WIRE_INT8, _native.BF16) == 2048 + 64 + 64
+    assert lib.lmoe_ep_row_bytes(100, 8, 0, 0) == _native.ERR_INVALID
+    assert lib.lmoe_ep_row_bytes(2048, 33, 0, 0) == _native.ERR_INVALID
+    assert lib.lmoe_ep_row_bytes(2048, 8, 2, 0) == _native.ERR_INVALID
+    p = ctypes.c_void_p(256)
+    assert lib.lmoe_ep_pack_rows(p, 4, p, p, p, 0, 2048, 8, 1, p, 0, None, None) == 0
+    assert lib.lmoe_ep_pack_rows(p, 4, p, p, p, 3, 2000, 8, 1, p, 0, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_pack_rows(None, 4, p, p, p, 3, 2048, 8, 1, p, 0, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_pack_rows(ctypes.c_void_p(258), 4, p, p, p, 3, 2048, 8, 1, p, 0, None,
+                                 None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_unpack_rows(p, 3, p, 0, 2048, 8, 1, p, 0, None, None) == 0
+    assert lib.lmoe_ep_unpack_rows(p, 3, p, 5, 2048, 8, 1, None, 0, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_unpack_rows(p, 3, p, 5, 2048, 8, 0, ctypes.c_void_p(260), 0, None,
+                                   None) == _native.ERR_INVALID
+
+
 def test_operator_validation_errors_match_reference():
     from localmoe35ba3b_b200.operators import int8, routing, w8a8
     from localmoe35ba3b_b200.runtime import gpu_routes

@@ -117,7 +117,10 @@ LMOE_API int lmoe_routed_reduce(const void* down, const int64_t* ordered, const 
  * is an array of 5 cudaEvent_t recorded before/between/after the four launches.
  * top == 0 (ids and weights may then be NULL) is accepted with a shared expert: the output
  * is the gated shared expert alone (+ residual) -- how an expert-parallel caller computes
- * its own tokens' shared expert while their routes run on other GPUs. */
+ * its own tokens' shared expert while their routes run on other GPUs.  A route id of -1
+ * is "no route": it is not computed and the combine skips it (an expert-parallel owner's
+ * received rows list only its own experts); any other id outside [0, experts) sets
+ * LMOE_DEVERR_BAD_EXPERT. */
 LMOE_API int64_t lmoe_moe_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t hidden, int64_t inter);
 LMOE_API int lmoe_routed_moe(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
                     const int8_t* qg, const float* sg, const int8_t* qd, const float* sd, int64_t experts,

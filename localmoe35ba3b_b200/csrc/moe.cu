@@ -21,7 +21,8 @@ constexpr int kCombineThreads = 256;
 
 template <int DT>
 __global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(
-    const typename Act<DT>::T* __restrict__ down, const int32_t* __restrict__ ordered, int top, int64_t H, int64_t R,
+    const typename Act<DT>::T* __restrict__ down, const int32_t* __restrict__ ordered,
+    const int32_t* __restrict__ hdr, int top, int64_t H, int64_t R,
     const typename Act<DT>::T* __restrict__ x, const typename Act<DT>::T* __restrict__ gate_w, int with_shared,
     const typename Act<DT>::T* __restrict__ residual, typename Act<DT>::T* __restrict__ out) {
   using A = Act<DT>;
@@ -54,12 +55,15 @@ __global__ void __launch_bounds__(kCombineThreads) moe_combine_kernel(
   // kernel's output
   grid_dep_wait();
   grid_dep_launch();
+  // routes at sorted positions >= valid have id -1 ("no route"): never computed, skipped
+  const int64_t valid = hdr[kHdrValid];
   for (int64_t c = threadIdx.x * 8; c < H; c += kCombineThreads * 8) {
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
     for (int i = 0; i < top; ++i) {
       const int64_t r = ordered[t * top + i];
+      if (r >= valid) continue;
       const uint4 v = *reinterpret_cast<const uint4*>(down + r * H + c);
       const uint32_t va[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -211,14 +215,15 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   if ((rc = mark(3))) return rc;
 
   const int32_t* ordered = (const int32_t*)(meta + ML.off_ordered);
+  const int32_t* hdr = (const int32_t*)(meta + ML.off_hdr);
   if (dtype == LMOE_BF16)
     LMOE_CUDA_CHECK(launch_pdl(moe_combine_kernel<LMOE_BF16>, dim3((unsigned)tokens), dim3(kCombineThreads), 0, st,
-                               (const __nv_bfloat16*)dn, ordered, (int)top, hidden, R, (const __nv_bfloat16*)x,
+                               (const __nv_bfloat16*)dn, ordered, hdr, (int)top, hidden, R, (const __nv_bfloat16*)x,
                                (const __nv_bfloat16*)sh_gate_w, with_shared ? 1 : 0,
                                (const __nv_bfloat16*)residual, (__nv_bfloat16*)out));
   else
     LMOE_CUDA_CHECK(launch_pdl(moe_combine_kernel<LMOE_F16>, dim3((unsigned)tokens), dim3(kCombineThreads), 0, st,
-                               (const __half*)dn, ordered, (int)top, hidden, R, (const __half*)x,
+                               (const __half*)dn, ordered, hdr, (int)top, hidden, R, (const __half*)x,
                                (const __half*)sh_gate_w, with_shared ? 1 : 0, (const __half*)residual,
                                (__half*)out));
   return mark(4);

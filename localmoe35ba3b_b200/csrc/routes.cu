@@ -30,6 +30,19 @@ __device__ __forceinline__ int clamp_id(int64_t v, int E, int* err) {
   return (int)v;
 }
 
+// Fused-path bucket of a route id: -1 is "no route" (a padded slot: an
+// expert-parallel owner's received row lists only the routes to its own
+// experts); it sorts into bucket E after every expert, like an out-of-range
+// id, so it gets no GEMM tile and the combine skips it.  Any other id outside
+// [0, E) is flagged.
+__device__ __forceinline__ int route_bucket(int64_t v, int E, int* err) {
+  if (v < 0 || v >= E) {
+    if (v != -1) raise_error(err, 2);
+    return E;
+  }
+  return (int)v;
+}
+
 // inclusive block scan over kRouteThreads values (one per thread)
 __device__ int block_incl_scan(int v, int* warp_tot) {
   const int lane = lane_id(), warp = warp_id();
@@ -122,6 +135,7 @@ __device__ void write_tiles(const RouteArgs& a, const int* s_first, int R, int* 
     a.hdr[kHdrTokens] = a.T;
     a.hdr[kHdrExperts] = E;
     a.hdr[kHdrShared] = a.with_shared;
+    a.hdr[kHdrValid] = s_first[E];
   }
 }
 
@@ -281,7 +295,7 @@ __global__ void __launch_bounds__(kMetaChunk) meta_count_kernel(const int64_t* _
   for (int i = threadIdx.x; i <= E; i += kMetaChunk) h[i] = 0;
   __syncthreads();
   const int f = blockIdx.x * kMetaChunk + threadIdx.x;
-  if (f < R) atomicAdd(&h[clamp_id(ids[f], E, err)], 1);
+  if (f < R) atomicAdd(&h[route_bucket(ids[f], E, err)], 1);
   __syncthreads();
   for (int i = threadIdx.x; i <= E; i += kMetaChunk) cc[(int64_t)blockIdx.x * (E + 1) + i] = h[i];
 }

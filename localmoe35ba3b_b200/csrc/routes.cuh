@@ -36,7 +36,7 @@ struct MetaLayout {
   }
 };
 
-// header words
-enum { kHdrNumTiles = 0, kHdrRoutes = 1, kHdrTokens = 2, kHdrExperts = 3, kHdrShared = 4 };
+// header words; kHdrValid = routes with an expert id in [0, experts) (sorted first)
+enum { kHdrNumTiles = 0, kHdrRoutes = 1, kHdrTokens = 2, kHdrExperts = 3, kHdrShared = 4, kHdrValid = 5 };
 
 }  // namespace lmoe

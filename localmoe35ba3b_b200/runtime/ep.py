@@ -15,10 +15,11 @@ The reference runs on one GPU (its experts stream over PCIe); on B200s the
    quantisation (int8 [H] + fp32 scales [H/128], operators/w8a8.py:8-22):
    2,112 instead of 4,096 bytes at H = 2048.  The owner dequantises an int8
    row to ``round_dtype(q * s)`` before its experts read it.
-3. The owner expands its received rows into one row per route and runs the
-   routed experts on them (``gpu_routes.moe_block`` with top 1: gate_up +
-   SwiGLU, down, ``round(round(v) * w)``), then pre-reduces each received row's
-   routes in ascending expert order: ``acc = round(acc + v)``.
+3. The owner runs its routed experts on the received rows with their route
+   lists (``gpu_routes.moe_block``; -1 slots, routed to other ranks, are
+   skipped: gate_up + SwiGLU, down, ``round(round(v) * w)``), whose ordered
+   combine pre-reduces each row's routes in ascending expert order:
+   ``acc = round(acc + v)``.
 4. The reverse ``all_to_all_single`` returns one row per (token, rank).
 5. Each token folds its returned rows in ascending rank order (= ascending
    expert order, the shards are contiguous), adds its gated shared expert
@@ -187,23 +188,44 @@ def pack_rows_gpu(x, tok, route_ids, route_w, wire):
 
 
 def unpack_rows_gpu(buf, row_of, h, top, wire, dtype):
-    """Payload of packed row ``row_of[r]`` as activation row r, in one kernel
-    (``lmoe_ep_unpack_rows``; the int8 wire dequantised to ``round_dtype(q * s)``)."""
+    """Payload of packed row ``row_of[r]`` (row r when ``row_of`` is None) as
+    activation row r, in one kernel (``lmoe_ep_unpack_rows``; the int8 wire
+    dequantised to ``round_dtype(q * s)``)."""
     from .. import _native as N
-    row_of = row_of.to(torch.int64).contiguous()
-    y = torch.empty((row_of.numel(), h), dtype=dtype, device=buf.device)
-    N.call('lmoe_ep_unpack_rows', N.ptr(buf.contiguous()), buf.shape[0], N.ptr(row_of), row_of.numel(), h, top,
+    if row_of is not None:
+        row_of = row_of.to(torch.int64).contiguous()
+    n = buf.shape[0] if row_of is None else row_of.numel()
+    y = torch.empty((n, h), dtype=dtype, device=buf.device)
+    N.call('lmoe_ep_unpack_rows', N.ptr(buf.contiguous()), buf.shape[0], N.ptr(row_of), n, h, top,
            _wire_code(wire), N.ptr(y), N.dtype_code(dtype), N.ptr(N.error_word(buf.device)), N.stream(buf.device))
     return y
+
+
+def prereduced(route_fn):
+    """A ``local_moe`` built from a one-route-per-row expert function
+    ``route_fn(x_rows [R', H], w [R', 1], ids [R', 1]) -> [R', H]``: the received
+    rows are expanded into one row per route, and each received row's routes are
+    then summed in ascending expert order, ``acc = round(acc + v)``."""
+    def run(x_rows, w, ids):
+        row, expert, weight, rank, max_routes = expand_routes(ids, w)
+        if not row.numel():
+            return torch.zeros_like(x_rows)
+        y = route_fn(x_rows[row].contiguous(), weight[:, None].contiguous(), expert[:, None].contiguous())
+        return prereduce(y, row, rank, x_rows.shape[0], max_routes, x_rows)
+    return run
 
 
 def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=None, group=None,
                 wire='bf16', quantize=None):
     """Expert-parallel MoE block for this rank's tokens ``x [T, H]``.
 
-    ``local_moe(x_rows, w [R',1], ids [R',1]) -> [R', H]`` runs this rank's
-    experts on route rows (local expert ids); ``shared_part(x) -> [T, H]`` is
-    round(sigmoid(gate) * shared_expert(x)) (or None).  ``wire`` is the format
+    ``local_moe(x_rows [n, H], w [n, top] fp32, ids [n, top] int32) -> [n, H]``
+    runs this rank's experts on the received rows: ids are local expert ids,
+    -1 where the slot routes to another rank, and row i of the result is
+    ``acc = round(acc + round(round(down_e(x_i)) * w))`` over the row's routes in
+    ascending expert order (``gpu_local_moe``: the routed block itself;
+    ``prereduced``: the same from a one-route-per-row function).
+    ``shared_part(x) -> [T, H]`` is round(sigmoid(gate) * shared_expert(x)) (or None).  ``wire`` is the format
     of the dispatched hidden rows ('bf16': the rows as they are; 'int8': W8A8
     activation quantisation).  CUDA tensors pack and unpack through the library
     kernels; CPU ranks (gloo) pack with torch and quantise through ``quantize``
@@ -234,18 +256,17 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
         send_buf = torch.empty((0, row_bytes), dtype=torch.uint8, device=x.device)
     recv_buf = torch.empty((n_recv, row_bytes), dtype=torch.uint8, device=x.device)
     _a2a(recv_buf, send_buf, rc, sc, group)
-    recv_ids, recv_w = route_fields(recv_buf, h, top, wire, x.dtype)
-    # 3. local experts on one row per route, then the per-row ordered pre-reduction
-    partial = torch.zeros((n_recv, h), dtype=x.dtype, device=x.device)
+    # 3. local experts on the received rows, each row's routes pre-reduced in
+    #    ascending expert order (on GPUs the block's own ordered combine)
     if n_recv:
-        row, expert, weight, rank, max_routes = expand_routes(recv_ids, recv_w)
-        if row.numel():
-            if x.is_cuda:
-                x_routes = unpack_rows_gpu(recv_buf, row, h, top, wire, x.dtype)
-            else:
-                x_routes = unpack_rows(recv_buf, h, top, wire, x.dtype)[0][row].contiguous()
-            out_routes = local_moe(x_routes, weight[:, None].contiguous(), expert[:, None].contiguous())
-            partial = prereduce(out_routes, row, rank, n_recv, max_routes, x)
+        if x.is_cuda:
+            recv_rows = unpack_rows_gpu(recv_buf, None, h, top, wire, x.dtype)
+            recv_ids, recv_w = route_fields(recv_buf, h, top, wire, x.dtype)
+        else:
+            recv_rows, recv_ids, recv_w = unpack_rows(recv_buf, h, top, wire, x.dtype)
+        partial = local_moe(recv_rows, recv_w, recv_ids)
+    else:
+        partial = torch.zeros((0, h), dtype=x.dtype, device=x.device)
     # 4. partial rows back to their tokens' ranks
     back = torch.empty((n_send, h), dtype=x.dtype, device=x.device)
     _a2a(back, partial, sc, rc, group)
@@ -264,7 +285,10 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
 
 
 def gpu_local_moe(banks):
-    """This rank's experts through the routed-MoE kernels (top 1 per route row)."""
+    """This rank's experts through the routed-MoE kernels on the received rows:
+    a -1 id is a slot routed elsewhere, which the block's routing metadata sorts
+    after every expert, gives no GEMM tile and leaves out of the ordered combine,
+    so the combine is the per-row pre-reduction."""
     from . import gpu_routes
 
     def run(x_rows, w, ids):

@@ -59,9 +59,10 @@ def _worker(rank, world, wire, port, out_dir):
         e_loc = E // world
         lb = [b[rank * e_loc:(rank + 1) * e_loc] for b in bank]
 
-        def local_moe(x_rows, w, i):
+        def route_fn(x_rows, w, i):
             y = O.routed_moe(x_rows.float().numpy(), w.numpy(), i.numpy(), lb, 'bf16')
             return _bf(y)
+        local_moe = ep.prereduced(route_fn)
 
         def shared_part(x):
             xn = x.float().numpy()

@@ -166,3 +166,37 @@ def test_pack_kernel_flags_a_token_index_out_of_range():
     _native.error_word('cuda').zero_()
     assert torch.all(rows[1] == 0) and torch.all(rows[3] == 0)
     assert torch.all(rows[0] == 1) and torch.all(rows[2] == 1)
+
+
+def test_block_skips_no_route_slots():
+    """A -1 route id is a padded slot (an expert-parallel owner's received row lists
+    only its own experts): it gets no GEMM tile and the ordered combine skips it.  The
+    result equals, bit for bit, the block with each -1 slot replaced by a real expert
+    at weight 0 (whose route adds round(v * 0) = 0, leaving every bf16 sum unchanged);
+    no error bit is set; and it matches the oracle over the valid routes."""
+    from localmoe35ba3b_b200 import _native
+    from localmoe35ba3b_b200.runtime import gpu_routes
+    x, ids, w, bank, shared, gate, res = _case(T=150)
+    r = rng(45)
+    ids = ids.copy()
+    w = w.copy()
+    drop = r.random(ids.shape) < 0.55
+    drop[7] = True          # a row with no route at all
+    ids[drop] = -1
+    w[drop] = 0.0
+    bd = [torch.from_numpy(b).cuda() for b in bank]
+    _native.check_device_errors()
+    got = gpu_routes.moe_block(to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(), bd)
+    filled = np.where(drop, (np.arange(ids.shape[1])[None, :] * 5 + 3) % bank[0].shape[0], ids)
+    same = gpu_routes.moe_block(to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(filled).cuda(), bd)
+    torch.cuda.synchronize()
+    assert int(_native.error_word('cuda').item()) == 0
+    assert torch.equal(got.view(torch.int16), same.view(torch.int16))
+    got = to_np(got)
+    assert np.all(got[7] == 0)
+    ref = np.zeros_like(got)
+    for t in range(x.shape[0]):
+        keep = ~drop[t]
+        if keep.any():
+            ref[t] = O.routed_moe(x[t:t + 1], w[t:t + 1, keep], ids[t:t + 1, keep], bank, BF16)[0]
+    assert rel_maxabs(got, ref) < 1e-2

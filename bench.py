@@ -41,6 +41,9 @@ UNIT = 'tok/s'
 # meta_place_kernel (routing metadata), permute_rows_kernel, grouped_ts_kernel<.., false>
 # (gate_up + SwiGLU), grouped_ts_kernel<.., true> (down + routing weight), moe_combine_kernel.
 LAUNCHES_PER_LAYER = 7
+# expert-parallel layer: the owner's routed block (as above), the shared-only block (top 0:
+# no per-chunk count or placement, 5 launches), the dispatch-row pack and unpack kernels
+EP_LAUNCHES_PER_LAYER = LAUNCHES_PER_LAYER + 5 + 2
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
 # `ncu --set full` capture (`python bench.py --layers 2 --steps 1 --warmup 1 --no-cpu-baseline
 # --no-extra`, -k regex:grouped_ts -s 2 -c 2): gate_up 404.2 MB + down 244.1 MB.  Per-layer
@@ -329,8 +332,8 @@ def run_ours(a, rank, world, local):
                    'active_experts_mean': round(float(np.mean(active)), 1),
                    'l2': 'inputs larger than L2 (33.2 GB of resident expert weights per GPU)'},
         'roofline': roof, 'cpu_baseline': cpu, 'e2e': e2e,
-        'gpu_launches': ((2 * LAUNCHES_PER_LAYER + (a.ep_wire == 'int8')) if use_ep else LAUNCHES_PER_LAYER)
-                        * a.layers * a.steps, 'clocks': clk.summary(),
+        'gpu_launches': (EP_LAUNCHES_PER_LAYER if use_ep else LAUNCHES_PER_LAYER) * a.layers * a.steps,
+        'clocks': clk.summary(),
     }
     if extra:
         line['extra'] = extra

@@ -1,12 +1,14 @@
 """Expert parallelism (runtime/ep.py) on CPU ranks over gloo, world sizes 2 and 4,
 with the bf16 and the int8 (W8A8-quantised) dispatch wire.
 
-The orchestration -- send plan, all-to-all of counts, rows and route lists,
-route expansion, per-rank ordered pre-reduction, reverse all-to-all, per-token
-fold in ascending rank order, gated shared expert, residual -- runs exactly as
-on GPUs; the expert compute is the oracle's.  Checked against (a) the
-single-device oracle within the 1e-2 bar, and (b) an independent restatement of
-the expert-parallel rounding sequence, bit for bit.
+The orchestration -- send plan, all-to-all of the counts and of the packed rows
+(payload, route ids, route weights), per-rank ordered pre-reduction, reverse
+all-to-all, per-token fold in ascending rank order, gated shared expert,
+residual -- runs as on GPUs; the expert compute is the oracle's, one route per
+row, pre-reduced by ``ep.prereduced`` (on GPUs the routed block's own ordered
+combine does that step).  Checked against (a) the single-device oracle within
+the 1e-2 bar, and (b) an independent restatement of the expert-parallel rounding
+sequence, bit for bit.
 """
 import os
 import socket

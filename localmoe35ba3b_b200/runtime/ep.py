@@ -271,12 +271,16 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     back = torch.empty((n_send, h), dtype=x.dtype, device=x.device)
     _a2a(back, partial, sc, rc, group)
     # 5. per token: ascending rank order, then the gated shared expert, then the residual
+    #    (the rows are grouped by rank, sc[g] of them for rank g, each token at most once
+    #    per rank: host-known slices, no device synchronisation)
     out = torch.zeros_like(x)
-    g_of_row = torch.repeat_interleave(torch.arange(world, device=x.device), send_counts)
+    start = 0
     for g in range(world):
-        sel = g_of_row == g
-        tok = route_tok[sel]
-        out[tok] = _round_add(out[tok], back[sel])
+        stop = start + sc[g]
+        if stop > start:
+            tok = route_tok[start:stop]
+            out[tok] = _round_add(out[tok], back[start:stop])
+        start = stop
     if shared_part is not None:
         out = _round_add(out, shared_part(x))
     if residual is not None:

@@ -136,6 +136,60 @@ def test_decode_graph_capture_replays_identically():
     del g
 
 
+def test_decode_layer_graph_capture():
+    """A whole one-token layer in one CUDA graph: a dense Int8Linear (an o_proj of
+    [H, H]), the router's bf16 logits and its softmax / top-k / renormalise, and the
+    MoE block with its gated shared expert and the residual -- no host
+    synchronisation anywhere (the reference syncs per layer, int8.py:160).  For two
+    token rows copied into the static input, every stage of a replay equals the
+    eager library call on the graph's own input to that stage, bit for bit (the
+    logits are cuBLAS's and are checked only through the stages that read them), and
+    the layer matches the oracle on the graph's routing."""
+    from localmoe35ba3b_b200.operators import int8
+    from localmoe35ba3b_b200.runtime import block, decode
+    E, H, I, top = 256, 2048, 512, 8
+    case = _case(93, E, H, I, top, BF16)
+    _, _, _, bank, shared, gate_w, _ = case
+    xd, _, _, bd, shd, gd, _ = _dev(case, BF16)
+    r = rng(94)
+    qo_np, so_np = rand_q(r, (H, H))
+    qo, so = torch.from_numpy(qo_np).cuda(), torch.from_numpy(so_np).cuda()
+    router = to_dev(act(r, (E, H), BF16, 0.02), BF16)
+    x = xd.clone()  # the graph's static input row
+
+    def layer():
+        h = int8.linear(x, qo, so)
+        logits = torch.nn.functional.linear(h, router)
+        w, ids = block.topk_from_logits(logits, top)
+        y = decode.decode_block(h, w, ids, bd, shared=shd, shared_gate_weight=gd, residual=x)
+        return h, logits, w, ids, y
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer()  # warm the workspaces and the library handles outside the capture
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        h, logits, w, ids, y = layer()
+    for seed in (95, 96):
+        x_np = act(rng(seed), (1, H), BF16)
+        x.copy_(to_dev(x_np, BF16))
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(h, int8.linear(x, qo, so))
+        w2, ids2 = block.topk_from_logits(logits, top)
+        assert torch.equal(w, w2) and torch.equal(ids, ids2)
+        y2 = decode.decode_block(h, w, ids, bd, shared=shd, shared_gate_weight=gd, residual=x)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y2)
+        h_np = to_np(h)
+        assert rel_maxabs(h_np, O.linear_w8a16(x_np, qo_np, so_np, BF16)) < 1e-2
+        blk = O.decode_block(h_np, ids.cpu().numpy(), w.cpu().numpy(), bank, shared, gate_w, 'w8a8', BF16)
+        assert rel_maxabs(to_np(y), O.round_to(x_np + blk, BF16)) < 1e-2
+    del g
+
+
 def test_decode_bad_expert_id_sets_error_bit():
     """An id outside [0, E) is caught by the table kernel's own bounds check:
     it raises the device error bit and reads expert 0 instead."""

@@ -53,7 +53,7 @@ NCU_TRAFFIC_SOURCE = ('ncu dram__bytes_read.sum + dram__bytes_write.sum, gate_up
                       '2048-token layer; bytes per layer like alg_bytes_per_layer')
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=50)
@@ -69,7 +69,7 @@ def parse():
     ap.add_argument('--ep-wire', choices=('bf16', 'int8'), default='bf16',
                     help='with --ep: format of the dispatched hidden rows (int8 = W8A8 activation '
                          'quantisation, 2112 instead of 4096 bytes per row)')
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 # ------------------------------------------------------------------ distributed
@@ -322,8 +322,7 @@ def run_ours(a, rank, world, local):
         'metric': METRIC, 'value': round(value, 1), 'unit': UNIT, 'n_gpus': world, 'steps': a.steps,
         'warmup': a.warmup, 'ms_per_step': round(ms_step, 4), 'higher_is_better': True, 'scaling': 'weak',
         'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded random-init INT8 weights, N(0,1) inputs)',
-        'config': {'workload': f'prefill chunk: {a.tokens} tokens x {a.layers} layers, 256 experts top-8 + shared, '
-                               'hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, Zipf(1.1) routing',
+        'config': {'workload': workload(a),
                    'tokens_per_gpu': a.tokens, 'layers': a.layers,
                    'parallelism': (f'ep{world} (experts {e_loc} per GPU, all-to-all over NCCL, '
                                    f'{a.ep_wire} dispatch rows)' if use_ep
@@ -472,6 +471,12 @@ def cpu_baseline_leg(repeats=3):
                       f'(HF experts loop), median of {repeats}, scaled to 40 layers; CPU: {C.cpu_model()}'}
 
 
+def workload(a):
+    """The workload name both arms report in ``config``."""
+    return (f'prefill chunk: {a.tokens} tokens x {a.layers} layers, 256 experts top-8 + shared, '
+            'hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, Zipf(1.1) routing')
+
+
 def run_reference(a, rank, world):
     if rank != 0:
         return
@@ -483,15 +488,22 @@ def run_reference(a, rank, world):
     for _ in range(a.steps):
         t, threads = C.time_layer(case, repeats=1)
     wall = time.perf_counter() - t0
-    value = 256 * a.steps / (wall * 40)
+    # each step times one layer of 256 tokens; tok/s of the whole workload = 256 tokens
+    # per (layer time x layers), and a workload step (a.tokens through a.layers) is
+    # a.tokens / value seconds
+    value = 256 * a.steps / (wall * a.layers)
     print(json.dumps({
         'impl': 'reference', 'metric': METRIC, 'value': round(value, 2), 'unit': UNIT, 'n_gpus': world,
-        'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(wall / a.steps * 1e3 * 40, 2),
-        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'prefill chunk (sample: 256 tokens x 1 layer per step, scaled to 40 layers)'},
+        'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(a.tokens / value * 1e3, 2),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+        'data': 'synthetic (seeded random-init INT8 weights, N(0,1) inputs)',
+        'config': {'workload': workload(a), 'tokens_per_gpu': a.tokens, 'layers': a.layers,
+                   'parallelism': 'host CPU (the oracle port of the reference path)',
+                   'l2': 'not applicable (host CPU)'},
         'cpu_baseline': {'value': round(value, 2), 'unit': UNIT, 'cores': threads, 'kind': 'port',
-                         'sample': '256 tokens x 1 MoE layer per step (HF experts loop, fp32 dequantised '
-                                   f'weights, torch on {threads} host threads; CPU: {C.cpu_model()})'},
+                         'sample': f'256 tokens x 1 MoE layer per step, scaled to {a.layers} layers (HF experts '
+                                   f'loop, fp32 dequantised weights, torch on {threads} host threads; CPU: '
+                                   f'{C.cpu_model()})'},
         'e2e': {'value': round(value, 2), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }), flush=True)
 

@@ -112,3 +112,25 @@ def test_no_cpu_fallback_when_library_missing(monkeypatch):
     monkeypatch.setattr(_native, '_lib', None)
     with pytest.raises(_native.NativeError, match='no fallback'):
         _native.lib()
+
+
+def test_bench_reference_arm_json_contract():
+    """``bench.py --impl reference`` (no GPU needed) prints one JSON line on our arm's
+    metric, unit and workload, with its cpu_baseline and e2e objects."""
+    import json
+    import subprocess
+    import sys
+    sys.path.insert(0, ROOT)
+    import bench
+    out = subprocess.run([sys.executable, os.path.join(ROOT, 'bench.py'), '--impl', 'reference', '--steps', '1',
+                          '--warmup', '0'], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith('{')]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d['impl'] == 'reference' and d['metric'] == bench.METRIC and d['unit'] == bench.UNIT
+    assert d['higher_is_better'] is True and d['value'] > 0 and d['n_gpus'] == 1
+    assert d['config']['workload'] == bench.workload(bench.parse([]))
+    cb = d['cpu_baseline']
+    assert cb['kind'] == 'port' and cb['cores'] >= 1 and cb['value'] == d['value'] and cb['sample']
+    assert d['e2e'] == {'value': d['value'], 'unit': d['unit'], 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}

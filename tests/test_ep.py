@@ -24,7 +24,9 @@ from oracle import oracle as O
 E, H, I, TOP, T = 16, 256, 128, 4, 12
 
 
-def _case(world):
+def _case(world, skew=False):
+    """Seeded layer and per-rank tokens; ``skew`` routes every token to rank 0's
+    experts only (the other ranks then receive no rows at all)."""
     r = np.random.default_rng(321)
     qg, sg = O.quantize_weight(r.standard_normal((E, 2 * I, H)).astype(np.float32) * 0.02)
     qd, sd = O.quantize_weight(r.standard_normal((E, H, I)).astype(np.float32) * 0.02)
@@ -34,6 +36,8 @@ def _case(world):
     xs, ids, ws, res = [], [], [], []
     for _ in range(world):
         logits = r.standard_normal((T, E)).astype(np.float32) + O.zipf_bias(E, r)[None]
+        if skew:
+            logits[:, :E // world] += 30.0
         i, w = O.route(logits, TOP)
         xs.append(O.round_to(r.standard_normal((T, H)).astype(np.float32), 'bf16'))
         ids.append(i)
@@ -51,13 +55,13 @@ def _wire_quantize(rows):
     return torch.from_numpy(q), torch.from_numpy(s)
 
 
-def _worker(rank, world, wire, port, out_dir):
+def _worker(rank, world, wire, port, out_dir, skew=False):
     os.environ['MASTER_ADDR'] = '127.0.0.1'
     os.environ['MASTER_PORT'] = str(port)
     dist.init_process_group('gloo', rank=rank, world_size=world)
     try:
         from localmoe35ba3b_b200.runtime import ep
-        bank, shared, gate, xs, ids, ws, res = _case(world)
+        bank, shared, gate, xs, ids, ws, res = _case(world, skew)
         e_loc = E // world
         lb = [b[rank * e_loc:(rank + 1) * e_loc] for b in bank]
 
@@ -176,4 +180,19 @@ def test_expert_parallel_matches_oracle(tmp_path, world, wire):
         err = np.abs(got - single).max() / np.abs(single).max()
         assert err < 1e-2, err
         exact = _ep_sequence(xs[rank], ws[rank], ids[rank], bank, shared, gate, res[rank], world, wire)
+        assert np.array_equal(got, exact)
+
+
+def test_expert_parallel_ranks_without_rows(tmp_path):
+    """Every token routes to rank 0's experts: rank 1 receives no rows, sends all of its
+    rows to rank 0 and gets them back pre-reduced; bit-exact as above."""
+    world = 2
+    port = _free_port()
+    mp.start_processes(_worker, args=(world, 'bf16', port, str(tmp_path), True), nprocs=world, join=True,
+                       start_method='spawn')
+    bank, shared, gate, xs, ids, ws, res = _case(world, skew=True)
+    assert all((i < E // world).all() for i in ids)
+    for rank in range(world):
+        got = np.load(tmp_path / f'ep{rank}.npy')
+        exact = _ep_sequence(xs[rank], ws[rank], ids[rank], bank, shared, gate, res[rank], world)
         assert np.array_equal(got, exact)

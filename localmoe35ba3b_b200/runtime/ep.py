@@ -23,8 +23,8 @@ The reference runs on one GPU (its experts stream over PCIe); on B200s the
 4. The reverse ``all_to_all_single`` returns one row per (token, rank).
 5. Each token folds its returned rows in ascending rank order (= ascending
    expert order, the shards are contiguous), adds its gated shared expert
-   (computed locally: the shared expert and the gate are replicated) and
-   the residual.
+   (computed locally -- the shared expert and the gate are replicated -- while
+   the dispatch exchange of step 2 is in flight) and the residual.
 
 The rounding sequence equals the reference's single chain
 (int8.py:245-249, prefill.py:44-46) except at the rank boundaries, where a
@@ -234,7 +234,7 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
         raise ValueError("wire must be 'bf16' or 'int8'")
     h = x.shape[-1]
     if h % GROUP:
-        raise ValueError('Expected CUDA rows with K divisible by 128')
+        raise ValueError('hidden size must be a multiple of 128')
     if wire == 'int8' and not x.is_cuda and quantize is None:
         raise ValueError('the int8 wire on CPU ranks needs a quantize function')
     world = dist.get_world_size(group)
@@ -255,7 +255,12 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     else:
         send_buf = torch.empty((0, row_bytes), dtype=torch.uint8, device=x.device)
     recv_buf = torch.empty((n_recv, row_bytes), dtype=torch.uint8, device=x.device)
-    _a2a(recv_buf, send_buf, rc, sc, group)
+    # the exchange runs asynchronously (NCCL on its own stream) while this rank's gated
+    # shared expert, which reads only the local rows, runs on the current stream
+    work = dist.all_to_all_single(recv_buf, send_buf, output_split_sizes=rc, input_split_sizes=sc, group=group,
+                                  async_op=True)
+    sh = shared_part(x) if shared_part is not None else None
+    work.wait()
     # 3. local experts on the received rows, each row's routes pre-reduced in
     #    ascending expert order (on GPUs the block's own ordered combine)
     if n_recv:
@@ -281,8 +286,8 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
             tok = route_tok[start:stop]
             out[tok] = _round_add(out[tok], back[start:stop])
         start = stop
-    if shared_part is not None:
-        out = _round_add(out, shared_part(x))
+    if sh is not None:
+        out = _round_add(out, sh)
     if residual is not None:
         out = _round_add(residual, out)
     return out

@@ -196,3 +196,39 @@ def test_expert_parallel_ranks_without_rows(tmp_path):
         got = np.load(tmp_path / f'ep{rank}.npy')
         exact = _ep_sequence(xs[rank], ws[rank], ids[rank], bank, shared, gate, res[rank], world)
         assert np.array_equal(got, exact)
+
+
+def _leaving_worker(rank, port, out_dir):
+    """Rank 1 leaves between layers (exits without joining the layer's exchange);
+    rank 0 runs the layer and must see an error from its collective, not hang."""
+    import datetime
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=2, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(0)
+    from localmoe35ba3b_b200.runtime import ep
+    bank, shared, gate, xs, ids, ws, res = _case(2)
+
+    def route_fn(x_rows, w, i):
+        return _bf(O.routed_moe(x_rows.float().numpy(), w.numpy(), i.numpy(), [b[:E // 2] for b in bank], 'bf16'))
+    try:
+        ep.moe_forward(_bf(xs[0]), torch.from_numpy(ws[0]), torch.from_numpy(ids[0]), E, ep.prereduced(route_fn))
+        result = 'not detected'
+    except RuntimeError as e:
+        result = 'detected: ' + str(e).splitlines()[0][:200]
+    with open(os.path.join(out_dir, 'leave.txt'), 'w') as f:
+        f.write(result)
+    os._exit(0)
+
+
+def test_rank_that_leaves_is_detected_by_the_next_exchange(tmp_path):
+    """Failure detection on the host: the surviving rank's next all-to-all ends with a
+    RuntimeError (closed peer or the process group's 10 s timeout) instead of waiting
+    for good."""
+    import time
+    port = _free_port()
+    t0 = time.time()
+    mp.start_processes(_leaving_worker, args=(port, str(tmp_path)), nprocs=2, join=True, start_method='spawn')
+    assert (tmp_path / 'leave.txt').read_text().startswith('detected')
+    assert time.time() - t0 < 120

@@ -33,8 +33,9 @@ def _int8_pair(m):
     q, s = getattr(m, 'q', None), getattr(m, 'scale', None)
     if not (isinstance(q, torch.Tensor) and isinstance(s, torch.Tensor)):
         return None
-    if q.dtype != torch.int8 or q.ndim != 2 or s.dtype != torch.float32 or tuple(s.shape) != (q.shape[0],
-                                                                                           q.shape[1] // 128):
+    if q.dtype != torch.int8 or q.ndim != 2 or q.shape[1] % 128 or s.dtype != torch.float32:
+        return None
+    if tuple(s.shape) != (q.shape[0], q.shape[1] // 128):
         return None
     return q, s
 

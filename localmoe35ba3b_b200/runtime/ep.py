@@ -42,27 +42,45 @@ import torch
 import torch.distributed as dist
 
 
+def plan_counts(ids, experts, world):
+    """Device-side first half of ``plan``: ``(dest [T, top], mask [T, world], send_counts
+    [world] int64)``, no host synchronisation."""
+    t, top = ids.shape
+    if experts % world:
+        raise ValueError('experts must divide evenly across ranks')
+    e_loc = experts // world
+    dest = torch.div(ids.long(), e_loc, rounding_mode='floor')                   # [T, top]
+    mask = torch.zeros((t, world), dtype=torch.bool, device=ids.device)
+    mask.scatter_(1, dest, True)
+    return dest, mask, mask.sum(0).to(torch.int64)
+
+
+def plan_rows(ids, weights, experts, dest, mask, n):
+    """Second half of ``plan`` for ``n`` (host-known) send rows: the selected
+    (rank, token) pairs in ascending (rank, token) order come first in a stable
+    sort of the unselected flags, so no ``nonzero`` (and no synchronisation) is
+    needed."""
+    t = ids.shape[0]
+    world = mask.shape[1]
+    e_loc = experts // world
+    flat = (~mask.t()).reshape(-1).to(torch.int8)                                 # 0 = selected, index g*T + t
+    order = torch.argsort(flat, stable=True)[:n]
+    g_idx, t_idx = torch.div(order, t, rounding_mode='floor'), order % t
+    rows_ids = ids.long()[t_idx]                                                  # [n, top]
+    mine = dest[t_idx] == g_idx[:, None]
+    route_ids = torch.where(mine, rows_ids - g_idx[:, None] * e_loc, torch.full_like(rows_ids, -1)).to(torch.int32)
+    route_w = torch.where(mine, weights[t_idx].float(), torch.zeros((), dtype=torch.float32, device=ids.device))
+    return t_idx, route_ids, route_w
+
+
 def plan(ids, weights, experts, world):
     """Send rows for one rank's tokens.
 
     Returns ``(send_tok [n] int64, send_counts [world] int64, route_ids [n, top]
     int32 local expert ids or -1, route_w [n, top] fp32)``; rows are grouped by
     destination rank (ascending), tokens ascending within a rank."""
-    t, top = ids.shape
-    if experts % world:
-        raise ValueError('experts must divide evenly across ranks')
-    e_loc = experts // world
-    ids = ids.long()
-    dest = torch.div(ids, e_loc, rounding_mode='floor')                          # [T, top]
-    mask = torch.zeros((t, world), dtype=torch.bool, device=ids.device)
-    mask.scatter_(1, dest, True)
-    send_counts = mask.sum(0).to(torch.int64)                                    # [world]
-    g_idx, t_idx = torch.nonzero(mask.t(), as_tuple=True)                        # grouped by rank, tokens ascending
-    rows_ids = ids[t_idx]                                                        # [n, top]
-    rows_dest = dest[t_idx]
-    mine = rows_dest == g_idx[:, None]
-    route_ids = torch.where(mine, rows_ids - g_idx[:, None] * e_loc, torch.full_like(rows_ids, -1)).to(torch.int32)
-    route_w = torch.where(mine, weights[t_idx].float(), torch.zeros((), dtype=torch.float32, device=ids.device))
+    dest, mask, send_counts = plan_counts(ids, experts, world)
+    t_idx, route_ids, route_w = plan_rows(ids, weights, experts, dest, mask, int(send_counts.sum()))
     return t_idx, send_counts, route_ids, route_w
 
 
@@ -238,12 +256,15 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     if wire == 'int8' and not x.is_cuda and quantize is None:
         raise ValueError('the int8 wire on CPU ranks needs a quantize function')
     world = dist.get_world_size(group)
-    route_tok, send_counts, route_ids, route_w = plan(ids, weights, experts, world)
-    # 1. counts
+    # 1. counts: computed and exchanged on the device, then read once (the layer's one
+    #    host synchronisation: the exchange sizes must be known on the host)
+    dest, mask, send_counts = plan_counts(ids, experts, world)
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
-    sc, rc = send_counts.tolist(), recv_counts.tolist()
+    counts = torch.cat([send_counts, recv_counts]).tolist()
+    sc, rc = counts[:world], counts[world:]
     n_recv, top = sum(rc), ids.shape[1]
+    route_tok, route_ids, route_w = plan_rows(ids, weights, experts, dest, mask, sum(sc))
     # 2. packed rows: payload, route ids and weights in one exchange (on the GPU one
     #    kernel gathers, quantises and packs; CPU ranks pack with torch byte views)
     n_send = route_tok.numel()

@@ -134,3 +134,35 @@ def test_bench_reference_arm_json_contract():
     cb = d['cpu_baseline']
     assert cb['kind'] == 'port' and cb['cores'] >= 1 and cb['value'] == d['value'] and cb['sample']
     assert d['e2e'] == {'value': d['value'], 'unit': d['unit'], 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """A C host (no C++ and no CUDA headers) compiles against the header, links the
+    library and calls its host-only entry points."""
+    import shutil
+    import subprocess
+    gcc = shutil.which('gcc')
+    if gcc is None:
+        pytest.skip('gcc not available')
+    from localmoe35ba3b_b200 import _native
+    src = tmp_path / 'host.c'
+    src.write_text('''
+#include <stdio.h>
+#include "localmoe_b200.h"
+int main(void) {
+  int64_t row = lmoe_ep_row_bytes(2048, 8, LMOE_WIRE_INT8, LMOE_BF16);
+  int64_t bad = lmoe_ep_row_bytes(100, 8, LMOE_WIRE_INT8, LMOE_BF16);
+  int rc = lmoe_quantize_rows((const void*)16, (int8_t*)16, (float*)16, 4, 100, LMOE_BF16, NULL);
+  printf("%d %lld %lld %d\\n", lmoe_abi_version(), (long long)row, (long long)bad, rc);
+  return 0;
+}
+''')
+    exe = tmp_path / 'host'
+    libdir = os.path.dirname(_native.LIB_PATH)
+    cc = subprocess.run([gcc, '-std=c99', '-Wall', '-Werror', '-I', os.path.join(ROOT, 'include'), str(src),
+                         '-o', str(exe), '-L', libdir, '-l:' + os.path.basename(_native.LIB_PATH),
+                         '-Wl,-rpath,' + libdir], capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    assert run.stdout.split() == ['1', '2176', str(_native.ERR_INVALID), str(_native.ERR_INVALID)]

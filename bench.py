@@ -1,23 +1,32 @@
 #!/usr/bin/env python
-"""Benchmark: routed-expert FFN prefill (2048-token chunk x 40 layers, W8A16).
+"""Benchmark: routed-expert FFN prefill through 40 MoE layers (W8A16).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one 2048-token prefill chunk through 40 MoE expert layers
-(256 experts top-8 + 1 shared expert, hidden 2048, intermediate 512, INT8
-group-128 weights with FP32 scales, bf16 activations, Zipf(1.1)-biased
-routing), every layer through ``gpu_routes.moe_block`` (routing metadata,
-gate_up GEMM + SwiGLU, down GEMM + routing weight, ordered combine with the
-gated shared expert and the residual add).  All 40 layers' weights (33.2 GB)
-stay resident, so each step streams ~18 GB of distinct expert weights: the
-inputs are larger than L2 and no L2 flush is needed.
+N = 1: one step = one 2048-token prefill chunk through 40 MoE
+layers (256 experts top-8 + 1 shared expert, hidden 2048, intermediate 512, INT8
+group-128 weights with FP32 scales, bf16 activations, Zipf(1.1)-biased routing),
+every layer through ``gpu_routes.moe_block`` (routing metadata, gate_up GEMM +
+SwiGLU, down GEMM + routing weight, ordered combine with the gated shared expert
+and the residual add).  All 40 layers' weights (33.2 GB) stay resident, so each
+step streams ~18 GB of distinct expert weights: the inputs are larger than L2 and
+no L2 flush is needed.
 
-Prints one JSON line (rank 0).  ``value`` = tokens/s over the whole job with
-inputs resident in HBM; ``e2e`` = the same through the public API with the
-step's inputs (hidden states, routing ids and weights for every layer) copied
-from pinned host memory and the final hidden states copied back inside the
-timed region.  ``--impl reference`` times the reference's CPU path (the HF
-experts loop on fp32-dequantised weights) on the host cores instead.
+N > 1 (torchrun): expert parallelism.  One step = 16,384 tokens
+in total (``--total-tokens``; 16384 / N per GPU) through 40 layers whose 256
+experts are sharded 256 / N per GPU; each layer is ``ep.GpuLayer.forward``
+(dispatch kernels, an all-to-all over NCCL, the owner's experts + the shared
+expert, the return all-to-all, the fold).  The total work is fixed as N grows
+(strong scaling).  ``--dp`` runs N independent data-parallel replicas instead.
+
+Prints one JSON line (rank 0).  ``value`` = tokens/s over the whole job with the
+inputs resident in HBM (no per-stage events inside the timed region); the
+per-stage times come from separate instrumented steps after it.  ``e2e`` = the
+same through the public API with the step's inputs (hidden states, routing ids
+and weights of all layers) copied from pinned host memory and the final hidden
+states copied back inside the timed region.  ``--impl reference`` times the
+reference's CPU path (the HF experts loop on fp32-dequantised weights) on the
+host cores instead.
 """
 import argparse
 import json
@@ -37,13 +46,14 @@ HIDDEN, INTER, EXPERTS, TOP = 2048, 512, 256, 8
 EXPERT_BYTES = 3 * INTER * HIDDEN + 3 * INTER * HIDDEN // 128 * 4  # 3,244,032
 METRIC = 'expert-FFN prefill tok/s (2048-chunk x 40 layers, W8A16)'
 UNIT = 'tok/s'
-# Kernels launched per layer of the step: meta_count_kernel, meta_scan_kernel,
+# Kernels launched per layer of the single-GPU step: meta_count_kernel, meta_scan_kernel,
 # meta_place_kernel (routing metadata), permute_rows_kernel, grouped_ts_kernel<.., false>
 # (gate_up + SwiGLU), grouped_ts_kernel<.., true> (down + routing weight), moe_combine_kernel.
 LAUNCHES_PER_LAYER = 7
-# expert-parallel layer: the owner's routed block (as above), the shared-only block (top 0:
-# no per-chunk count or placement, 5 launches), the dispatch-row pack and unpack kernels
-EP_LAUNCHES_PER_LAYER = LAUNCHES_PER_LAYER + 5 + 2
+# expert-parallel layer: ep_plan_kernel, ep_pack_kernel (dispatch), ep_owner_meta_kernel,
+# ep_owner_scatter_kernel, the two grouped_ts_kernel launches, ep_owner_combine_kernel,
+# ep_fold_kernel (+ two NCCL all-to-all kernels, not counted)
+EP_LAUNCHES_PER_LAYER = 8
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
 # `ncu --set full` capture (`python bench.py --layers 2 --steps 1 --warmup 1 --no-cpu-baseline
 # --no-extra`, -k regex:grouped_ts -s 2 -c 2): gate_up 404.2 MB + down 244.1 MB.  Per-layer
@@ -56,20 +66,37 @@ NCU_TRAFFIC_SOURCE = ('ncu dram__bytes_read.sum + dram__bytes_write.sum, gate_up
 def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=50)
+    ap.add_argument('--steps', type=int, default=20)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--layers', type=int, default=40)
-    ap.add_argument('--tokens', type=int, default=2048)
+    ap.add_argument('--tokens', type=int, default=2048, help='tokens per GPU (single GPU, --dp)')
+    ap.add_argument('--total-tokens', type=int, default=16384, help='tokens of the whole job (expert parallelism)')
+    ap.add_argument('--stage-steps', type=int, default=3, help='instrumented steps after the timed region')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--seed', type=int, default=0)
-    ap.add_argument('--no-extra', action='store_true', help='skip the decode (C3) and dense-sweep (C4) legs')
-    ap.add_argument('--ep', action='store_true', help='with --gpus N > 1: expert parallelism (experts sharded, '
-                                                      'all-to-all) instead of N data-parallel replicas')
+    ap.add_argument('--no-extra', action='store_true', help='skip the decode (C3), dense (C4) and C5 1-GPU legs')
+    ap.add_argument('--only', choices=('c3', 'c4', 'c5'), default=None,
+                    help='run one extra leg alone (1 GPU; for profiling) and print its JSON')
+    ap.add_argument('--dp', action='store_true', help='with --gpus N > 1: N data-parallel replicas (full weights '
+                                                      'per GPU) instead of expert parallelism')
     ap.add_argument('--ep-wire', choices=('bf16', 'int8'), default='bf16',
-                    help='with --ep: format of the dispatched hidden rows (int8 = W8A8 activation '
-                         'quantisation, 2112 instead of 4096 bytes per row)')
+                    help='expert parallelism: format of the dispatched hidden rows (int8 = W8A8 activation '
+                         'quantisation, 2112 instead of 4096 payload bytes per row)')
     return ap.parse_args(argv)
+
+
+def use_ep(a, world):
+    return world > 1 and not a.dp
+
+
+def job_tokens(a, world):
+    """(tokens of the whole job per step, tokens per GPU)."""
+    if use_ep(a, world):
+        if a.total_tokens % world:
+            raise SystemExit(f'--total-tokens {a.total_tokens} is not divisible by {world} GPUs')
+        return a.total_tokens, a.total_tokens // world
+    return a.tokens * world, a.tokens
 
 
 # ------------------------------------------------------------------ distributed
@@ -82,7 +109,8 @@ def dist_setup(n):
     if world > 1:
         import datetime
         torch.cuda.set_device(local)
-        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device('cuda', local))
     else:
         torch.cuda.set_device(0)
     return rank, world, local
@@ -96,9 +124,10 @@ def barrier(world):
 def max_over_ranks(v, world):
     if world == 1:
         return v
-    t = torch.tensor([v], dtype=torch.float64, device='cuda')
+    t = torch.tensor(np.atleast_1d(np.asarray(v, dtype=np.float64)), device='cuda')
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
+    r = t.cpu().numpy()
+    return float(r[0]) if np.ndim(v) == 0 else r
 
 
 # ------------------------------------------------------------------ clocks
@@ -159,22 +188,26 @@ def quantize_gpu(w):
     return q.reshape(w.shape).contiguous(), s.contiguous()
 
 
-def make_layers(layers, dev, seed, experts=EXPERTS):
-    """Per layer: the routed bank (``experts`` experts: all 256, or this rank's shard
-    under expert parallelism), the shared expert and its gate."""
-    g = torch.Generator(device=dev).manual_seed(seed)
+def make_layers(layers, dev, seed, experts=EXPERTS, shard=0):
+    """Per layer: the routed bank (``experts`` experts: all 256, or shard ``shard`` of
+    them under expert parallelism), the shared expert and its gate (the same on
+    every rank)."""
+    g = torch.Generator(device=dev).manual_seed(seed + 7919 * shard)
+    gs = torch.Generator(device=dev).manual_seed(seed + 104729)
     out = []
     for _ in range(layers):
         qg, sg = quantize_gpu(torch.randn((experts, 2 * INTER, HIDDEN), generator=g, device=dev) * 0.02)
         qd, sd = quantize_gpu(torch.randn((experts, HIDDEN, INTER), generator=g, device=dev) * 0.02)
-        shared = [quantize_gpu(torch.randn(s, generator=g, device=dev) * 0.02)
+        shared = [quantize_gpu(torch.randn(s, generator=gs, device=dev) * 0.02)
                   for s in ((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER))]
-        gate = (torch.randn((1, HIDDEN), generator=g, device=dev) * 0.02).bfloat16()
+        gate = (torch.randn((1, HIDDEN), generator=gs, device=dev) * 0.02).bfloat16()
         out.append(((qg, sg, qd, sd), shared, gate))
     return out
 
 
 def make_routing(layers, tokens, dev, seed):
+    """Per layer: router logits ~N(0,1) plus a Zipf(1.1) bias over a seeded permutation of
+    the experts, softmax top-8 renormalised (HF's router tail); and the layer-0 input."""
     g = torch.Generator(device=dev).manual_seed(seed + 1)
     ids, wts = [], []
     for _ in range(layers):
@@ -189,30 +222,68 @@ def make_routing(layers, tokens, dev, seed):
     return x, torch.stack(ids), torch.stack(wts)
 
 
+def load_peaks():
+    p = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {'hbm': float(d['hbm_gbs']), 'tc': float(d['bf16_tflops']),
+                'tc_sustained': float(d.get('bf16_tflops_sustained', d['bf16_tflops'])),
+                'src': 'measured (MEASURED_PEAKS.json, sustained bf16)'}
+    return {'hbm': 6650.0, 'tc': 1590.0, 'tc_sustained': 1400.0, 'src': 'fallback'}
+
+
+def workload(a, world=1):
+    """The workload name both arms report in ``config``."""
+    total, per = job_tokens(a, world)
+    if use_ep(a, world):
+        return (f'expert-parallel prefill: {total} tokens x {a.layers} layers over {world} GPUs ({per} per GPU), '
+                '256 experts top-8 + shared, hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, '
+                'Zipf(1.1) routing')
+    return (f'prefill chunk: {per} tokens x {a.layers} layers{f" per GPU x {world} replicas" if world > 1 else ""}'
+            ', 256 experts top-8 + shared, hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, '
+            'Zipf(1.1) routing')
+
+
+def config(a, world):
+    """``config`` of the JSON line, the same for both arms."""
+    total, per = job_tokens(a, world)
+    if use_ep(a, world):
+        par = (f'ep{world} (experts {EXPERTS // world} per GPU, all-to-all over NCCL, {a.ep_wire} dispatch rows, '
+               'fixed-size exchanges)')
+    else:
+        par = f'dp{world} replicas (full weights per GPU)' if world > 1 else 'single'
+    return {'workload': workload(a, world), 'tokens': total, 'tokens_per_gpu': per, 'layers': a.layers,
+            'parallelism': par, 'l2': 'inputs larger than L2 (every layer\'s expert weights resident in HBM, '
+                                      'streamed once per step)'}
+
+
+def scaling(a, world):
+    return 'strong' if use_ep(a, world) else 'weak'
+
+
+# ------------------------------------------------------------------ our arm
 def run_ours(a, rank, world, local):
     from localmoe35ba3b_b200 import _native
     from localmoe35ba3b_b200.runtime import ep, gpu_routes
     dev = torch.device('cuda', local)
     peaks = load_peaks()
-    # N > 1: data-parallel replicas by default (all 40 layers' weights, 33.2 GB, fit on every
-    # B200, and each GPU runs its own tokens); --ep shards the experts instead
-    use_ep = world > 1 and a.ep
-    e_loc = EXPERTS // world if use_ep else EXPERTS
-    layers = make_layers(a.layers, dev, a.seed + 1000 * rank, e_loc)
-    x0, ids, wts = make_routing(a.layers, a.tokens, dev, a.seed + 1000 * rank)
+    ep_mode = use_ep(a, world)
+    total, tokens = job_tokens(a, world)
+    e_loc = EXPERTS // world if ep_mode else EXPERTS
+    layers = make_layers(a.layers, dev, a.seed, e_loc, shard=rank if ep_mode else 0)
+    x0, ids, wts = make_routing(a.layers, tokens, dev, a.seed + 1000 * rank)
     active = [int(torch.unique(ids[l]).numel()) for l in range(a.layers)]
-    if use_ep:
-        fns = [(ep.gpu_local_moe(bank), ep.gpu_shared_part(bank, shared, gate)) for bank, shared, gate in layers]
+    layer_ep = ep.GpuLayer(tokens, TOP, EXPERTS, world, HIDDEN, INTER, torch.bfloat16, dev, a.ep_wire) \
+        if ep_mode else None
 
     def step(x, ids, wts, events=None):
-        if use_ep:
-            # expert parallelism: this rank's experts serve every rank's routes to them
-            for l in range(a.layers):
-                x = ep.moe_forward(x, wts[l], ids[l], EXPERTS, fns[l][0], fns[l][1], residual=x, wire=a.ep_wire)
-            return x
         for l, (bank, shared, gate) in enumerate(layers):
-            x = gpu_routes.moe_block(x, wts[l], ids[l], bank, shared=shared, shared_gate_weight=gate,
-                                     residual=x, stage_events=None if events is None else events[l])
+            ev = None if events is None else events[l]
+            if ep_mode:
+                x = layer_ep.forward(x, wts[l], ids[l], bank, shared, gate, residual=x, events=ev)
+            else:
+                x = gpu_routes.moe_block(x, wts[l], ids[l], bank, shared=shared, shared_gate_weight=gate,
+                                         residual=x, stage_events=ev)
         return x
 
     for _ in range(a.warmup):
@@ -220,64 +291,101 @@ def run_ours(a, rank, world, local):
     torch.cuda.synchronize()
     _native.check_device_errors(dev)
 
-    # ---- timed region: inputs resident in HBM
-    timed_with_events = 0 if use_ep else min(a.steps, 10)
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(a.layers)]
-           for _ in range(timed_with_events)]
+    # ---- timed region: inputs resident in HBM, no per-stage events
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         start.record()
-        for k in range(a.steps):
-            step(x0, ids, wts, evs[k] if k < timed_with_events else None)
+        for _ in range(a.steps):
+            step(x0, ids, wts)
         end.record()
         torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world)
     _native.check_device_errors(dev)
     ms_step = ms / a.steps
-    value = world * a.tokens * a.steps / (ms / 1e3)
+    value = total * a.steps / (ms / 1e3)
 
-    # per-stage times from the events recorded inside the timed region
-    st = np.zeros(4)
-    for k in range(timed_with_events):
+    # ---- stage times: separate instrumented steps (events between the launches stop the
+    #      programmatic-dependent-launch overlap, so they stay out of the timed region)
+    nev = 6 if ep_mode else 5
+    S = max(1, a.stage_steps)
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(a.layers)] for _ in range(S)]
+    barrier(world)
+    for k in range(S):
+        step(x0, ids, wts, evs[k])
+    torch.cuda.synchronize()
+    barrier(world)
+    st = np.zeros(nev - 1)
+    for k in range(S):
         for l in range(a.layers):
             e = evs[k][l]
-            st += [e[i].elapsed_time(e[i + 1]) for i in range(4)]
-    if timed_with_events:
-        st /= timed_with_events * a.layers  # ms per layer
-        gemm_ms = st[1] + st[2]
+            st += [e[i].elapsed_time(e[i + 1]) for i in range(nev - 1)]
+    st /= S * a.layers  # ms per layer
+    st_max = max_over_ranks(st, world)
+    if ep_mode:
+        # the owner's own stages (metadata + scatter, gate_up, down, combine) from one more step
+        oev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(a.layers)]
+        x = x0
+        for l, (bank, shared, gate) in enumerate(layers):
+            layer_ep.dispatch(x, wts[l], ids[l])
+            layer_ep.exchange(layer_ep.recv, layer_ep.send)
+            layer_ep.owner(x, bank, shared, stage_events=oev[l])
+            layer_ep.exchange(layer_ep.back, layer_ep.partial)
+            x = layer_ep.fold(x, gate, residual=x)
+        torch.cuda.synchronize()
+        ost = np.mean([[oev[l][i].elapsed_time(oev[l][i + 1]) for i in range(4)] for l in range(a.layers)], 0)
+        ost_max = max_over_ranks(ost, world)
+        gemm_ms = float(ost_max[1] + ost_max[2])
     else:
-        # expert parallelism: no per-launch events across the exchange; the whole layer
-        gemm_ms = ms_step / a.layers
-    routes = a.tokens * TOP
-    rows = routes + a.tokens
+        gemm_ms = float(st[1] + st[2])
+
+    routes = tokens * TOP
+    rows = routes + tokens
     flops = 2.0 * rows * 3 * INTER * HIDDEN  # gate_up + down, routed + shared
-    act_bytes = a.tokens * HIDDEN * 2 + 2 * rows * INTER * 2 + rows * HIDDEN * 2
-    wbytes = (float(np.mean(active)) / (world if use_ep else 1) + 1) * EXPERT_BYTES
+    act_bytes = tokens * HIDDEN * 2 + 2 * rows * INTER * 2 + rows * HIDDEN * 2
+    if ep_mode:
+        # experts of this rank with at least one route from any rank: measured on the device
+        wbytes = (e_loc + 1) * EXPERT_BYTES
+    else:
+        wbytes = (float(np.mean(active)) + 1) * EXPERT_BYTES
     gemm_bytes = wbytes + act_bytes
     tflops = flops / (gemm_ms / 1e3) / 1e12
     gbs = gemm_bytes / (gemm_ms / 1e3) / 1e9
-    pk_tc, pk_tc_src = peaks['tc_sustained'], peaks['src']
-    pk_hbm = peaks['hbm']
-    t_tc, t_hbm = flops / (pk_tc * 1e12), gemm_bytes / (pk_hbm * 1e9)
-    bound = 'tensor' if t_tc >= t_hbm else 'hbm'
+    pk_tc, pk_hbm = peaks['tc_sustained'], peaks['hbm']
+    bound = 'tensor' if flops / (pk_tc * 1e12) >= gemm_bytes / (pk_hbm * 1e9) else 'hbm'
     if bound == 'tensor':
         roof = {'bound': 'tensor', 'achieved': round(tflops, 1), 'peak': pk_tc, 'unit': 'TFLOP/s',
                 'frac': round(tflops / pk_tc, 4)}
     else:
         roof = {'bound': 'hbm', 'achieved': round(gbs, 1), 'peak': pk_hbm, 'unit': 'GB/s',
                 'frac': round(gbs / pk_hbm, 4)}
-    roof.update({'traffic': None if use_ep else NCU_TRAFFIC_PER_LAYER,
-                 'traffic_source': 'not captured for the expert-parallel step' if use_ep else NCU_TRAFFIC_SOURCE,
-                 'kernel': ('whole expert-parallel layer (all-to-all + local experts + shared + combine), per rank'
-                            if use_ep else 'grouped GEMMs (gate_up+SwiGLU, down+weight) per layer'),
-                 'peak_source': pk_tc_src, 'flops_per_layer': flops, 'alg_bytes_per_layer': round(gemm_bytes),
+    roof.update({'traffic': None if ep_mode else NCU_TRAFFIC_PER_LAYER,
+                 'traffic_source': ('not captured for the expert-parallel owner' if ep_mode else NCU_TRAFFIC_SOURCE),
+                 'kernel': ('grouped GEMMs (gate_up+SwiGLU, down+weight) per layer' +
+                            (', on each rank\'s received routes + its own tokens\' shared expert (max over ranks)'
+                             if ep_mode else '')),
+                 'timing': f'CUDA events between the launches, {S} instrumented steps after the timed region',
+                 'peak_source': peaks['src'], 'flops_per_layer': flops, 'alg_bytes_per_layer': round(gemm_bytes),
                  'tensor_frac': round(tflops / pk_tc, 4), 'hbm_frac': round(gbs / pk_hbm, 4),
-                 'gemm_us_per_layer': round(gemm_ms * 1e3, 2),
-                 'stage_us_per_layer': {'route_meta': round(st[0] * 1e3, 2), 'gate_up': round(st[1] * 1e3, 2),
-                                        'down': round(st[2] * 1e3, 2), 'combine': round(st[3] * 1e3, 2)}})
+                 'gemm_us_per_layer': round(gemm_ms * 1e3, 2)})
+    if ep_mode:
+        names = ('dispatch', 'all_to_all_dispatch', 'owner', 'all_to_all_return', 'fold')
+        phases = {n: round(float(v) * 1e3, 2) for n, v in zip(names, st_max)}
+        phases.update({f'owner_{n}': round(float(v) * 1e3, 2)
+                       for n, v in zip(('meta_scatter', 'gate_up', 'down', 'combine'), ost_max)})
+        seg = (layer_ep.cap + 1) * layer_ep.row_bytes
+        cross = (world - 1) * seg
+        a2a_us = phases['all_to_all_dispatch']
+        roof['phase_us_per_layer_max_over_ranks'] = phases
+        roof['limiting_phase'] = max(names, key=lambda n: phases[n])
+        roof['nvlink'] = {'dispatch_bytes_per_rank': cross, 'return_bytes_per_rank': (world - 1) * layer_ep.cap *
+                          HIDDEN * 2, 'dispatch_gbs': round(cross / (a2a_us * 1e-6) / 1e9, 1) if a2a_us > 0 else None,
+                          'peer_copy_ref_gbs': 770.0}
+    else:
+        roof['stage_us_per_layer'] = {'route_meta': round(st[0] * 1e3, 2), 'gate_up': round(st[1] * 1e3, 2),
+                                      'down': round(st[2] * 1e3, 2), 'combine': round(st[3] * 1e3, 2)}
 
     # ---- end to end through the public API with host buffers
     xh = x0.cpu().pin_memory()
@@ -306,34 +414,34 @@ def run_ours(a, rank, world, local):
     torch.cuda.synchronize()
     barrier(world)
     ms_e2e = max_over_ranks(s2.elapsed_time(e2), world)
-    e2e = {'value': round(world * a.tokens * e_steps / (ms_e2e / 1e3), 1), 'unit': UNIT,
+    e2e = {'value': round(total * e_steps / (ms_e2e / 1e3), 1), 'unit': UNIT,
            'h2d_bytes_per_step': int(xh.numel() * 2 + idh.numel() * 8 + wh.numel() * 4),
-           'd2h_bytes_per_step': int(outh.numel() * 2)}
+           'd2h_bytes_per_step': int(outh.numel() * 2),
+           'api': 'ep.GpuLayer.forward per layer' if ep_mode else 'gpu_routes.moe_block per layer'}
 
-    cpu = None
+    cpu = check = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cpu = cpu_baseline_leg()
+        cpu, check = cpu_baseline_leg(layers[0], x0, ids[0], wts[0], dev)
     extra = {}
     if not a.no_extra and world == 1:
-        extra['c3_decode'] = decode_leg(layers, dev, peaks, max(3, a.steps), a.warmup, a.seed + 1000 * rank)
+        extra['c3_decode'] = decode_leg(layers, dev, peaks, max(3, a.steps), a.warmup, a.seed)
         extra['c4_dense'] = dense_leg(dev, peaks)
+        extra['c5_ep_1gpu'] = ep_single_gpu_leg(a, layers, dev)
 
+    gpu_launches = (EP_LAUNCHES_PER_LAYER if ep_mode else LAUNCHES_PER_LAYER) * a.layers * a.steps
     line = {
         'metric': METRIC, 'value': round(value, 1), 'unit': UNIT, 'n_gpus': world, 'steps': a.steps,
-        'warmup': a.warmup, 'ms_per_step': round(ms_step, 4), 'higher_is_better': True, 'scaling': 'weak',
-        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded random-init INT8 weights, N(0,1) inputs)',
-        'config': {'workload': workload(a),
-                   'tokens_per_gpu': a.tokens, 'layers': a.layers,
-                   'parallelism': (f'ep{world} (experts {e_loc} per GPU, all-to-all over NCCL, '
-                                   f'{a.ep_wire} dispatch rows)' if use_ep
-                                   else (f'dp{world} replicas (full weights per GPU; --ep for expert parallelism)'
-                                         if world > 1 else 'single')),
-                   'active_experts_mean': round(float(np.mean(active)), 1),
-                   'l2': 'inputs larger than L2 (33.2 GB of resident expert weights per GPU)'},
+        'warmup': a.warmup, 'ms_per_step': round(ms_step, 4), 'higher_is_better': True,
+        'scaling': scaling(a, world), 'vs_baseline': None, 'dtype': 'bf16',
+        'data': 'synthetic (seeded random-init INT8 weights, N(0,1) inputs)',
+        'config': config(a, world),
+        'workload_stats': {'active_experts_mean_per_layer': round(float(np.mean(active)), 1)},
         'roofline': roof, 'cpu_baseline': cpu, 'e2e': e2e,
-        'gpu_launches': (EP_LAUNCHES_PER_LAYER if use_ep else LAUNCHES_PER_LAYER) * a.layers * a.steps,
+        'gpu_launches': gpu_launches,
         'clocks': clk.summary(),
     }
+    if check is not None:
+        line['check'] = check
     if extra:
         line['extra'] = extra
     if rank == 0:
@@ -451,65 +559,124 @@ def dense_leg(dev, peaks, iters=20):
     return out
 
 
-def load_peaks():
-    p = os.path.join(ROOT, 'MEASURED_PEAKS.json')
-    if os.path.exists(p):
-        d = json.load(open(p))
-        return {'hbm': float(d['hbm_gbs']), 'tc': float(d['bf16_tflops']),
-                'tc_sustained': float(d.get('bf16_tflops_sustained', d['bf16_tflops'])),
-                'src': 'measured (MEASURED_PEAKS.json, sustained bf16)'}
-    return {'hbm': 6650.0, 'tc': 1590.0, 'tc_sustained': 1400.0, 'src': 'fallback'}
+def ep_single_gpu_leg(a, layers, dev, steps=3, warmup=2):
+    """C5 at one GPU: the expert-parallel benchmark's whole job (``--total-tokens``
+    through the same layers) on this GPU through ``gpu_routes.moe_block`` -- the t1 of
+    the scaling efficiency t1 / (N * tN) of the N-GPU expert-parallel runs."""
+    from localmoe35ba3b_b200.runtime import gpu_routes
+    tokens = a.total_tokens
+    x0, ids, wts = make_routing(a.layers, tokens, dev, a.seed + 555)
+
+    def step():
+        x = x0
+        for l, (bank, shared, gate) in enumerate(layers):
+            x = gpu_routes.moe_block(x, wts[l], ids[l], bank, shared=shared, shared_gate_weight=gate, residual=x)
+        return x
+
+    for _ in range(warmup):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del x0, ids, wts
+    return {'tokens': tokens, 'layers': a.layers, 'ms_per_step': round(ms, 3),
+            'tok_per_s': round(tokens / (ms / 1e3), 1), 'us_per_layer': round(ms * 1e3 / a.layers, 2),
+            'workload': f'{tokens} tokens x {a.layers} layers on 1 GPU (moe_block; all 256 experts), the '
+                        'expert-parallel job at N = 1'}
 
 
 # ------------------------------------------------------------------ CPU legs
-def cpu_baseline_leg(repeats=3):
+def _bf16_np(t):
+    return t.float().cpu().numpy()
+
+
+def cpu_baseline_leg(layer, x, ids, wts, dev, repeats=3):
+    """The reference's CPU path (HF experts loop, fp32 dequantise-then-matmul, plus the
+    gated shared expert) on layer 0 of this run's own weights and all of its tokens,
+    timed on the host cores; its output is also the fp32 check of the GPU block on the
+    same inputs (max-abs-normalised error, the north-star's 1e-2 bar)."""
+    from localmoe35ba3b_b200.runtime import gpu_routes
     from oracle import cpu_baseline as C
-    case = C.make_case(tokens=256)
+    (qg, sg, qd, sd), shared, gate = layer
+    gpu = gpu_routes.moe_block(x, wts, ids, [qg, sg, qd, sd], shared=shared, shared_gate_weight=gate)
+    torch.cuda.synchronize()
+    case = (x.float().cpu(), ids.cpu(), wts.cpu(), tuple(t.cpu() for t in (qg, sg, qd, sd)),
+            [(q.cpu(), s.cpu()) for q, s in shared], gate.float().cpu())
     t, threads = C.time_layer(case, repeats=repeats)
-    return {'value': round(256 / (t * 40), 2), 'unit': UNIT, 'cores': threads, 'kind': 'port',
-            'sample': f'1 MoE layer (256 experts top-8 + shared), 256 tokens, torch fp32 dequantise-then-matmul '
-                      f'(HF experts loop), median of {repeats}, scaled to 40 layers; CPU: {C.cpu_model()}'}
-
-
-def workload(a):
-    """The workload name both arms report in ``config``."""
-    return (f'prefill chunk: {a.tokens} tokens x {a.layers} layers, 256 experts top-8 + shared, '
-            'hidden 2048, moe_intermediate 512, INT8 g128 FP32 scales, Zipf(1.1) routing')
+    with torch.no_grad():
+        ref = C.moe_block(*case).numpy()
+    got = _bf16_np(gpu)
+    err = float(np.abs(got - ref).max() / np.abs(ref).max())
+    tokens = x.shape[0]
+    cpu = {'value': round(tokens / (t * 40), 2), 'unit': UNIT, 'cores': threads, 'kind': 'port',
+           'sample': f'all {tokens} tokens through layer 0 (1 of the 40 layers) of this run\'s weights per repeat, '
+                     f'median of {repeats} after 1 warm-up, tok/s = tokens / (40 x layer time); torch fp32 '
+                     f'dequantise-then-matmul (HF experts loop + shared expert); CPU: {C.cpu_model()}',
+           'layer_s': round(t, 4)}
+    check = {'what': 'GPU moe_block vs the CPU fp32 dequantise-then-matmul block, layer 0, all tokens',
+             'max_abs_norm_err': err, 'tol': 1e-2, 'ok': err < 1e-2}
+    return cpu, check
 
 
 def run_reference(a, rank, world):
+    """The reference arm: the reference's CPU path (HF experts loop on fp32-dequantised
+    INT8 weights + the shared expert; the oracle port, oracle/cpu_baseline.py) on all the
+    host cores.  Each step is one MoE layer over ALL the job's tokens (2048, or the
+    expert-parallel job's total): a sample of 1 of the job's layers, every layer being
+    the same work; tok/s = tokens / (layers x layer time)."""
     if rank != 0:
         return
     from oracle import cpu_baseline as C
-    case = C.make_case(tokens=256)
+    total, _ = job_tokens(a, world)
+    case = C.make_case(tokens=total, seed=a.seed)
+    threads = os.cpu_count()
     for _ in range(a.warmup):
-        C.time_layer(case, repeats=1)
-    t0 = time.perf_counter()
+        C.time_layer(case, repeats=1, threads=threads, warmup=False)
+    times = []
     for _ in range(a.steps):
-        t, threads = C.time_layer(case, repeats=1)
-    wall = time.perf_counter() - t0
-    # each step times one layer of 256 tokens; tok/s of the whole workload = 256 tokens
-    # per (layer time x layers), and a workload step (a.tokens through a.layers) is
-    # a.tokens / value seconds
-    value = 256 * a.steps / (wall * a.layers)
+        t, threads = C.time_layer(case, repeats=1, threads=threads, warmup=False)
+        times.append(t)
+    t_layer = float(np.mean(times))
+    value = total / (a.layers * t_layer)
     print(json.dumps({
         'impl': 'reference', 'metric': METRIC, 'value': round(value, 2), 'unit': UNIT, 'n_gpus': world,
-        'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(a.tokens / value * 1e3, 2),
-        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+        'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(t_layer * 1e3, 2),
+        'higher_is_better': True, 'scaling': scaling(a, world), 'vs_baseline': None, 'dtype': 'f32',
         'data': 'synthetic (seeded random-init INT8 weights, N(0,1) inputs)',
-        'config': {'workload': workload(a), 'tokens_per_gpu': a.tokens, 'layers': a.layers,
-                   'parallelism': 'host CPU (the oracle port of the reference path)',
-                   'l2': 'not applicable (host CPU)'},
+        'config': config(a, world),
         'cpu_baseline': {'value': round(value, 2), 'unit': UNIT, 'cores': threads, 'kind': 'port',
-                         'sample': f'256 tokens x 1 MoE layer per step, scaled to {a.layers} layers (HF experts '
-                                   f'loop, fp32 dequantised weights, torch on {threads} host threads; CPU: '
-                                   f'{C.cpu_model()})'},
+                         'sample': f'each step = all {total} tokens through 1 MoE layer (1 of the {a.layers}; '
+                                   f'ms_per_step is that layer), tok/s = tokens / ({a.layers} x mean layer time); '
+                                   f'HF experts loop, fp32 dequantised weights, torch on {threads} host threads; '
+                                   f'CPU: {C.cpu_model()}'},
         'e2e': {'value': round(value, 2), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }), flush=True)
 
 
+def run_only(a):
+    """One extra leg on its own (no prefill timing): the profiling entry point."""
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    peaks = load_peaks()
+    if a.only == 'c4':
+        out = dense_leg(dev, peaks)
+    else:
+        layers = make_layers(a.layers, dev, a.seed)
+        out = (decode_leg(layers, dev, peaks, max(3, a.steps), a.warmup, a.seed) if a.only == 'c3'
+               else ep_single_gpu_leg(a, layers, dev))
+    print(json.dumps({'only': a.only, 'layers': a.layers, a.only: out}), flush=True)
+
+
 def main():
     a = parse()
+    if a.only is not None and a.impl == 'ours':
+        run_only(a)
+        return
     if a.impl == 'reference':
         rank = int(os.environ.get('RANK', '0'))
         run_reference(a, rank, a.gpus)

@@ -9,9 +9,11 @@
  *    [I, 2I) are up;
  *  - activations are bf16 (dtype LMOE_BF16) or fp16 (LMOE_F16);
  *  - `stream` is a cudaStream_t passed as void*; work is enqueued on it with
- *    no host synchronisation, so every call can be captured in a CUDA graph;
+ *    no host synchronisation, so the calls can be captured in a CUDA graph
+ *    (this does not cover lmoe_routed_moe_noalloc, which makes no such promise);
  *  - no entry point allocates device memory: scratch ("workspace") buffers are
- *    passed in by the caller, sized by the *_workspace_size functions;
+ *    passed in by the caller, sized by the *_workspace_size functions
+ *    (lmoe_routed_moe_noalloc uses a fixed array inside the library instead);
  *  - the return value is LMOE_OK or a negative LMOE_ERR_* code (invalid
  *    geometry or a CUDA launch error); nothing aborts or traps.  Device-side
  *    bounded waits that give up set LMOE_DEVERR_* bits in the caller's
@@ -131,15 +133,18 @@ LMOE_API int lmoe_routed_moe(const void* x, const float* weights, const int64_t*
 
 /* Allocation-free form of lmoe_routed_moe (no counterpart in the reference: the reference
  * runtime allocates its own buffers with torch).  For callers that cannot allocate device
- * memory where they run the block -- inside CUDA-graph stream capture, under a fixed arena
- * owned by a host runtime, or from a C/FFI host with no device allocator.  Same arguments
- * as lmoe_routed_moe without ws/stage_events; scratch is a file-scope device array of
+ * memory where they run the block: host runtimes that hand out device memory only from a
+ * fixed, pre-sized arena they keep to themselves, and C/FFI hosts that link this library
+ * with no device allocator of their own.  Same arguments as lmoe_routed_moe without
+ * ws/stage_events; the scratch is a file-scope device array of
  * lmoe_routed_moe_noalloc_limit() bytes (16 MiB) that each GPU using the library keeps for
  * the life of the process.  Returns LMOE_ERR_UNSUPPORTED when lmoe_moe_workspace_size()
  * for the call exceeds that limit (at hidden 2048, inter 512, top 8 and 256 experts about 200
- * tokens fit; 256 do not).  The first call on a device looks up the array's device address (this may
- * load the module): make it before any stream capture.  All calls share the array, so calls
- * that overlap on the GPU (different streams, or different threads) race: serialise them. */
+ * tokens fit; 256 do not), LMOE_ERR_INVALID for hidden or inter above 2^20.  The first call
+ * in each CUDA context (per device) looks up the array's device address, which may load the
+ * module: make it before any stream capture.  All calls share the array and a call leaves
+ * its contents behind, so calls that overlap on the GPU (different streams, or different
+ * threads) race: serialise them. */
 LMOE_API int64_t lmoe_routed_moe_noalloc_limit(void);
 LMOE_API int lmoe_routed_moe_noalloc(const void* x, const float* weights, const int64_t* ids, int64_t tokens,
                             int64_t top, const int8_t* qg, const float* sg, const int8_t* qd, const float* sd,
@@ -182,33 +187,55 @@ LMOE_API int lmoe_decode_moe(const void* x, const float* weights, const int64_t*
 LMOE_API int lmoe_router_topk(const void* logits, int64_t tokens, int64_t experts, int64_t top, float* weights,
                               int64_t* ids, float* probs, int dtype, void* stream);
 
-/* Expert-parallel dispatch rows.  The reference runs the block on one GPU, so these
- * replace no reference call: they pack and unpack the rows that the sharded block
- * exchanges over all_to_all before the owner's routed experts (gpu_routes.routed_moe,
- * runtime/gpu_routes.py:66-82) read them.  A packed row is
- *   [payload | route ids int32 x top | route weights fp32 x top]
- * with payload = the hidden row in the activation dtype (wire LMOE_WIRE_DTYPE) or its
- * W8A8 activation quantisation, int8 [hidden] then fp32 scales [hidden/128], exactly as
- * lmoe_quantize_rows (w8a8.quantize, operators/w8a8.py:8-22) computes it (LMOE_WIRE_INT8).
- * hidden % 128 == 0, 0 <= top <= 32. */
-#define LMOE_WIRE_DTYPE 0
-#define LMOE_WIRE_INT8 1
-/* Bytes of one packed row, or LMOE_ERR_INVALID. */
-LMOE_API int64_t lmoe_ep_row_bytes(int64_t hidden, int64_t top, int wire, int dtype);
-/* out [rows, lmoe_ep_row_bytes] row r = pack(x[tok[r]], route_ids[r], route_w[r]);
- * x [tokens, hidden], tok [rows] int64, route_ids [rows, top] int32, route_w [rows, top]
- * fp32.  A tok outside [0, tokens) writes a zero payload and sets LMOE_DEVERR_BAD_INDEX.
- * x 8-byte aligned; out 4-byte (int8 wire) or 8-byte aligned. */
-LMOE_API int lmoe_ep_pack_rows(const void* x, int64_t tokens, const int64_t* tok, const int32_t* route_ids,
-                               const float* route_w, int64_t rows, int64_t hidden, int64_t top, int wire,
-                               void* out, int dtype, int* err, void* stream);
-/* y [routes, hidden] row r = the payload of packed row row_of[r] (row r when row_of is
- * NULL) of buf [rows, lmoe_ep_row_bytes], an int8 payload as round_dtype(float(q) * s)
- * per 128-column group.  A row_of outside [0, rows) writes zeros and sets
- * LMOE_DEVERR_BAD_INDEX.  y 8-byte aligned; buf 4-byte (int8 wire) or 8-byte aligned. */
-LMOE_API int lmoe_ep_unpack_rows(const void* buf, int64_t rows, const int64_t* row_of, int64_t routes,
-                                 int64_t hidden, int64_t top, int wire, void* y, int dtype, int* err,
-                                 void* stream);
+#define LMOE_WIRE_DTYPE 0 /* expert-parallel dispatch payload: the hidden row in the activation dtype */
+#define LMOE_WIRE_INT8 1  /* ... or its W8A8 activation quantisation (w8a8.quantize, operators/w8a8.py:8-22) */
+
+/* Expert-parallel MoE layer with fixed-size exchanges (no host synchronisation
+ * inside a layer).  The reference runs the whole block on one GPU
+ * (gpu_routes.routed_moe, qwen35_deploy/runtime/gpu_routes.py:66-82, inside the HF
+ * block, modeling_qwen3_5_moe.py:781-792): these three calls split that block
+ * around two all_to_all exchanges of equal-sized segments, which the caller runs
+ * (NCCL).  `experts` is the global expert count E, sharded over `world` ranks
+ * (1..8) in contiguous blocks of E / world; every rank uses the same `cap`
+ * (>= its tokens) so that all segments have the same size.
+ *
+ * 1. lmoe_ep_dispatch: from this rank's x [tokens, hidden], ids [tokens, top]
+ *    (global expert ids) and weights [tokens, top] fp32, fills send
+ *    [world][cap + 1][row_bytes]: segment d, row 0 = header (row count, routes
+ *    per local expert of rank d), rows 1.. = one packed row per token with a
+ *    route to rank d (tokens ascending): [payload | local ids int32 x top |
+ *    weights fp32 x top | ranks int32 x top], the payload being the hidden row
+ *    (wire LMOE_WIRE_DTYPE) or its W8A8 activation quantisation (LMOE_WIRE_INT8).
+ *    plan_ws: lmoe_ep_plan_workspace_size bytes, read again by lmoe_ep_fold.
+ * 2. all_to_all(recv, send), equal splits.
+ * 3. lmoe_ep_owner: this rank's experts (banks [E/world, ...]) on the received
+ *    rows, plus the shared expert on its own x; partial [world][cap][hidden] = per
+ *    received row the ordered sum of its routes' round(round(down) * w).
+ *    ws: lmoe_ep_owner_workspace_size bytes (256-byte aligned), read again by
+ *    lmoe_ep_fold.  stage_events (nullable): 5 cudaEvent_t recorded before the
+ *    metadata, after the scatter, after gate_up, after down and after the combine.
+ * 4. all_to_all(back, partial), equal splits.
+ * 5. lmoe_ep_fold: out [tokens, hidden] = the returned rows in ascending rank
+ *    order, + round(sigmoid(round(x . sh_gate_w)) * shared expert) when
+ *    with_shared, + residual.
+ * hidden % 256 == 0, inter % 128 == 0, 1 <= top <= 16. */
+LMOE_API int64_t lmoe_ep_layer_row_bytes(int64_t hidden, int64_t top, int wire);
+LMOE_API int64_t lmoe_ep_plan_workspace_size(int64_t tokens, int64_t top, int64_t world);
+LMOE_API int64_t lmoe_ep_owner_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t world,
+                                              int64_t cap, int64_t hidden, int64_t inter);
+LMOE_API int lmoe_ep_dispatch(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
+                              int64_t experts, int64_t world, int64_t cap, int64_t hidden, int wire, int dtype,
+                              void* send, void* plan_ws, int* err, void* stream);
+LMOE_API int lmoe_ep_owner(const void* recv, const void* x, int64_t tokens, int64_t top, int64_t experts,
+                           int64_t world, int64_t cap, int64_t hidden, int64_t inter, int wire, const int8_t* qg,
+                           const float* sg, const int8_t* qd, const float* sd, const int8_t* sh_qg,
+                           const float* sh_sg, const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd,
+                           const float* sh_sd, void* ws, void* partial, int dtype, int* err, void** stage_events,
+                           void* stream);
+LMOE_API int lmoe_ep_fold(const void* back, const void* plan_ws, const void* x, int64_t tokens, int64_t top,
+                          int64_t experts, int64_t world, int64_t cap, int64_t hidden, int64_t inter,
+                          const void* owner_ws, int with_shared, const void* sh_gate_w, const void* residual,
+                          void* out, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

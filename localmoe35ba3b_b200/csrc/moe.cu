@@ -233,37 +233,66 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
 // Allocation-free variant of lmoe_routed_moe.
 //
 // Some callers cannot allocate device memory at the point where they run the
-// MoE block: code executing while a CUDA graph is being captured (allocation
-// calls are not capturable), runtimes that hand out device memory only from a
-// fixed, pre-sized arena they do not expose to plug-ins, and C/FFI hosts that
-// link this library without any device allocator of their own.  For them the
+// MoE block: host runtimes that hand out device memory only from a fixed,
+// pre-sized arena they do not expose to plug-ins, and C/FFI hosts that link
+// this library without any device allocator of their own.  For them the
 // scratch space lives in a file-scope __device__ array of a fixed size,
 // kNoAllocScratchBytes, which every GPU that loads this library keeps for
 // the life of the process.
 namespace lmoe {
 constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // 16 MiB per device
+constexpr int64_t kNoAllocMaxDim = int64_t(1) << 20;        // hidden, inter: keeps the size products in range
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 }  // namespace lmoe
 
 #include <mutex>
 
-// Device address of the scratch array for the current device.  Host code
-// cannot use the array's name as a pointer (it is a host-side stand-in), so
-// the address is looked up once per device, with that device current, and
-// cached.  That first lookup may load the module on the device: make the
-// first call on each device before any stream capture begins.
+// Device address of the scratch array in the calling thread's current CUDA
+// context.  Host code cannot use the array's name as a pointer (it is a
+// host-side stand-in), so the address is looked up with cudaGetSymbolAddress,
+// with the caller's device current, the first time a context calls, and cached
+// per (context, device).  That first lookup may load the module on the device:
+// make the first call on each device (or context) before any stream capture.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = []() -> CtxGetCurrentFn {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return (CtxGetCurrentFn)f;
+    return nullptr;
+  }();
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
 static void* noalloc_scratch() {
+  struct Entry {
+    CUcontext ctx;
+    int dev;
+    void* ptr;
+  };
   static std::mutex mu;
-  static void* ptrs[128] = {};
+  static Entry cache[64] = {};
+  static int next = 0;
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (ptrs[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, lmoe::g_noalloc_scratch) != cudaSuccess) return nullptr;
-    ptrs[dev] = p;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return nullptr;
+  // cudaSetDevice makes the device's primary context current when the thread has none yet
+  CUcontext ctx = current_context();
+  if (ctx == nullptr) {
+    if (cudaSetDevice(dev) != cudaSuccess) return nullptr;
+    ctx = current_context();
   }
-  return ptrs[dev];
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : cache)
+    if (e.ptr != nullptr && e.ctx == ctx && e.dev == dev) return e.ptr;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, lmoe::g_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
+  cache[next] = Entry{ctx, dev, p};
+  next = (next + 1) % 64;
+  return p;
 }
 
 extern "C" int64_t lmoe_routed_moe_noalloc_limit(void) { return lmoe::kNoAllocScratchBytes; }
@@ -276,6 +305,9 @@ extern "C" int lmoe_routed_moe_noalloc(const void* x, const float* weights, cons
                                        const void* sh_gate_w, const void* residual, void* out, int dtype, int* err,
                                        void* stream) {
   if (tokens <= 0 || top < 0 || (top == 0 && sh_qg == nullptr) || experts <= 0 || hidden <= 0 || inter <= 0)
+    return LMOE_ERR_INVALID;
+  if (tokens > (int64_t(1) << 30) || top > 64 || experts > (int64_t(1) << 20) || hidden > lmoe::kNoAllocMaxDim ||
+      inter > lmoe::kNoAllocMaxDim)
     return LMOE_ERR_INVALID;
   // every byte of the scratch that a call reads is written earlier in the same
   // call, so nothing needs clearing between calls

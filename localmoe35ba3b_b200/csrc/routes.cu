@@ -14,11 +14,10 @@
 // the same pass, so `ordered`/`slots` need no second pass over `inverse`.
 #include "common.cuh"
 #include "routes.cuh"
+#include "routes_dev.cuh"
 
 namespace lmoe {
 
-constexpr int kRouteThreads = 1024;
-constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kMaxTop = 32;
 constexpr int kBatch = 16;  // ids held per lane per batch
 
@@ -43,31 +42,6 @@ __device__ __forceinline__ int route_bucket(int64_t v, int E, int* err) {
   return (int)v;
 }
 
-// inclusive block scan over kRouteThreads values (one per thread)
-__device__ int block_incl_scan(int v, int* warp_tot) {
-  const int lane = lane_id(), warp = warp_id();
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int u = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += u;
-  }
-  if (lane == 31) warp_tot[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    int t = warp_tot[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, t, o);
-      if (lane >= o) t += u;
-    }
-    warp_tot[lane] = t;
-  }
-  __syncthreads();
-  const int r = v + (warp > 0 ? warp_tot[warp - 1] : 0);
-  __syncthreads();
-  return r;
-}
-
 struct RouteArgs {
   const int64_t* ids;
   const float* weights;  // nullable: [T, top] fp32 routing weights
@@ -89,55 +63,6 @@ struct RouteArgs {
   int max_tiles_ref;
   int* err;
 };
-
-// Tile list of the fused path (experts by descending route count, ties by lower
-// id; the shared expert's T rows are expert E when present) and the header.
-// Called by all kRouteThreads threads; s_first[e] = first sorted slot of expert e,
-// s_first[E + 1] = R.
-__device__ void write_tiles(const RouteArgs& a, const int* s_first, int R, int* warp_tot) {
-  __shared__ int s_total_tiles;
-  const int E = a.E;
-  const int Es = E + (a.with_shared ? 1 : 0);
-  const int e = threadIdx.x;
-  int cnt = 0, ntl = 0, rank = 0;
-  if (e < Es) {
-    cnt = (e < E) ? (s_first[e + 1] - s_first[e]) : a.T;
-    ntl = (cnt + kTileRoutes - 1) / kTileRoutes;
-    for (int o = 0; o < Es; ++o) {
-      const int co = (o < E) ? (s_first[o + 1] - s_first[o]) : a.T;
-      rank += (co > cnt) || (co == cnt && o < e);
-    }
-  }
-  __shared__ int s_by_rank[1025];
-  if (e < Es) s_by_rank[rank] = ntl;
-  __syncthreads();
-  const int r_ntl = (e < Es) ? s_by_rank[e] : 0;  // thread e now holds rank e's tile count
-  const int r_incl = block_incl_scan(r_ntl, warp_tot);
-  __shared__ int s_tile_first[1025];
-  if (e < Es) s_tile_first[e] = r_incl - r_ntl;
-  if (e == Es - 1) s_total_tiles = r_incl;
-  __syncthreads();
-  if (e < Es) {
-    const int t0 = s_tile_first[rank];
-    const int start0 = (e < E) ? s_first[e] : R;
-    for (int j = 0; j < ntl; ++j) {
-      Tile tl;
-      tl.expert = e;
-      tl.start = start0 + j * kTileRoutes;
-      tl.count = min(kTileRoutes, cnt - j * kTileRoutes);
-      tl.pad = 0;
-      a.tiles[t0 + j] = tl;
-    }
-  }
-  if (threadIdx.x == 0) {
-    a.hdr[kHdrNumTiles] = s_total_tiles;
-    a.hdr[kHdrRoutes] = R;
-    a.hdr[kHdrTokens] = a.T;
-    a.hdr[kHdrExperts] = E;
-    a.hdr[kHdrShared] = a.with_shared;
-    a.hdr[kHdrValid] = s_first[E];
-  }
-}
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   extern __shared__ int cw[];  // [kRouteWarps][E+1] counts, then first slots
@@ -246,7 +171,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __syncthreads();
 
   // fused-path tiles, experts ordered by descending count (ties: lower id first)
-  if (a.tiles != nullptr) write_tiles(a, s_first, R, warp_tot);
+  if (a.tiles != nullptr) write_tile_list(a.E, a.T, a.with_shared, s_first, R, R, a.tiles, a.hdr, warp_tot);
 
   // reference table: ends = cumsum(ceil(count / bm)) in expert-id order
   if (a.table64 != nullptr) {
@@ -331,7 +256,7 @@ __global__ void __launch_bounds__(kRouteThreads) meta_scan_kernel(RouteArgs a, i
   if (a.with_shared)
     for (int t = threadIdx.x; t < a.T; t += kRouteThreads) a.pos32[R + t] = t;
   __syncthreads();
-  write_tiles(a, s_first, R, warp_tot);
+  write_tile_list(E, a.T, a.with_shared, s_first, R, R, a.tiles, a.hdr, warp_tot);
 }
 
 __global__ void __launch_bounds__(kMetaChunk) meta_place_kernel(RouteArgs a, const int32_t* __restrict__ cc) {

@@ -1,42 +1,46 @@
 """Expert parallelism for the routed MoE block over ``torch.distributed``.
 
 The reference runs on one GPU (its experts stream over PCIe); on B200s the
-256 experts shard by contiguous blocks across G GPUs (rank g owns experts
-``[g*E/G, (g+1)*E/G)``) and each rank keeps its own tokens.  One layer:
+256 experts shard by contiguous blocks across G ranks (rank g owns experts
+``[g*E/G, (g+1)*E/G)``) and each rank keeps its own tokens.  The sequence of one
+layer:
 
-1. ``plan``: every (token, destination rank) pair with at least one route to
-   that rank becomes one send row -- the token's hidden row plus its routes
-   for that rank (local expert ids, routing weights; unused slots -1 / 0).
-   Rows are grouped by destination rank, tokens ascending.
-2. ``all_to_all_single`` of the row counts, then ONE of the packed send rows
-   (NCCL on GPUs, gloo on CPU).  A packed row is ``[payload | route ids int32
-   x top | route weights fp32 x top]`` as bytes; the payload is the hidden row
-   itself (``wire='bf16'``) or, with ``wire='int8'``, its W8A8 activation
-   quantisation (int8 [H] + fp32 scales [H/128], operators/w8a8.py:8-22):
-   2,112 instead of 4,096 bytes at H = 2048.  The owner dequantises an int8
-   row to ``round_dtype(q * s)`` before its experts read it.
-3. The owner runs its routed experts on the received rows with their route
-   lists (``gpu_routes.moe_block``; -1 slots, routed to other ranks, are
-   skipped: gate_up + SwiGLU, down, ``round(round(v) * w)``), whose ordered
-   combine pre-reduces each row's routes in ascending expert order:
-   ``acc = round(acc + v)``.
-4. The reverse ``all_to_all_single`` returns one row per (token, rank).
-5. Each token folds its returned rows in ascending rank order (= ascending
-   expert order, the shards are contiguous), adds its gated shared expert
-   (computed locally -- the shared expert and the gate are replicated -- while
-   the dispatch exchange of step 2 is in flight) and the residual.
+1. every (token, destination rank) pair with at least one route to that rank
+   becomes one send row -- the token's hidden row plus its routes for that
+   rank (local expert ids, routing weights; unused slots -1 / 0), rows grouped
+   by destination rank, tokens ascending;
+2. an all-to-all carries the rows; the payload is the hidden row itself
+   (``wire='bf16'``) or, with ``wire='int8'``, its W8A8 activation
+   quantisation (int8 [H] + fp32 scales [H/128], operators/w8a8.py:8-22),
+   2,112 instead of 4,096 bytes at H = 2048, which the owner dequantises to
+   ``round_dtype(q * s)`` before its experts read it;
+3. the owner runs its experts on the received rows (gate_up + SwiGLU, down,
+   ``round(round(v) * w)``) and pre-reduces each row's routes in ascending
+   expert order, ``acc = round(acc + v)``;
+4. the reverse all-to-all returns one row per (token, rank);
+5. each token folds its returned rows in ascending rank order (= ascending
+   expert order: the shards are contiguous), then adds its gated shared
+   expert (the shared expert and the gate are replicated) and the residual.
 
 The rounding sequence equals the reference's single chain
 (int8.py:245-249, prefill.py:44-46) except at the rank boundaries, where a
 pre-reduced partial sum is added instead of its terms one by one; the results
-stay within the 1e-2 bar (tests/test_ep.py checks both the bound and the exact
-EP sequence against the oracle).  The int8 wire adds the activation
-quantisation error of the routed experts' input (the shared expert reads the
-local bf16 row); the return trip always carries the dtype rows.
+stay within the 1e-2 bar.
 
-The compute is injected (``local_moe(x, weights, ids)`` and
-``shared_part(x)``), so the same orchestration runs the GPU kernels in the
-product and oracle functions in the CPU multi-process tests.
+Two implementations of that sequence:
+
+* ``GpuLayer`` / ``moe_forward_gpu`` -- the product path on B200s.  Five steps
+  per layer with every exchange size fixed in advance, so a layer has no host
+  synchronisation: ``lmoe_ep_dispatch`` (plan + pack, 2 kernels), an equal-split
+  ``all_to_all_single`` of W segments of ``cap + 1`` rows (row 0 of a segment
+  is its header: row count and routes per local expert), ``lmoe_ep_owner``
+  (the owner's metadata, scatter, the two grouped GEMMs with the shared
+  expert's own-token tiles folded in, the ordered combine: 5 kernels), the
+  return ``all_to_all_single``, ``lmoe_ep_fold`` (1 kernel).
+* ``moe_forward`` -- the same sequence with variable-size exchanges and
+  injected compute (``local_moe(x, weights, ids)``, ``shared_part(x)``), which
+  the CPU multi-process tests (gloo) run with oracle functions to check the
+  orchestration and the rounding sequence.
 """
 import torch
 import torch.distributed as dist
@@ -185,40 +189,6 @@ def unpack_rows(buf, h, top, wire, dtype):
     return (rows.reshape(n, h), *route_fields(buf, h, top, wire, dtype))
 
 
-def _wire_code(wire):
-    from .. import _native as N
-    return N.WIRE_INT8 if wire == 'int8' else N.WIRE_DTYPE
-
-
-def pack_rows_gpu(x, tok, route_ids, route_w, wire):
-    """``pack_rows(x[tok], ...)`` in one kernel (``lmoe_ep_pack_rows``): gather, W8A8
-    quantisation on the int8 wire, route ids and weights."""
-    from .. import _native as N
-    x, tok = x.contiguous(), tok.to(torch.int64).contiguous()
-    route_ids = route_ids.to(torch.int32).contiguous()
-    route_w = route_w.to(torch.float32).contiguous()
-    n, top = route_ids.shape
-    h = x.shape[-1]
-    out = torch.empty((n, wire_row_bytes(h, top, wire, x.element_size())), dtype=torch.uint8, device=x.device)
-    N.call('lmoe_ep_pack_rows', N.ptr(x), x.shape[0], N.ptr(tok), N.ptr(route_ids), N.ptr(route_w), n, h, top,
-           _wire_code(wire), N.ptr(out), N.dtype_code(x.dtype), N.ptr(N.error_word(x.device)), N.stream(x.device))
-    return out
-
-
-def unpack_rows_gpu(buf, row_of, h, top, wire, dtype):
-    """Payload of packed row ``row_of[r]`` (row r when ``row_of`` is None) as
-    activation row r, in one kernel (``lmoe_ep_unpack_rows``; the int8 wire
-    dequantised to ``round_dtype(q * s)``)."""
-    from .. import _native as N
-    if row_of is not None:
-        row_of = row_of.to(torch.int64).contiguous()
-    n = buf.shape[0] if row_of is None else row_of.numel()
-    y = torch.empty((n, h), dtype=dtype, device=buf.device)
-    N.call('lmoe_ep_unpack_rows', N.ptr(buf.contiguous()), buf.shape[0], N.ptr(row_of), n, h, top,
-           _wire_code(wire), N.ptr(y), N.dtype_code(dtype), N.ptr(N.error_word(buf.device)), N.stream(buf.device))
-    return y
-
-
 def prereduced(route_fn):
     """A ``local_moe`` built from a one-route-per-row expert function
     ``route_fn(x_rows [R', H], w [R', 1], ids [R', 1]) -> [R', H]``: the received
@@ -241,20 +211,20 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     runs this rank's experts on the received rows: ids are local expert ids,
     -1 where the slot routes to another rank, and row i of the result is
     ``acc = round(acc + round(round(down_e(x_i)) * w))`` over the row's routes in
-    ascending expert order (``gpu_local_moe``: the routed block itself;
-    ``prereduced``: the same from a one-route-per-row function).
+    ascending expert order (``prereduced`` builds one from a one-route-per-row
+    function).
     ``shared_part(x) -> [T, H]`` is round(sigmoid(gate) * shared_expert(x)) (or None).  ``wire`` is the format
     of the dispatched hidden rows ('bf16': the rows as they are; 'int8': W8A8
-    activation quantisation).  CUDA tensors pack and unpack through the library
-    kernels; CPU ranks (gloo) pack with torch and quantise through ``quantize``
-    (``rows -> (q int8 [n, H], s fp32 [n, H/128])``)."""
+    activation quantisation, through ``quantize``: ``rows -> (q int8 [n, H], s fp32
+    [n, H/128])``).  Rows are packed with torch byte views; the product path on
+    GPUs is ``moe_forward_gpu``."""
     if wire not in WIRES:
         raise ValueError("wire must be 'bf16' or 'int8'")
     h = x.shape[-1]
     if h % GROUP:
         raise ValueError('hidden size must be a multiple of 128')
-    if wire == 'int8' and not x.is_cuda and quantize is None:
-        raise ValueError('the int8 wire on CPU ranks needs a quantize function')
+    if wire == 'int8' and quantize is None:
+        raise ValueError('the int8 wire needs a quantize function')
     world = dist.get_world_size(group)
     # 1. counts: computed and exchanged on the device, then read once (the layer's one
     #    host synchronisation: the exchange sizes must be known on the host)
@@ -265,13 +235,10 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     sc, rc = counts[:world], counts[world:]
     n_recv, top = sum(rc), ids.shape[1]
     route_tok, route_ids, route_w = plan_rows(ids, weights, experts, dest, mask, sum(sc))
-    # 2. packed rows: payload, route ids and weights in one exchange (on the GPU one
-    #    kernel gathers, quantises and packs; CPU ranks pack with torch byte views)
+    # 2. packed rows: payload, route ids and weights in one exchange
     n_send = route_tok.numel()
     row_bytes = wire_row_bytes(h, top, wire, x.element_size())
-    if x.is_cuda:
-        send_buf = pack_rows_gpu(x, route_tok, route_ids, route_w, wire)
-    elif n_send:
+    if n_send:
         send_buf = pack_rows(x[route_tok].contiguous(), route_ids, route_w, wire, quantize)
     else:
         send_buf = torch.empty((0, row_bytes), dtype=torch.uint8, device=x.device)
@@ -283,13 +250,9 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     sh = shared_part(x) if shared_part is not None else None
     work.wait()
     # 3. local experts on the received rows, each row's routes pre-reduced in
-    #    ascending expert order (on GPUs the block's own ordered combine)
+    #    ascending expert order
     if n_recv:
-        if x.is_cuda:
-            recv_rows = unpack_rows_gpu(recv_buf, None, h, top, wire, x.dtype)
-            recv_ids, recv_w = route_fields(recv_buf, h, top, wire, x.dtype)
-        else:
-            recv_rows, recv_ids, recv_w = unpack_rows(recv_buf, h, top, wire, x.dtype)
+        recv_rows, recv_ids, recv_w = unpack_rows(recv_buf, h, top, wire, x.dtype)
         partial = local_moe(recv_rows, recv_w, recv_ids)
     else:
         partial = torch.zeros((0, h), dtype=x.dtype, device=x.device)
@@ -314,26 +277,135 @@ def moe_forward(x, weights, ids, experts, local_moe, shared_part=None, residual=
     return out
 
 
-def gpu_local_moe(banks):
-    """This rank's experts through the routed-MoE kernels on the received rows:
-    a -1 id is a slot routed elsewhere, which the block's routing metadata sorts
-    after every expert, gives no GEMM tile and leaves out of the ordered combine,
-    so the combine is the per-row pre-reduction."""
-    from . import gpu_routes
-
-    def run(x_rows, w, ids):
-        return gpu_routes.moe_block(x_rows, w, ids, banks)
-    return run
 
 
-def gpu_shared_part(banks, shared, shared_gate_weight):
-    """round(sigmoid(round(x . gate)) * shared_expert(x)) through the same library call
-    with no routed experts (top 0)."""
-    from . import gpu_routes
+# ---------------------------------------------------------------------------- GPU path
+class GpuLayer:
+    """Buffers and calls of one expert-parallel layer on this rank's GPU.
 
-    def run(x):
-        t = x.shape[0]
-        ids = torch.empty((t, 0), dtype=torch.int64, device=x.device)
-        w = torch.empty((t, 0), dtype=torch.float32, device=x.device)
-        return gpu_routes.moe_block(x, w, ids, banks, shared=shared, shared_gate_weight=shared_gate_weight)
-    return run
+    ``tokens`` rows per rank (every rank must use the same ``cap`` >= its token
+    count, default ``tokens``: the exchanges are equal-split), ``experts`` global
+    experts sharded over ``world`` ranks, ``top`` routes per token.  The buffers
+    are allocated once and reused by every layer and step of the same geometry:
+    ``send``/``recv`` ``[world * (cap + 1) * row_bytes]`` bytes, ``partial``/``back``
+    ``[world * cap, hidden]``, the plan and owner workspaces.
+    """
+
+    def __init__(self, tokens, top, experts, world, hidden, inter, dtype, device, wire='bf16', cap=None):
+        from .. import _native as N
+        if wire not in WIRES:
+            raise ValueError("wire must be 'bf16' or 'int8'")
+        self.N = N
+        self.tokens, self.top, self.experts, self.world = int(tokens), int(top), int(experts), int(world)
+        self.hidden, self.inter, self.dtype, self.wire = int(hidden), int(inter), dtype, wire
+        self.cap = int(cap if cap is not None else tokens)
+        self.device = torch.device(device)
+        self.wire_code = N.WIRE_INT8 if wire == 'int8' else N.WIRE_DTYPE
+        lib = N.lib()
+        self.row_bytes = lib.lmoe_ep_layer_row_bytes(self.hidden, self.top, self.wire_code)
+        ows = lib.lmoe_ep_owner_workspace_size(self.tokens, self.top, self.experts, self.world, self.cap,
+                                               self.hidden, self.inter)
+        pws = lib.lmoe_ep_plan_workspace_size(self.tokens, self.top, self.world)
+        if min(self.row_bytes, ows, pws) < 0:
+            raise ValueError('unsupported expert-parallel geometry')
+        seg = (self.cap + 1) * self.row_bytes
+        dev = self.device
+        self.send = torch.empty(self.world * seg, dtype=torch.uint8, device=dev)
+        self.recv = self.send if self.world == 1 else torch.empty_like(self.send)
+        self.plan_ws = torch.empty(pws, dtype=torch.uint8, device=dev)
+        self.owner_ws = torch.empty(ows, dtype=torch.uint8, device=dev)
+        self.partial = torch.empty((self.world * self.cap, self.hidden), dtype=dtype, device=dev)
+        self.back = self.partial if self.world == 1 else torch.empty_like(self.partial)
+
+    def _check(self, x, weights, ids):
+        if x.shape != (self.tokens, self.hidden) or x.dtype != self.dtype or not x.is_contiguous():
+            raise ValueError('x does not match the layer geometry')
+        if ids.shape != (self.tokens, self.top) or weights.shape != (self.tokens, self.top):
+            raise ValueError('routing does not match the layer geometry')
+
+    def dispatch(self, x, weights, ids):
+        """Fill ``send`` from this rank's tokens and their routing."""
+        N = self.N
+        self._check(x, weights, ids)
+        ids = ids if ids.dtype == torch.int64 else ids.long()
+        weights = weights if weights.dtype == torch.float32 else weights.float()
+        N.call('lmoe_ep_dispatch', N.ptr(x), N.ptr(weights.contiguous()), N.ptr(ids.contiguous()), self.tokens,
+               self.top, self.experts, self.world, self.cap, self.hidden, self.wire_code, N.dtype_code(self.dtype),
+               N.ptr(self.send), N.ptr(self.plan_ws), N.ptr(N.error_word(self.device)), N.stream(self.device))
+
+    def owner(self, x, banks, shared=None, stage_events=None):
+        """This rank's experts on ``recv`` (+ the shared expert on its own ``x``)
+        into ``partial``; ``banks`` hold the local experts ``[E / world, ...]``."""
+        import ctypes
+        N = self.N
+        qg, sg, qd, sd = banks
+        if qg.shape != (self.experts // self.world, 2 * self.inter, self.hidden):
+            raise ValueError('local expert bank does not match the layer geometry')
+        sh = [None] * 6
+        if shared is not None:
+            (qsg, ssg), (qsu, ssu), (qsd, ssd) = shared
+            sh = [qsg, ssg, qsu, ssu, qsd, ssd]
+        evs = None
+        if stage_events is not None:
+            for ev in stage_events:
+                ev.record()
+            evs = (ctypes.c_void_p * 5)(*[ctypes.c_void_p(ev.cuda_event) for ev in stage_events])
+        N.call('lmoe_ep_owner', N.ptr(self.recv), N.ptr(x), self.tokens, self.top, self.experts, self.world,
+               self.cap, self.hidden, self.inter, self.wire_code, N.ptr(qg), N.ptr(sg), N.ptr(qd), N.ptr(sd),
+               *[N.ptr(v) for v in sh], N.ptr(self.owner_ws), N.ptr(self.partial), N.dtype_code(self.dtype),
+               N.ptr(N.error_word(self.device)), evs, N.stream(self.device))
+        self.with_shared = shared is not None
+
+    def fold(self, x, shared_gate_weight=None, residual=None):
+        """Per token: the returned rows (``back``) in ascending rank order, the
+        gated shared expert computed by ``owner`` and the residual."""
+        N = self.N
+        out = torch.empty_like(x)
+        gate = None if shared_gate_weight is None else shared_gate_weight.to(self.dtype).contiguous()
+        N.call('lmoe_ep_fold', N.ptr(self.back), N.ptr(self.plan_ws), N.ptr(x), self.tokens, self.top, self.experts,
+               self.world, self.cap, self.hidden, self.inter, N.ptr(self.owner_ws), 1 if self.with_shared else 0,
+               N.ptr(gate), N.ptr(residual), N.ptr(out), N.dtype_code(self.dtype), N.stream(self.device))
+        return out
+
+    def exchange(self, out, inp, group=None):
+        if self.world > 1:
+            dist.all_to_all_single(out, inp, group=group)
+
+    def forward(self, x, weights, ids, banks, shared=None, shared_gate_weight=None, residual=None, group=None,
+                events=None):
+        """One expert-parallel layer for this rank's ``x [tokens, hidden]``.  ``events``
+        (optional): 6 CUDA events recorded around dispatch, the first exchange, the
+        owner, the return exchange and the fold."""
+        def mark(i):
+            if events is not None:
+                events[i].record()
+        mark(0)
+        self.dispatch(x, weights, ids)
+        mark(1)
+        self.exchange(self.recv, self.send, group)
+        mark(2)
+        self.owner(x, banks, shared)
+        mark(3)
+        self.exchange(self.back, self.partial, group)
+        mark(4)
+        out = self.fold(x, shared_gate_weight, residual)
+        mark(5)
+        return out
+
+
+_layers = {}
+
+
+def moe_forward_gpu(x, weights, ids, experts, banks, shared=None, shared_gate_weight=None, residual=None,
+                    group=None, wire='bf16', cap=None):
+    """Expert-parallel MoE block on this rank's GPU (``GpuLayer``, cached per
+    geometry): ``banks`` are this rank's experts ``[experts / world, ...]``,
+    ``shared``/``shared_gate_weight`` the replicated shared expert and its gate."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    t, top = ids.shape
+    key = (x.device, t, top, experts, world, x.shape[1], banks[2].shape[2], x.dtype, wire, cap)
+    layer = _layers.get(key)
+    if layer is None:
+        layer = _layers[key] = GpuLayer(t, top, experts, world, x.shape[1], banks[2].shape[2], x.dtype, x.device,
+                                        wire, cap)
+    return layer.forward(x.contiguous(), weights, ids, banks, shared, shared_gate_weight, residual, group)

@@ -78,13 +78,15 @@ def make_case(tokens=256, experts=256, hidden=2048, inter=512, top=8, seed=0, ex
     return x, idx, w, (qg, sg, qd, sd), shared, gate_w
 
 
-def time_layer(case, repeats=3, threads=None):
-    """Median seconds for one MoE block on the host (1 warm-up)."""
+def time_layer(case, repeats=3, threads=None, warmup=True):
+    """Median seconds for one MoE block on the host (after 1 warm-up call unless
+    ``warmup`` is False)."""
     threads = threads or os.cpu_count()
     torch.set_num_threads(threads)
     x, idx, w, bank, shared, gate_w = case
     with torch.no_grad():
-        moe_block(x, idx, w, bank, shared, gate_w)
+        if warmup:
+            moe_block(x, idx, w, bank, shared, gate_w)
         times = []
         for _ in range(repeats):
             t0 = time.perf_counter()

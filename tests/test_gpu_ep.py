@@ -1,6 +1,7 @@
-"""Expert-parallel path on the GPU kernels, one process (world size 1 over NCCL):
-route rows through gpu_routes.moe_block with one route per row, the shared
-expert through the same library call with no routed experts (top 0)."""
+"""Expert-parallel layer on the GPU kernels (lmoe_ep_dispatch, lmoe_ep_owner,
+lmoe_ep_fold): W ranks emulated on one GPU (the exchanges as segment copies),
+one process over NCCL, and two processes on two GPUs when present; plus the
+block's no-route slots and its shared-only form."""
 import os
 import socket
 
@@ -60,10 +61,94 @@ def _wire_ref(x, ids, w, bank, shared, gate, res, wire):
     return O.round_to(res + O.shared_gate_combine(routed, O.shared_expert(x, shared, BF16), x, gate, BF16), BF16)
 
 
-@pytest.mark.parametrize('wire', ['bf16', 'int8'])
-def test_expert_parallel_world1_matches_oracle(wire):
-    import torch.distributed as dist
+def _round_add(a, b):
+    return (a.float() + b.float()).to(a.dtype)
+
+
+def _ep_sequence_gpu(x, w, ids, bank, shared, gate, res, world, wire):
+    """The expert-parallel rounding sequence from single-GPU library calls: per rank
+    g, the block on the token's routes to g's experts only (the others -1), whose
+    ordered combine is that rank's pre-reduced partial; the partials folded in
+    ascending rank order for the tokens that have a route there; then the gated
+    shared expert (the block with top 0) and the residual."""
+    from localmoe35ba3b_b200.operators import w8a8
+    from localmoe35ba3b_b200.runtime import gpu_routes
+    e_loc = bank[0].shape[0] // world
+    xr = x
+    if wire == 'int8':
+        q, s = w8a8.quantize(x)
+        xr = (q.float() * s.repeat_interleave(128, -1)).to(x.dtype)
+    acc = torch.zeros_like(x)
+    for g in range(world):
+        mine = torch.div(ids, e_loc, rounding_mode='floor') == g
+        part = gpu_routes.moe_block(xr, torch.where(mine, w, torch.zeros_like(w)),
+                                    torch.where(mine, ids, torch.full_like(ids, -1)), bank)
+        has = mine.any(1)
+        acc[has] = _round_add(acc[has], part[has])
+    t = x.shape[0]
+    sh = gpu_routes.moe_block(x, torch.empty((t, 0), device=x.device), torch.empty((t, 0), dtype=torch.int64,
+                                                                                  device=x.device),
+                              bank, shared=shared, shared_gate_weight=gate)
+    return _round_add(res, _round_add(acc, sh))
+
+
+def _emulate_ranks(x, w, ids, bank, shared, gate, res, world, wire):
+    """The GPU expert-parallel layer of `world` ranks run one after another on one
+    GPU: rank r owns tokens [r*T/world, (r+1)*T/world) and experts [r*E/world, ...);
+    the two all-to-all exchanges are segment copies between the ranks' buffers."""
     from localmoe35ba3b_b200.runtime import ep
+    T, H = x.shape
+    E, I = bank[0].shape[0], bank[2].shape[2]
+    tr, e_loc = T // world, E // world
+    L = [ep.GpuLayer(tr, ids.shape[1], E, world, H, I, x.dtype, x.device, wire) for _ in range(world)]
+    sl = [slice(r * tr, (r + 1) * tr) for r in range(world)]
+    for r in range(world):
+        L[r].dispatch(x[sl[r]].contiguous(), w[sl[r]].contiguous(), ids[sl[r]].contiguous())
+    seg = (L[0].cap + 1) * L[0].row_bytes
+    recv = [torch.empty_like(l.send) for l in L]
+    for d in range(world):
+        for s in range(world):
+            recv[d][s * seg:(s + 1) * seg] = L[s].send[d * seg:(d + 1) * seg]
+    for d in range(world):
+        L[d].recv = recv[d]
+        L[d].owner(x[sl[d]].contiguous(), [b[d * e_loc:(d + 1) * e_loc].contiguous() for b in bank], shared)
+    cap = L[0].cap
+    back = [torch.empty_like(l.partial) for l in L]
+    for s in range(world):
+        for d in range(world):
+            back[s][d * cap:(d + 1) * cap] = L[d].partial[s * cap:(s + 1) * cap]
+    outs = []
+    for s in range(world):
+        L[s].back = back[s]
+        outs.append(L[s].fold(x[sl[s]].contiguous(), gate, res[sl[s]].contiguous()))
+    return torch.cat(outs)
+
+
+@pytest.mark.parametrize('world', [1, 2, 4, 8])
+@pytest.mark.parametrize('wire', ['bf16', 'int8'])
+def test_expert_parallel_layer_emulated_ranks(world, wire):
+    """All W ranks of the GPU expert-parallel layer (dispatch, owner, fold kernels)
+    on one GPU: bit-exact against the EP rounding sequence built from the
+    single-GPU block, and within 1e-2 of the oracle."""
+    from localmoe35ba3b_b200 import _native
+    x, ids, w, bank, shared, gate, res = _case(T=192)
+    bd = [torch.from_numpy(b).cuda() for b in bank]
+    sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
+    xd, rd, gd = to_dev(x, BF16), to_dev(res, BF16), to_dev(gate, BF16)
+    wd, idd = torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda()
+    got = _emulate_ranks(xd, wd, idd, bd, sh, gd, rd, world, wire)
+    want = _ep_sequence_gpu(xd, wd, idd, bd, sh, gd, rd, world, wire)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    assert torch.equal(got.float(), want.float())
+    assert rel_maxabs(to_np(got), _wire_ref(x, ids, w, bank, shared, gate, res, wire)) < 1e-2
+
+
+def test_expert_parallel_layer_world1_equals_block():
+    """At world 1 (NCCL, one process) the layer's sequence is the block's own: the
+    result equals gpu_routes.moe_block bit for bit."""
+    import torch.distributed as dist
+    from localmoe35ba3b_b200.runtime import ep, gpu_routes
     x, ids, w, bank, shared, gate, res = _case()
     s = socket.socket()
     s.bind(('127.0.0.1', 0))
@@ -75,18 +160,19 @@ def test_expert_parallel_world1_matches_oracle(wire):
     try:
         bd = [torch.from_numpy(b).cuda() for b in bank]
         sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
-        out = ep.moe_forward(to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(), bank[0].shape[0],
-                             ep.gpu_local_moe(bd), ep.gpu_shared_part(bd, sh, to_dev(gate, BF16)),
-                             residual=to_dev(res, BF16), wire=wire)
+        xd, wd, idd, gd, rd = (to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(),
+                               to_dev(gate, BF16), to_dev(res, BF16))
+        out = ep.moe_forward_gpu(xd, wd, idd, bank[0].shape[0], bd, sh, gd, residual=rd)
+        blk = gpu_routes.moe_block(xd, wd, idd, bd, shared=sh, shared_gate_weight=gd, residual=rd)
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
-    assert rel_maxabs(to_np(out), _wire_ref(x, ids, w, bank, shared, gate, res, wire)) < 1e-2
+    assert torch.equal(out.float(), blk.float())
 
 
 def _ep2_worker(rank, wire, port, out_dir):
     import torch.distributed as dist
-    from localmoe35ba3b_b200.runtime import ep, gpu_routes
+    from localmoe35ba3b_b200.runtime import ep
     os.environ['MASTER_ADDR'] = '127.0.0.1'
     os.environ['MASTER_PORT'] = str(port)
     torch.cuda.set_device(rank)
@@ -98,11 +184,16 @@ def _ep2_worker(rank, wire, port, out_dir):
         e_loc = bank[0].shape[0] // 2
         lb = [torch.from_numpy(b[rank * e_loc:(rank + 1) * e_loc]).cuda() for b in bank]
         sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
-        out = ep.moe_forward(to_dev(x[sl], BF16), torch.from_numpy(w[sl]).cuda(), torch.from_numpy(ids[sl]).cuda(),
-                             bank[0].shape[0], ep.gpu_local_moe(lb), ep.gpu_shared_part(lb, sh, to_dev(gate, BF16)),
-                             residual=to_dev(res[sl], BF16), wire=wire)
+        out = ep.moe_forward_gpu(to_dev(x[sl], BF16), torch.from_numpy(w[sl]).cuda(),
+                                 torch.from_numpy(ids[sl]).cuda(), bank[0].shape[0], lb, sh, to_dev(gate, BF16),
+                                 residual=to_dev(res[sl], BF16), wire=wire)
         torch.cuda.synchronize()
         np.save(os.path.join(out_dir, f'ep2_{rank}.npy'), to_np(out))
+        if rank == 0:
+            bd = [torch.from_numpy(b).cuda() for b in bank]
+            seq = _ep_sequence_gpu(to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(), bd,
+                                   sh, to_dev(gate, BF16), to_dev(res, BF16), 2, wire)
+            np.save(os.path.join(out_dir, 'ep2_seq.npy'), to_np(seq))
     finally:
         dist.destroy_process_group()
 
@@ -110,6 +201,8 @@ def _ep2_worker(rank, wire, port, out_dir):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
 @pytest.mark.parametrize('wire', ['bf16', 'int8'])
 def test_expert_parallel_two_gpus_matches_oracle(tmp_path, wire):
+    """Two processes, one GPU each, NCCL exchanges: bit-exact against the EP
+    sequence built from single-GPU block calls, and within 1e-2 of the oracle."""
     import torch.multiprocessing as mp
     s = socket.socket()
     s.bind(('127.0.0.1', 0))
@@ -119,53 +212,8 @@ def test_expert_parallel_two_gpus_matches_oracle(tmp_path, wire):
     x, ids, w, bank, shared, gate, res = _case()
     ref = _wire_ref(x, ids, w, bank, shared, gate, res, wire)
     got = np.concatenate([np.load(tmp_path / f'ep2_{r}.npy') for r in range(2)])
+    assert np.array_equal(got, np.load(tmp_path / 'ep2_seq.npy'))
     assert rel_maxabs(got, ref) < 1e-2
-
-
-@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize('wire', ['bf16', 'int8'])
-def test_pack_and_unpack_kernels_match_torch_packing(wire, dtype):
-    """lmoe_ep_pack_rows == the torch byte packing of the gathered rows (with the
-    library's W8A8 quantiser on the int8 wire), byte for byte; lmoe_ep_unpack_rows ==
-    the torch unpacking gathered per route, bit for bit."""
-    from localmoe35ba3b_b200.operators.w8a8 import quantize
-    from localmoe35ba3b_b200.runtime import ep
-    g = torch.Generator(device='cpu').manual_seed(9)
-    T, H, top, n = 40, 1024, 8, 77
-    x = (torch.randn((T, H), generator=g) * 3).to(dtype).cuda()
-    x[3, 128:256] = 0  # an all-zero group: the scale floor
-    tok = torch.randint(0, T, (n,), generator=g).cuda()
-    rid = torch.randint(-1, 16, (n, top), generator=g, dtype=torch.int32).cuda()
-    rw = torch.rand((n, top), generator=g).cuda()
-    got = ep.pack_rows_gpu(x, tok, rid, rw, wire)
-    want = ep.pack_rows(x[tok].contiguous(), rid, rw, wire, quantize)
-    torch.cuda.synchronize()
-    assert got.shape == (n, ep.wire_row_bytes(H, top, wire)) and torch.equal(got, want)
-    row_of = torch.randint(0, n, (200,), generator=g).cuda()
-    rows = ep.unpack_rows_gpu(got, row_of, H, top, wire, dtype)
-    ref_rows, ids, w = ep.unpack_rows(want, H, top, wire, dtype)
-    torch.cuda.synchronize()
-    assert torch.equal(rows.view(torch.int16), ref_rows[row_of].view(torch.int16))
-    assert torch.equal(ids, rid) and torch.equal(w, rw)
-
-
-def test_pack_kernel_flags_a_token_index_out_of_range():
-    """The kernel checks each token index before it reads x: an index outside
-    [0, tokens) writes zeros and sets LMOE_DEVERR_BAD_INDEX (4)."""
-    from localmoe35ba3b_b200 import _native
-    from localmoe35ba3b_b200.runtime import ep
-    _native.check_device_errors()
-    x = torch.ones((4, 256), dtype=torch.bfloat16, device='cuda')
-    tok = torch.tensor([0, 4, 2], device='cuda')
-    rid = torch.zeros((3, 2), dtype=torch.int32, device='cuda')
-    rw = torch.ones((3, 2), device='cuda')
-    buf = ep.pack_rows_gpu(x, tok, rid, rw, 'int8')
-    rows = ep.unpack_rows_gpu(buf, torch.tensor([0, 1, 2, 3], device='cuda'), 256, 2, 'int8', torch.bfloat16)
-    torch.cuda.synchronize()
-    assert int(_native.error_word('cuda').item()) == _native.DEVERR_BAD_INDEX
-    _native.error_word('cuda').zero_()
-    assert torch.all(rows[1] == 0) and torch.all(rows[3] == 0)
-    assert torch.all(rows[0] == 1) and torch.all(rows[2] == 1)
 
 
 def test_block_skips_no_route_slots():

@@ -40,7 +40,7 @@ def test_binding_covers_header():
 def test_host_only_entry_points():
     from localmoe35ba3b_b200 import _native
     lib = _native.lib()
-    assert lib.lmoe_abi_version() == 1
+    assert lib.lmoe_abi_version() == 2
     a = lib.lmoe_route_meta_size(2048, 8, 256)
     b = lib.lmoe_route_meta_size(4096, 8, 256)
     assert 0 < a < b and a % 256 == 0
@@ -64,29 +64,34 @@ def test_c_abi_rejects_bad_geometry_without_launching():
                                None, None) == _native.ERR_INVALID
 
 
-def test_ep_wire_row_bytes_and_validation():
-    """The dispatch-row size agrees with the Python packer; bad geometry, a null
+def test_ep_layer_sizes_and_validation():
+    """The expert-parallel layer's row and workspace sizes; bad geometry, a null
     pointer or a misaligned buffer is refused before any launch."""
     from localmoe35ba3b_b200 import _native
-    from localmoe35ba3b_b200.runtime import ep
     lib = _native.lib()
-    for h, top in ((2048, 8), (128, 1), (4096, 32), (256, 0)):
-        for wire, code in (('bf16', _native.WIRE_DTYPE), ('int8', _native.WIRE_INT8)):
-            assert lib.lmoe_ep_row_bytes(h, top, code, _native.BF16) == ep.wire_row_bytes(h, top, wire)
-    assert lib.lmoe_ep_row_bytes(2048, 8, _native.WIRE_INT8, _native.BF16) == 2048 + 64 + 64
-    assert lib.lmoe_ep_row_bytes(100, 8, 0, 0) == _native.ERR_INVALID
-    assert lib.lmoe_ep_row_bytes(2048, 33, 0, 0) == _native.ERR_INVALID
-    assert lib.lmoe_ep_row_bytes(2048, 8, 2, 0) == _native.ERR_INVALID
+    # [payload | ids | weights | ranks] rounded up to 16 bytes
+    assert lib.lmoe_ep_layer_row_bytes(2048, 8, _native.WIRE_DTYPE) == 4096 + 96
+    assert lib.lmoe_ep_layer_row_bytes(2048, 8, _native.WIRE_INT8) == 2048 + 64 + 96
+    assert lib.lmoe_ep_layer_row_bytes(2048, 1, _native.WIRE_INT8) == 2128
+    assert lib.lmoe_ep_layer_row_bytes(100, 8, 0) == _native.ERR_INVALID
+    assert lib.lmoe_ep_layer_row_bytes(2048, 17, 0) == _native.ERR_INVALID
+    assert lib.lmoe_ep_layer_row_bytes(2048, 8, 2) == _native.ERR_INVALID
+    assert lib.lmoe_ep_plan_workspace_size(2048, 8, 4) == 2048 * 4 * 4 + 2048 * 8 * 4
+    ows = lib.lmoe_ep_owner_workspace_size(2048, 8, 256, 8, 2048, 2048, 512)
+    routes = 8 * 2048 * 8
+    assert ows >= (routes + 2048) * (2048 + 512 + 2048) * 2 + routes * 4 + 8 * 2048 * 8 * 4
+    assert lib.lmoe_ep_owner_workspace_size(2048, 8, 256, 3, 2048, 2048, 512) == _native.ERR_INVALID  # 256 % 3
+    assert lib.lmoe_ep_owner_workspace_size(2048, 8, 256, 16, 2048, 2048, 512) == _native.ERR_INVALID  # world > 8
+    assert lib.lmoe_ep_owner_workspace_size(2048, 8, 256, 2, 1024, 2048, 512) == _native.ERR_INVALID  # cap < tokens
     p = ctypes.c_void_p(256)
-    assert lib.lmoe_ep_pack_rows(p, 4, p, p, p, 0, 2048, 8, 1, p, 0, None, None) == 0
-    assert lib.lmoe_ep_pack_rows(p, 4, p, p, p, 3, 2000, 8, 1, p, 0, None, None) == _native.ERR_INVALID
-    assert lib.lmoe_ep_pack_rows(None, 4, p, p, p, 3, 2048, 8, 1, p, 0, None, None) == _native.ERR_INVALID
-    assert lib.lmoe_ep_pack_rows(ctypes.c_void_p(258), 4, p, p, p, 3, 2048, 8, 1, p, 0, None,
-                                 None) == _native.ERR_INVALID
-    assert lib.lmoe_ep_unpack_rows(p, 3, p, 0, 2048, 8, 1, p, 0, None, None) == 0
-    assert lib.lmoe_ep_unpack_rows(p, 3, p, 5, 2048, 8, 1, None, 0, None, None) == _native.ERR_INVALID
-    assert lib.lmoe_ep_unpack_rows(p, 3, p, 5, 2048, 8, 0, ctypes.c_void_p(260), 0, None,
-                                   None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_dispatch(p, p, p, 64, 8, 256, 2, 64, 2000, 0, 0, p, p, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_dispatch(None, p, p, 64, 8, 256, 2, 64, 2048, 0, 0, p, p, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_dispatch(ctypes.c_void_p(264), p, p, 64, 8, 256, 2, 64, 2048, 0, 0, p, p, None,
+                                None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_owner(p, p, 64, 8, 256, 2, 64, 2048, 512, 0, p, p, p, p, *([None] * 6), ctypes.c_void_p(272),
+                             p, 0, None, None, None) == _native.ERR_INVALID  # workspace not 256-byte aligned
+    assert lib.lmoe_ep_fold(p, p, p, 64, 8, 256, 2, 64, 2048, 512, None, 1, None, None, p, 0,
+                            None) == _native.ERR_INVALID  # shared expert without the owner workspace
 
 
 def test_operator_validation_errors_match_reference():
@@ -130,7 +135,7 @@ def test_bench_reference_arm_json_contract():
     d = json.loads(lines[0])
     assert d['impl'] == 'reference' and d['metric'] == bench.METRIC and d['unit'] == bench.UNIT
     assert d['higher_is_better'] is True and d['value'] > 0 and d['n_gpus'] == 1
-    assert d['config']['workload'] == bench.workload(bench.parse([]))
+    assert d['config'] == bench.config(bench.parse([]), 1)
     cb = d['cpu_baseline']
     assert cb['kind'] == 'port' and cb['cores'] >= 1 and cb['value'] == d['value'] and cb['sample']
     assert d['e2e'] == {'value': d['value'], 'unit': d['unit'], 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}
@@ -150,8 +155,8 @@ def test_header_compiles_as_c_and_links(tmp_path):
 #include <stdio.h>
 #include "localmoe_b200.h"
 int main(void) {
-  int64_t row = lmoe_ep_row_bytes(2048, 8, LMOE_WIRE_INT8, LMOE_BF16);
-  int64_t bad = lmoe_ep_row_bytes(100, 8, LMOE_WIRE_INT8, LMOE_BF16);
+  int64_t row = lmoe_ep_layer_row_bytes(2048, 8, LMOE_WIRE_INT8);
+  int64_t bad = lmoe_ep_layer_row_bytes(100, 8, LMOE_WIRE_INT8);
   int rc = lmoe_quantize_rows((const void*)16, (int8_t*)16, (float*)16, 4, 100, LMOE_BF16, NULL);
   printf("%d %lld %lld %d\\n", lmoe_abi_version(), (long long)row, (long long)bad, rc);
   return 0;
@@ -165,4 +170,4 @@ int main(void) {
     assert cc.returncode == 0, cc.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0, run.stderr
-    assert run.stdout.split() == ['1', '2176', str(_native.ERR_INVALID), str(_native.ERR_INVALID)]
+    assert run.stdout.split() == ['2', '2208', str(_native.ERR_INVALID), str(_native.ERR_INVALID)]

@@ -1,18 +1,18 @@
 """The allocation-free MoE entry point (lmoe_routed_moe_noalloc).
 
 Some callers cannot allocate device memory where they run the expert block:
-code running during CUDA-graph stream capture, hosts that hand out device
-memory only from their own fixed arena, or C/FFI hosts with no device
-allocator.  lmoe_routed_moe_noalloc takes its scratch from a fixed-size
-device array inside the library instead of a caller-provided workspace.
+host runtimes that hand out device memory only from their own fixed arena,
+and C/FFI hosts with no device allocator.  lmoe_routed_moe_noalloc takes its
+scratch from a fixed-size device array inside the library instead of a
+caller-provided workspace.
 
-This test calls it through the C ABI twice in a row, on two different inputs
-(so the second call runs on scratch the first one left behind), and checks
-each result against the ordinary entry point lmoe_routed_moe on the same
-inputs, with the bf16 tolerance the other tests use (they run the same kernels,
-so the results are expected to be identical).  It also checks that a call
-too large for the fixed scratch is refused.  The file name makes pytest
-collect it last.
+This test calls it through the C ABI several times in a row -- a large case,
+a small one, the large one again -- so every call after the first runs on
+scratch that an earlier call of a different size left behind, and checks each
+result against the ordinary entry point lmoe_routed_moe on the same inputs,
+within the bf16 tolerance the other tests use and bit for bit (both run the
+same kernels).  It also checks that a call too large for the fixed scratch is
+refused.  The file name makes pytest collect it last.
 """
 import ctypes
 
@@ -63,13 +63,14 @@ def _reference_entry(c):
     return out
 
 
-def test_noalloc_matches_allocating_entry_point_twice():
+def test_noalloc_matches_allocating_entry_point_large_small_large():
     if not torch.cuda.is_available():
         pytest.skip('needs a CUDA device')
     from localmoe35ba3b_b200 import _native as N
     lib = N.lib()
     r = rng(2024)
-    cases = [_case(r, 96, 32, 512, 256, 8), _case(r, 128, 64, 2048, 512, 8)]
+    big, small = _case(r, 128, 64, 2048, 512, 8), _case(r, 96, 32, 512, 256, 8)
+    cases = [big, small, big]
     refs = [_reference_entry(c) for c in cases]
     err = torch.zeros(1, dtype=torch.int32, device='cuda')
     for c, ref in zip(cases, refs):

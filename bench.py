@@ -495,7 +495,7 @@ def decode_leg(layers, dev, peaks, steps, warmup, seed):
     gbs = wbytes / (us_layer * 1e-6) / 1e9
     return {'us_per_layer': round(us_layer, 2), 'tok_per_s': round(1e6 / (us_layer * L), 1),
             'weight_bytes_per_layer': wbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peaks['hbm'],
-            'hbm_frac': round(gbs / peaks['hbm'], 4), 'launches_per_layer': 2,
+            'hbm_frac': round(gbs / peaks['hbm'], 4), 'launches_per_layer': 1,
             'workload': f'1 token x {L} layers, 8 routed (W8A8) + shared (W8A16) experts, one CUDA graph',
             'l2': f'{L} layers of weights ({L * 9 * EXPERT_BYTES / 1e9:.2f} GB touched per step) exceed L2'}
 

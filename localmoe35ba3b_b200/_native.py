@@ -133,11 +133,13 @@ def check_device_errors(device=None, reset=True):
 _workspaces = {}
 
 
-def workspace(device, nbytes, tag='ws'):
-    """A cached uint8 device buffer of at least nbytes (grown, never shrunk)."""
+def workspace(device, nbytes, tag='ws', zeroed=False):
+    """A cached uint8 device buffer of at least nbytes (grown, never shrunk); with
+    ``zeroed`` a (re)allocated buffer starts as zeros."""
     key = (str(device), tag)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        alloc = torch.zeros if zeroed else torch.empty
+        buf = alloc(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf

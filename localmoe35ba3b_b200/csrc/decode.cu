@@ -1,27 +1,36 @@
 // One-token MoE decode: the reference's Int8Experts decode branch
 // (qwen35_deploy/operators/int8.py:158-187) with the gated HF shared expert
-// (modeling_qwen3_5_moe.py:781-790), in two launches on the caller's stream with
-// no host synchronisation (so it can be captured in a CUDA graph):
-//   1. decode_gu_kernel  one CTA per (selected expert, block of CB hidden columns):
-//      the block's gate rows and up rows (contiguous in the bank) and their
-//      group scales arrive in shared memory by a few bulk copies issued at once,
-//      then one warp per column computes both dot products (W8A8 or W8A16 routed,
-//      W8A16 shared) and hidden = round(round(silu(g)) * u) (int8.py:182-184)
-//   2. decode_dn_kernel  one CTA per block of CBd output columns: the down rows
-//      of every selected expert and of the shared expert for those columns
-//      arrive the same way -- issued before the kernel waits for kernel 1, so
-//      they stream while kernel 1 computes -- then one warp per column computes
-//      the down dots, folding them in ascending expert order into the ordered
-//      combine of _ordered_reduce (int8.py:240-250), then
-//      + round(sigmoid(round(x . gate)) * shared), then + residual.
-// The weight bytes of a whole layer are requested at the kernels' start, so HBM
-// streams them at full rate instead of one row per warp per round trip.  Each
-// row's K is split over the 32 lanes of its warp (16 bytes per lane per chunk);
-// the group partial sums are added in group order, as the reference's loop over
-// groups does (w8a8.py:37-40).  Each CTA rebuilds the experts' ascending order
-// from the router's ids (int8.py:170-179's table, without the ids.cpu() sync and
-// the upload).  The per-row arithmetic is the grouped GEMV's (gemv.cuh).
+// (modeling_qwen3_5_moe.py:781-790), as ONE launch on the caller's stream with no
+// host synchronisation (so it can be captured in a CUDA graph).
+//
+// decode_layer_kernel, one CTA per SM (persistent), two phases:
+//   1. gate_up: a CTA takes blocks of CB hidden columns of one selected expert
+//      (or of the shared expert): the block's gate rows and up rows (contiguous in
+//      the bank) and their group scales arrive in shared memory by a few bulk
+//      copies; one warp per column computes both dot products (W8A8 or W8A16
+//      routed, W8A16 shared) and hidden = round(round(silu(g)) * u)
+//      (int8.py:182-184), written to the workspace;
+//   -- grid barrier (every CTA's hidden columns written) --
+//   2. down: a CTA takes blocks of CBd output columns: the down rows of every
+//      selected expert and of the shared expert for those columns, then one warp
+//      per column computes the down dots, folding them in ascending expert order
+//      into the ordered combine of _ordered_reduce (int8.py:240-250),
+//      + round(sigmoid(round(x . gate)) * shared), + residual.
+// Both phases' first blocks are requested at the kernel's start, so all of a
+// layer's weight bytes (29.2 MB at the benchmark geometry) stream from HBM at once
+// while phase 1 computes.  Each row's K is split over the 32 lanes of its warp
+// (16 bytes per lane per chunk); the group partial sums are added in group order,
+// as the reference's loop over groups does (w8a8.py:37-40).  Each CTA rebuilds
+// the experts' ascending order from the router's ids (int8.py:170-179's table,
+// without the ids.cpu() sync and the upload).  The per-row arithmetic is the
+// grouped GEMV's (gemv.cuh).
+//
+// The grid barrier needs every CTA resident at once: the grid is at most the
+// number of CTAs the device can hold (checked on the host), the kernel lets a
+// dependent launch start only after the barrier, and the barrier's wait is
+// bounded (a timeout sets LMOE_DEVERR_TIMEOUT and the CTAs return).
 #include "common.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 
 namespace lmoe {
@@ -29,16 +38,17 @@ namespace lmoe {
 constexpr int kDecodeMaxTop = 32;
 constexpr int kDecThreads = 512;
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kDecGuSmemMax = 140 * 1024;  // kernel 1's shared memory, so a kernel-2 CTA fits beside it
-constexpr int kDecDnSmemMax = 84 * 1024;
+constexpr int kDecRowsMax = 8;  // down rows whose dots are computed together (one chunk per lane)
+constexpr int kDecSmemMax = 220 * 1024;  // both phases' shared-memory regions
 
-// Warp 0: s_eid[r] = the r-th smallest expert id (ties by slot), s_slot[r] its slot.
-// An id outside [0, E) becomes expert 0 (no read leaves the bank) and, when
-// `report`, raises LMOE_DEVERR_BAD_EXPERT.
-__device__ __forceinline__ void expert_ranks(const int64_t* ids, int top, int64_t E, int64_t* s_eid, int* s_slot,
-                                             int* err, bool report) {
+// Warp 0: s_eid[r] = the r-th smallest expert id (ties by slot) and s_w[r] the
+// routing weight of its slot.  An id outside [0, E) becomes expert 0 (no read leaves
+// the bank) and, when `report`, raises LMOE_DEVERR_BAD_EXPERT.
+__device__ __forceinline__ void expert_ranks_w(const int64_t* ids, const float* weights, int top, int64_t E,
+                                               int64_t* s_eid, float* s_w, int* err, bool report) {
   const int lane = lane_id();
   int64_t e = lane < top ? ids[lane] : INT64_MAX;
+  const float wv = lane < top ? weights[lane] : 0.f;
   if (lane < top && (e < 0 || e >= E)) {
     if (report) raise_error(err, LMOE_DEVERR_BAD_EXPERT);
     e = 0;
@@ -50,14 +60,11 @@ __device__ __forceinline__ void expert_ranks(const int64_t* ids, int top, int64_
   }
   if (lane < top) {
     s_eid[rank] = e;
-    if (s_slot) s_slot[rank] = lane;
+    s_w[rank] = wv;
   }
 }
 
 __device__ __forceinline__ float silu_exact(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
-
-// every lane waits (bounded) for the barrier's first phase; false after a timeout
-__device__ __forceinline__ bool dec_wait(uint32_t bar, int* err) { return mbar_wait_drain(bar, 0, err); }
 
 // one weight row of `chunks` 16-byte chunks from shared memory: chunk lane + 32 i -> w[i]
 template <int MAXI>
@@ -82,86 +89,6 @@ struct GuSmem {
   }
 };
 
-// rows 0..top-1: the routed experts in ascending id order; row top: the shared
-// expert (when sh_qg != nullptr).  hid [rows, I].  Grid: rows x (I / CB) CTAs.
-template <int DT, bool W8A8, int MAXI>
-__global__ void __launch_bounds__(kDecThreads) decode_gu_kernel(
-    const typename Act<DT>::T* __restrict__ x, const int64_t* __restrict__ ids, int top, int64_t E,
-    const int8_t* __restrict__ qg, const float* __restrict__ sg, int64_t H, int64_t I, const int8_t* __restrict__ sh_qg,
-    const float* __restrict__ sh_sg, const int8_t* __restrict__ sh_qu, const float* __restrict__ sh_su, int CB,
-    typename Act<DT>::T* __restrict__ hid, int* err) {
-  using A = Act<DT>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int64_t s_eid[kDecodeMaxTop];
-  const int lane = lane_id(), warp = warp_id();
-  const int GH = (int)(H / kGroup);
-  const GuSmem L(CB, H);
-  const uint32_t sb = smem_u32(smem);
-  const int npieces = CB / 8;
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < npieces; ++p) mbar_init(sb + (uint32_t)L.bars + 8u * p, 1);
-    fence_mbar_init();
-  }
-  // launched so that it may start before the previous kernel ends: the ids, x and the
-  // hidden buffer (which the previous call's down kernel reads) all wait for it
-  grid_dep_wait();
-  if (warp == 0) expert_ranks(ids, top, E, s_eid, nullptr, err, blockIdx.x == 0);
-  __syncthreads();
-  const int nblk = (int)(I / CB);
-  const int r = blockIdx.x / nblk;
-  const int64_t c0 = (int64_t)(blockIdx.x % nblk) * CB;
-  if (threadIdx.x == 0) {
-    const int8_t *gq, *uq;
-    const float *gs, *us;
-    if (r < top) {
-      const int64_t e = s_eid[r];
-      gq = qg + (e * 2 * I + c0) * H;
-      uq = qg + (e * 2 * I + I + c0) * H;
-      gs = sg + (e * 2 * I + c0) * GH;
-      us = sg + (e * 2 * I + I + c0) * GH;
-    } else {
-      gq = sh_qg + c0 * H;
-      uq = sh_qu + c0 * H;
-      gs = sh_sg + c0 * GH;
-      us = sh_su + c0 * GH;
-    }
-    // pieces of 8 columns, each on its own barrier, so warps start as their rows land
-    const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
-    for (int p = 0; p < npieces; ++p) {
-      const uint32_t bar = sb + (uint32_t)L.bars + 8u * p;
-      mbar_arrive_expect_tx(bar, 2 * (wbytes + sbytes));
-      bulk_g2s(sb + (uint32_t)(L.wg + p * 8 * H), gq + p * 8 * H, wbytes, bar);
-      bulk_g2s(sb + (uint32_t)(L.wu + p * 8 * H), uq + p * 8 * H, wbytes, bar);
-      bulk_g2s(sb + (uint32_t)(L.sg + p * 8 * GH * 4), gs + p * 8 * GH, sbytes, bar);
-      bulk_g2s(sb + (uint32_t)(L.su + p * 8 * GH * 4), us + p * 8 * GH, sbytes, bar);
-    }
-  }
-  grid_dep_launch();  // the down kernel may start and stream its own rows beside this one
-  int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq);
-  float* xs = reinterpret_cast<float*>(smem + L.xs);
-  if (W8A8 && r < top)
-    for (int g = warp; g < GH; g += kDecWarps) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
-  __syncthreads();
-  const int chunks = (int)(H / 16);
-  for (int j = warp; j < CB; j += kDecWarps) {
-    if (!dec_wait(sb + (uint32_t)L.bars + 8u * (j / 8), err)) return;
-    uint4 wg[MAXI], wu[MAXI];
-    row_lds(sb + (uint32_t)(L.wg + j * H), chunks, lane, wg);
-    row_lds(sb + (uint32_t)(L.wu + j * H), chunks, lane, wu);
-    const float* gsr = reinterpret_cast<const float*>(smem + L.sg) + j * GH;
-    const float* usr = reinterpret_cast<const float*>(smem + L.su) + j * GH;
-    float g, u;
-    if (W8A8 && r < top) {
-      g = row_dot_w8a8(wg, gsr, xq, xs, chunks, lane);
-      u = row_dot_w8a8(wu, usr, xq, xs, chunks, lane);
-    } else {  // W8A16 routed experts, and the shared expert (Int8Linear arithmetic)
-      g = row_dot_w16<DT>(wg, gsr, x, chunks, lane);
-      u = row_dot_w16<DT>(wu, usr, x, chunks, lane);
-    }
-    if (lane == 0) hid[(int64_t)r * I + c0 + j] = A::from_f(__fmul_rn(A::round(silu_exact(A::round(g))), A::round(u)));
-  }
-}
-
 struct DnSmem {
   int64_t w, sc, hq, hs, bar, bytes;
   __host__ __device__ DnSmem(int64_t rows, int64_t top, int64_t CBd, int64_t I) {
@@ -175,169 +102,350 @@ struct DnSmem {
   }
 };
 
-// out[n] = ordered combine over the routed experts of round(round(v) * w_slot),
-// + round(sig * round(v_shared)) with sig = round(sigmoid(round(x . gate))), + residual.
-// Grid: H / CBd CTAs.
-template <int DT, bool W8A8, int MAXI>
-__global__ void __launch_bounds__(kDecThreads) decode_dn_kernel(
-    const typename Act<DT>::T* __restrict__ x, const float* __restrict__ weights, const int64_t* __restrict__ ids,
-    int top, int64_t E, const int8_t* __restrict__ qd, const float* __restrict__ sd, int64_t H, int64_t I,
-    const int8_t* __restrict__ sh_qd, const float* __restrict__ sh_sd, const typename Act<DT>::T* __restrict__ gate_w,
-    const typename Act<DT>::T* __restrict__ residual, const typename Act<DT>::T* __restrict__ hid, int CBd,
-    typename Act<DT>::T* __restrict__ out, int* err) {
-  using A = Act<DT>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int64_t s_eid[kDecodeMaxTop];
-  __shared__ int s_slot[kDecodeMaxTop];
-  __shared__ float red[kDecWarps];
-  const int lane = lane_id(), warp = warp_id();
-  const int GI = (int)(I / kGroup);
-  const bool with_shared = sh_qd != nullptr;
-  const bool gated = with_shared && gate_w != nullptr;
-  const int rows = top + (with_shared ? 1 : 0);
-  const DnSmem L(rows, top, CBd, I);
-  const uint32_t sb = smem_u32(smem);
-  const uint32_t bar = sb + (uint32_t)L.bar;
-  const int64_t n0 = (int64_t)blockIdx.x * CBd;
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-  }
-  // the ids were written before the gate_up kernel started (it waited for them before
-  // letting this kernel launch): this kernel's weight rows go out before it waits
-  if (warp == 0) expert_ranks(ids, top, E, s_eid, s_slot, err, false);
+// Grid barrier over all CTAs of a launch (every CTA resident), on one 64-bit word:
+// the low half counts arrivals, the high half is the generation.  Each CTA adds 1;
+// the last to arrive adds (1 << 32) - nctas, which restores the count to 0 and
+// advances the generation in the same atomic; the others wait for the generation
+// their own arrival returned to change.  The word's low half must be 0 before the
+// first launch on a workspace, and every completed barrier leaves it 0.  The wait
+// is bounded.
+__device__ __forceinline__ bool grid_barrier(unsigned long long* bar, unsigned nctas, int* err) {
+  __shared__ int s_ok;
+  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const uint32_t wb = (uint32_t)(CBd * I), sbt = (uint32_t)(CBd * GI * 4);
-    mbar_arrive_expect_tx(bar, (uint32_t)rows * (wb + sbt));
-    for (int rr = 0; rr < rows; ++rr) {
-      const int8_t* q = rr < top ? qd + (s_eid[rr] * H + n0) * I : sh_qd + n0 * I;
-      const float* s = rr < top ? sd + (s_eid[rr] * H + n0) * GI : sh_sd + n0 * GI;
-      bulk_g2s(sb + (uint32_t)(L.w + (int64_t)rr * CBd * I), q, wb, bar);
-      bulk_g2s(sb + (uint32_t)(L.sc + (int64_t)rr * CBd * GI * 4), s, sbt, bar);
+    const unsigned long long v = atomicAdd(bar, 1ull);
+    const unsigned gen = (unsigned)(v >> 32);
+    int ok = 1;
+    if ((unsigned)v == nctas - 1) {
+      atomicAdd(bar, (1ull << 32) - nctas);
+    } else {
+      volatile unsigned* hi = reinterpret_cast<volatile unsigned*>(bar) + 1;
+      const uint64_t t0 = gtime_ns();
+      while (*hi == gen) {
+        if (gtime_ns() - t0 > LMOE_WAIT_NS) {
+          raise_error(err, LMOE_DEVERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+struct LayerArgs {
+  const void* x;
+  const float* weights;
+  const int64_t* ids;
+  int top;
+  int64_t E, H, I;
+  const int8_t *qg, *qd, *sh_qg, *sh_qu, *sh_qd;
+  const float *sg, *sd, *sh_sg, *sh_su, *sh_sd;
+  const void* gate_w;
+  const void* residual;
+  void* hid;
+  void* out;
+  unsigned long long* bar;
+  int* err;
+  int CB, CBd, n_gu, n_dn;
+  int64_t gu_bytes;  // shared-memory bytes of the phase-1 region (the phase-2 region follows)
+};
+
+template <int DT, bool W8A8, int MAXG, int MAXD>
+__global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const LayerArgs a) {
+  using A = Act<DT>;
+  using T = typename A::T;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int64_t s_eid[kDecodeMaxTop];
+  __shared__ float s_w[kDecodeMaxTop];
+  __shared__ float red[kDecWarps];
+  const int lane = lane_id(), warp = warp_id();
+  const int top = a.top;
+  const int64_t H = a.H, I = a.I;
+  const int GH = (int)(H / kGroup), GI = (int)(I / kGroup);
+  const bool with_shared = a.sh_qg != nullptr;
+  const bool gated = with_shared && a.gate_w != nullptr;
+  const int rows = top + (with_shared ? 1 : 0);
+  const T* x = (const T*)a.x;
+  T* hid = (T*)a.hid;
+  const GuSmem G(a.CB, H);
+  const DnSmem D(rows, top, a.CBd, I);
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t sd0 = sb + (uint32_t)a.gu_bytes;  // phase-2 region
+  uint8_t* dsm = smem + a.gu_bytes;
+  const int npieces = a.CB / 8;
+  const int nblk = (int)(I / a.CB);
+  if (threadIdx.x == 0) {
+    for (int p = 0; p < npieces; ++p) mbar_init(sb + (uint32_t)G.bars + 8u * p, 1);
+    mbar_init(sd0 + (uint32_t)D.bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // copies of one block, spread over the lanes of warp 0 (one bulk copy per lane):
+  // gate_up block blk = pieces of 8 columns, each on its own barrier (gate rows, up
+  // rows, their scales: 4 copies per piece), so warps start as their rows land
+  auto issue_gu = [&](int blk) {
+    const int r = blk / nblk;
+    const int64_t c0 = (int64_t)(blk % nblk) * a.CB;
+    const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
+    if (lane < npieces) mbar_arrive_expect_tx(sb + (uint32_t)G.bars + 8u * lane, 2 * (wbytes + sbytes));
+    __syncwarp();
+    for (int k = lane; k < 4 * npieces; k += 32) {
+      const int p = k >> 2, which = k & 3;
+      const uint32_t bar = sb + (uint32_t)G.bars + 8u * p;
+      const int64_t row = c0 + p * 8 + ((which & 1) ? I : 0);  // gate rows, then up rows
+      if (r < top) {
+        const int64_t e = s_eid[r];
+        if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), a.qg + (e * 2 * I + row) * H, wbytes, bar);
+        else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), a.sg + (e * 2 * I + row) * GH, sbytes, bar);
+      } else {
+        const int64_t srow = c0 + p * 8;
+        const int8_t* q = (which & 1) ? a.sh_qu : a.sh_qg;
+        const float* sc = (which & 1) ? a.sh_su : a.sh_sg;
+        if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), q + srow * H, wbytes, bar);
+        else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), sc + srow * GH, sbytes, bar);
+      }
+    }
+  };
+  // down block blk: per row (routed experts in ascending order, then the shared
+  // expert) its CBd weight rows and their scales, all on one barrier
+  auto issue_dn = [&](int blk) {
+    const int64_t n0 = (int64_t)blk * a.CBd;
+    const uint32_t wb = (uint32_t)(a.CBd * I), sbt = (uint32_t)(a.CBd * GI * 4);
+    const uint32_t bar = sd0 + (uint32_t)D.bar;
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)rows * (wb + sbt));
+    __syncwarp();
+    for (int k = lane; k < 2 * rows; k += 32) {
+      const int rr = k >> 1;
+      if ((k & 1) == 0) {
+        const int8_t* q = rr < top ? a.qd + (s_eid[rr] * H + n0) * I : a.sh_qd + n0 * I;
+        bulk_g2s(sd0 + (uint32_t)(D.w + (int64_t)rr * a.CBd * I), q, wb, bar);
+      } else {
+        const float* sc = rr < top ? a.sd + (s_eid[rr] * H + n0) * GI : a.sh_sd + n0 * GI;
+        bulk_g2s(sd0 + (uint32_t)(D.sc + (int64_t)rr * a.CBd * GI * 4), sc, sbt, bar);
+      }
+    }
+  };
+
+  // launched so that it may start before the previous kernel ends: the ids, the
+  // routing weights, x and the hidden buffer (which the previous call reads) all
+  // wait for it
+  grid_dep_wait();
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + G.xq);
+  float* xs = reinterpret_cast<float*>(smem + G.xs);
+  if (warp == 0) {
+    // the experts' order, their routing weights, then both phases' first blocks
+    expert_ranks_w(a.ids, a.weights, top, a.E, s_eid, s_w, a.err, blockIdx.x == 0);
+    __syncwarp();
+    if ((int)blockIdx.x < a.n_gu) issue_gu(blockIdx.x);
+    // a CTA with no gate_up block streams its down rows at once; the others once their
+    // gate_up rows have landed, so that the two phases do not share the HBM stream
+    else if ((int)blockIdx.x < a.n_dn) issue_dn(blockIdx.x);
+  } else {
+    // meanwhile the other warps quantise x (W8A8) and form the shared gate's logit
+    if (W8A8)
+      for (int g = warp - 1; g < GH; g += kDecWarps - 1) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
+    if (gated) {
+      const T* gw = (const T*)a.gate_w;
+      float part = 0.f;
+      for (int64_t c = threadIdx.x - 32; c < H; c += kDecThreads - 32) part = fmaf(A::to_f(x[c]), A::to_f(gw[c]), part);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0) red[warp] = part;
     }
   }
-  if (gated) {
-    float part = 0.f;
-    for (int64_t c = threadIdx.x; c < H; c += kDecThreads) part = fmaf(A::to_f(x[c]), A::to_f(gate_w[c]), part);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (lane == 0) red[warp] = part;
+  __syncthreads();
+
+  // ---- phase 1: gate_up + SwiGLU
+  int ok = 1;
+  const int chunks1 = (int)(H / 16);
+  int it = 0;
+  for (int blk = blockIdx.x; blk < a.n_gu && ok; blk += gridDim.x, ++it) {
+    const int r = blk / nblk;
+    const int64_t c0 = (int64_t)(blk % nblk) * a.CB;
+    for (int j = warp; j < a.CB; j += kDecWarps) {
+      if (!mbar_wait_drain(sb + (uint32_t)G.bars + 8u * (j / 8), it & 1, a.err)) {
+        ok = 0;
+        break;
+      }
+      uint4 wg[MAXG], wu[MAXG];
+      row_lds(sb + (uint32_t)(G.wg + j * H), chunks1, lane, wg);
+      row_lds(sb + (uint32_t)(G.wu + j * H), chunks1, lane, wu);
+      const float* gsr = reinterpret_cast<const float*>(smem + G.sg) + j * GH;
+      const float* usr = reinterpret_cast<const float*>(smem + G.su) + j * GH;
+      float g, u;
+      if (W8A8 && r < top) {
+        g = row_dot_w8a8_ilp(wg, gsr, xq, xs, chunks1, lane);
+        u = row_dot_w8a8_ilp(wu, usr, xq, xs, chunks1, lane);
+      } else {  // W8A16 routed experts, and the shared expert (Int8Linear arithmetic)
+        g = row_dot_w16<DT>(wg, gsr, x, chunks1, lane);
+        u = row_dot_w16<DT>(wu, usr, x, chunks1, lane);
+      }
+      if (lane == 0) hid[(int64_t)r * I + c0 + j] = A::from_f(__fmul_rn(A::round(silu_exact(A::round(g))), A::round(u)));
+    }
+    if (it == 0 && warp == 0 && (int)blockIdx.x < a.n_dn) {
+      // all of this CTA's first gate_up pieces have landed: its down rows go out now
+      for (int p = 0; p < npieces; ++p)
+        if (!mbar_wait_drain(sb + (uint32_t)G.bars + 8u * p, 0, a.err)) ok = 0;
+      issue_dn(blockIdx.x);
+    }
+    ok = __syncthreads_and(ok);  // every warp is done with this block's rows
+    if (warp == 0 && ok && blk + (int)gridDim.x < a.n_gu) issue_gu(blk + gridDim.x);
   }
-  // everything above reads only what existed before the gate_up kernel started; the
-  // hidden rows below are its output
-  grid_dep_wait();
-  grid_dep_launch();  // the next call's gate_up kernel may launch (it waits on this one at its start)
-  int8_t* hq = reinterpret_cast<int8_t*>(smem + L.hq);
-  float* hs = reinterpret_cast<float*>(smem + L.hs);
-  if (W8A8)
+  const bool passed = grid_barrier(a.bar, gridDim.x, a.err);
+  grid_dep_launch();  // every CTA of this launch is resident: a dependent may take SMs as they leave
+  if (!passed || !ok) {
+    // never leave this CTA with its phase-2 copies still in flight
+    if ((int)blockIdx.x < a.n_dn) mbar_wait_drain(sd0 + (uint32_t)D.bar, 0, a.err);
+    return;
+  }
+
+  // ---- phase 2: down + ordered combine + gated shared expert + residual
+  int8_t* hq = reinterpret_cast<int8_t*>(dsm + D.hq);
+  float* hs = reinterpret_cast<float*>(dsm + D.hs);
+  if ((int)blockIdx.x < a.n_dn && W8A8) {
     for (int t = warp; t < top * GI; t += kDecWarps) {
       const int rr = t / GI, g = t % GI;
-      quant_group<DT>(hid + (int64_t)rr * I + g * kGroup, hq + (int64_t)rr * I + g * kGroup, hs + rr * GI + g, lane);
+      // the hidden rows come from other CTAs: read through L2
+      const T* src = hid + (int64_t)rr * I + g * kGroup;
+      float v[4];
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(src + lane * 4));
+      v[0] = A::lo_f(raw.x);
+      v[1] = A::hi_f(raw.x);
+      v[2] = A::lo_f(raw.y);
+      v[3] = A::hi_f(raw.y);
+      quant_vals(v, hq + (int64_t)rr * I + g * kGroup, hs + rr * GI + g, lane);
     }
+  }
   __syncthreads();
   float sig = 1.f;
   if (gated) {
     float tot = 0.f;
 #pragma unroll
-    for (int i = 0; i < kDecWarps; ++i) tot += red[i];
+    for (int i = 1; i < kDecWarps; ++i) tot += red[i];
     sig = A::round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-A::round(tot)))));
   }
-  if (!dec_wait(bar, err)) return;
-  const int chunks = (int)(I / 16);
-  const float* scs = reinterpret_cast<const float*>(smem + L.sc);
-  for (int j = warp; j < CBd; j += kDecWarps) {
-    const int64_t n = n0 + j;
-    float acc = 0.f;
-    for (int rr = 0; rr < top; ++rr) {
-      uint4 w[MAXI];
-      row_lds(sb + (uint32_t)(L.w + ((int64_t)rr * CBd + j) * I), chunks, lane, w);
-      const float* srow = scs + ((int64_t)rr * CBd + j) * GI;
-      const float v = W8A8 ? row_dot_w8a8(w, srow, hq + (int64_t)rr * I, hs + rr * GI, chunks, lane)
-                           : row_dot_w16<DT>(w, srow, hid + (int64_t)rr * I, chunks, lane);
-      acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::round(v), weights[s_slot[rr]]))));
+  const int chunks2 = (int)(I / 16);
+  const float* scs = reinterpret_cast<const float*>(dsm + D.sc);
+  const T* res = (const T*)a.residual;
+  T* out = (T*)a.out;
+  int it2 = 0;
+  for (int blk = blockIdx.x; blk < a.n_dn; blk += gridDim.x, ++it2) {
+    const int64_t n0 = (int64_t)blk * a.CBd;
+    // per column j (one warp): its residual and the shared expert's hidden chunk are
+    // loaded before the weights' wait
+    const int j0 = warp;
+    const bool have_col = j0 < a.CBd;
+    float resv = 0.f;
+    if (have_col && res != nullptr) resv = A::to_f(res[n0 + j0]);
+    if (!__syncthreads_and(mbar_wait_drain(sd0 + (uint32_t)D.bar, it2 & 1, a.err) ? 1 : 0)) return;
+    for (int j = warp; j < a.CBd; j += kDecWarps) {
+      const int64_t n = n0 + j;
+      if (j != j0 && res != nullptr) resv = A::to_f(res[n]);
+      float acc = 0.f;
+      constexpr int kDecRows = MAXD == 1 ? kDecRowsMax : 1;  // keep the rows' chunks in registers
+      for (int r0 = 0; r0 < top; r0 += kDecRows) {
+        uint4 w[kDecRows][MAXD];
+        const float* srow[kDecRows];
+        const int8_t* xr[kDecRows];
+        const float* xsr[kDecRows];
+        float v[kDecRows];
+#pragma unroll
+        for (int k = 0; k < kDecRows; ++k) {
+          const int rr = min(r0 + k, top - 1);  // rows past top repeat the last one (unused)
+          row_lds(sd0 + (uint32_t)(D.w + ((int64_t)rr * a.CBd + j) * I), chunks2, lane, w[k]);
+          srow[k] = scs + ((int64_t)rr * a.CBd + j) * GI;
+          xr[k] = hq + (int64_t)rr * I;
+          xsr[k] = hs + rr * GI;
+        }
+        if (W8A8) {
+          rows_dot_w8a8_ilp<MAXD, kDecRows>(w, srow, xr, xsr, chunks2, lane, v);
+        } else {
+#pragma unroll
+          for (int k = 0; k < kDecRows; ++k)
+            v[k] = row_dot_w16<DT, MAXD, true>(w[k], srow[k], hid + (int64_t)min(r0 + k, top - 1) * I, chunks2, lane);
+        }
+#pragma unroll
+        for (int k = 0; k < kDecRows; ++k)
+          if (r0 + k < top) acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::round(v[k]), s_w[r0 + k]))));
+      }
+      if (with_shared) {
+        uint4 w[MAXD];
+        row_lds(sd0 + (uint32_t)(D.w + ((int64_t)top * a.CBd + j) * I), chunks2, lane, w);
+        const float sv = A::round(
+            row_dot_w16<DT, MAXD, true>(w, scs + ((int64_t)top * a.CBd + j) * GI, hid + (int64_t)top * I, chunks2, lane));
+        acc = A::round(__fadd_rn(acc, gated ? A::round(__fmul_rn(sig, sv)) : sv));
+      }
+      if (res != nullptr) acc = A::round(__fadd_rn(resv, acc));
+      if (lane == 0) out[n] = A::from_f(acc);
     }
-    if (with_shared) {
-      uint4 w[MAXI];
-      row_lds(sb + (uint32_t)(L.w + ((int64_t)top * CBd + j) * I), chunks, lane, w);
-      const float s =
-          A::round(row_dot_w16<DT>(w, scs + ((int64_t)top * CBd + j) * GI, hid + (int64_t)top * I, chunks, lane));
-      acc = A::round(__fadd_rn(acc, gated ? A::round(__fmul_rn(sig, s)) : s));
-    }
-    if (residual != nullptr) acc = A::round(__fadd_rn(A::to_f(residual[n]), acc));
-    if (lane == 0) out[n] = A::from_f(acc);
+    __syncthreads();
+    if (warp == 0 && blk + (int)gridDim.x < a.n_dn) issue_dn(blk + gridDim.x);
   }
+
 }
 
+// The grid barrier's two words come first, at a fixed offset, so that a workspace
+// reused for another geometry keeps them where the previous calls left them (zero).
 struct DecodeWs {
-  int64_t off_h, bytes;
+  int64_t off_bar, off_h, bytes;
   static int64_t align(int64_t v) { return (v + 255) & ~int64_t(255); }
   DecodeWs(int64_t top, int64_t H, int64_t I) {
     (void)H;
-    off_h = 0;
-    bytes = align((top + 1) * I * 2);  // hidden rows: routed + shared
+    off_bar = 0;
+    off_h = 256;                                  // hidden rows: routed + shared
+    bytes = off_h + align((top + 1) * I * 2);
   }
 };
 
-// columns per CTA: the largest block whose rows fit the kernel's shared-memory budget
-static int pick_cb(int64_t H, int64_t I) {
-  for (int cb = 32; cb >= 8; cb >>= 1)
-    if (I % cb == 0 && GuSmem(cb, H).bytes <= kDecGuSmemMax) return cb;
-  return 0;
-}
-static int pick_cbd(int64_t rows, int64_t top, int64_t H, int64_t I) {
-  for (int cb = 16; cb >= 4; cb >>= 1)
-    if (H % cb == 0 && DnSmem(rows, top, cb, I).bytes <= kDecDnSmemMax) return cb;
-  return 0;
-}
+static int64_t a128(int64_t v) { return (v + 127) & ~int64_t(127); }
 
-template <typename K>
-static int set_smem(K kernel, int64_t bytes) {
-  LMOE_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-  return LMOE_OK;
+// columns per CTA: the largest blocks whose rows fit both phases' shared memory
+static bool pick_blocks(int64_t rows, int64_t top, int64_t H, int64_t I, int& cb, int& cbd) {
+  for (cb = 32; cb >= 8; cb >>= 1) {
+    if (I % cb) continue;
+    for (cbd = 16; cbd >= 4; cbd >>= 1)
+      if (H % cbd == 0 && a128(GuSmem(cb, H).bytes) + DnSmem(rows, top, cbd, I).bytes <= kDecSmemMax) return true;
+  }
+  return false;
 }
 
 template <int DT, bool W8A8, int MAXG, int MAXD>
-static int launch_decode_t(const void* x, const float* weights, const int64_t* ids, int top, const int8_t* qg,
-                           const float* sg, const int8_t* qd, const float* sd, int64_t E, int64_t H, int64_t I,
-                           const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu, const float* sh_su,
-                           const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w, const void* residual,
-                           void* out, void* hid, int* err, int cb, int cbd, cudaStream_t st) {
-  using T = typename Act<DT>::T;
-  const int rows = top + (sh_qg != nullptr ? 1 : 0);
-  const int64_t sm1 = GuSmem(cb, H).bytes, sm2 = DnSmem(rows, top, cbd, I).bytes;
-  auto k1 = decode_gu_kernel<DT, W8A8, MAXG>;
-  auto k2 = decode_dn_kernel<DT, W8A8, MAXD>;
-  int rc = set_smem(k1, sm1);
-  if (rc || (rc = set_smem(k2, sm2))) return rc;
-  LMOE_CUDA_CHECK(launch_pdl(k1, dim3((unsigned)(rows * (I / cb))), dim3(kDecThreads), (size_t)sm1, st, (const T*)x,
-                             ids, top, E, qg, sg, H, I, sh_qg, sh_sg, sh_qu, sh_su, cb, (T*)hid, err));
-  LMOE_CUDA_CHECK(launch_pdl(k2, dim3((unsigned)(H / cbd)), dim3(kDecThreads), (size_t)sm2, st, (const T*)x, weights,
-                             ids, top, E, qd, sd, H, I, sh_qd, sh_sd, (const T*)sh_gate_w, (const T*)residual,
-                             (const T*)hid, cbd, (T*)out, err));
+static int launch_layer(LayerArgs& a, int rows, cudaStream_t st) {
+  auto k = decode_layer_kernel<DT, W8A8, MAXG, MAXD>;
+  a.gu_bytes = a128(GuSmem(a.CB, a.H).bytes);
+  const int64_t smem = a.gu_bytes + DnSmem(rows, a.top, a.CBd, a.I).bytes;
+  LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       (int)cudaSharedmemCarveoutMaxShared));
+  // every CTA must be resident at once for the grid barrier
+  int per_sm = 0;
+  LMOE_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kDecThreads, (size_t)smem));
+  const int64_t resident = (int64_t)per_sm * sm_count();
+  if (resident <= 0) return LMOE_ERR_UNSUPPORTED;
+  const int64_t want = a.n_gu > a.n_dn ? a.n_gu : a.n_dn;
+  const unsigned grid = (unsigned)(want < resident ? want : resident);
+  LMOE_CUDA_CHECK(launch_pdl(k, dim3(grid), dim3(kDecThreads), (size_t)smem, st, a));
   return LMOE_OK;
 }
 
 template <int DT, bool W8A8>
-static int launch_decode(const void* x, const float* weights, const int64_t* ids, int top, const int8_t* qg,
-                         const float* sg, const int8_t* qd, const float* sd, int64_t E, int64_t H, int64_t I,
-                         const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu, const float* sh_su,
-                         const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w, const void* residual,
-                         void* out, void* hid, int* err, cudaStream_t st) {
-  const int rows = top + (sh_qg != nullptr ? 1 : 0);
-  const int cb = pick_cb(H, I), cbd = pick_cbd(rows, top, H, I);
-  if (cb == 0 || cbd == 0) return LMOE_ERR_UNSUPPORTED;
+static int launch_decode(LayerArgs& a, int rows, cudaStream_t st) {
+  if (!pick_blocks(rows, a.top, a.H, a.I, a.CB, a.CBd)) return LMOE_ERR_UNSUPPORTED;
+  a.n_gu = (int)(rows * (a.I / a.CB));
+  a.n_dn = (int)(a.H / a.CBd);
   // MAXI = 16-byte chunks per lane of one row: H / 512 (gate_up), I / 512 (down)
-#define LMOE_DEC(MG, MD)                                                                                           \
-  return launch_decode_t<DT, W8A8, MG, MD>(x, weights, ids, top, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu, sh_su, \
-                                           sh_qd, sh_sd, sh_gate_w, residual, out, hid, err, cb, cbd, st)
-  if (H <= 2048) {
-    if (I <= 512) LMOE_DEC(4, 1);
-    LMOE_DEC(4, kMaxChunksPerLane);
+  if (a.H <= 2048) {
+    if (a.I <= 512) return launch_layer<DT, W8A8, 4, 1>(a, rows, st);
+    return launch_layer<DT, W8A8, 4, kMaxChunksPerLane>(a, rows, st);
   }
-  if (I <= 512) LMOE_DEC(kMaxChunksPerLane, 1);
-  LMOE_DEC(kMaxChunksPerLane, kMaxChunksPerLane);
-#undef LMOE_DEC
+  if (a.I <= 512) return launch_layer<DT, W8A8, kMaxChunksPerLane, 1>(a, rows, st);
+  return launch_layer<DT, W8A8, kMaxChunksPerLane, kMaxChunksPerLane>(a, rows, st);
 }
 
 static bool a16(const void* p) { return p == nullptr || ((uintptr_t)p & 15) == 0; }
@@ -366,15 +474,34 @@ extern "C" int lmoe_decode_moe(const void* x, const float* weights, const int64_
       !a16(sh_qd) || !a16(sh_sd) || !a16(x) || !a16(ws))
     return LMOE_ERR_INVALID;
   if (H > 16 * 32 * kMaxChunksPerLane || I > 16 * 32 * kMaxChunksPerLane) return LMOE_ERR_UNSUPPORTED;
-  const int t = (int)top;
+  const DecodeWs W(top, H, I);
+  LayerArgs a = {};
+  a.x = x;
+  a.weights = weights;
+  a.ids = ids;
+  a.top = (int)top;
+  a.E = E;
+  a.H = H;
+  a.I = I;
+  a.qg = qg;
+  a.qd = qd;
+  a.sh_qg = sh_qg;
+  a.sh_qu = sh_qu;
+  a.sh_qd = sh_qd;
+  a.sg = sg;
+  a.sd = sd;
+  a.sh_sg = sh_sg;
+  a.sh_su = sh_su;
+  a.sh_sd = sh_sd;
+  a.gate_w = sh_gate_w;
+  a.residual = residual;
+  a.hid = (char*)ws + W.off_h;
+  a.bar = (unsigned long long*)((char*)ws + W.off_bar);
+  a.out = out;
+  a.err = err;
+  const int rows = (int)top + (with_shared ? 1 : 0);
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == LMOE_BF16)
-    return w8a8 ? launch_decode<LMOE_BF16, true>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu, sh_su,
-                                                 sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st)
-                : launch_decode<LMOE_BF16, false>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu,
-                                                  sh_su, sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st);
-  return w8a8 ? launch_decode<LMOE_F16, true>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu, sh_su,
-                                              sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st)
-              : launch_decode<LMOE_F16, false>(x, weights, ids, t, qg, sg, qd, sd, E, H, I, sh_qg, sh_sg, sh_qu, sh_su,
-                                               sh_qd, sh_sd, sh_gate_w, residual, out, ws, err, st);
+    return w8a8 ? launch_decode<LMOE_BF16, true>(a, rows, st) : launch_decode<LMOE_BF16, false>(a, rows, st);
+  return w8a8 ? launch_decode<LMOE_F16, true>(a, rows, st) : launch_decode<LMOE_F16, false>(a, rows, st);
 }

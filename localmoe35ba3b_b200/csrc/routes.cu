@@ -233,18 +233,35 @@ __global__ void __launch_bounds__(kRouteThreads) meta_scan_kernel(RouteArgs a, i
   grid_dep_launch();
   const int E = a.E, R = a.T * a.top;
   const int e = threadIdx.x;
+  // per expert: its total over the chunks (loads in independent batches, so the
+  // chunk counts' latencies overlap), then the block scan over experts, then each
+  // chunk's first slot written in a second batched pass
+  constexpr int kB = 16;
   int count = 0;
   if (e <= E) {
-    for (int c = 0; c < nchunks; ++c) {
-      const int t = cc[(int64_t)c * (E + 1) + e];
-      cc[(int64_t)c * (E + 1) + e] = count;
-      count += t;
+    for (int c0 = 0; c0 < nchunks; c0 += kB) {
+      int v[kB];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) v[i] = c0 + i < nchunks ? cc[(int64_t)(c0 + i) * (E + 1) + e] : 0;
+#pragma unroll
+      for (int i = 0; i < kB; ++i) count += v[i];
     }
   }
   const int incl = block_incl_scan(e <= E ? count : 0, warp_tot);
   const int first = incl - (e <= E ? count : 0);
   if (e <= E) {
-    for (int c = 0; c < nchunks; ++c) cc[(int64_t)c * (E + 1) + e] += first;
+    int run = first;
+    for (int c0 = 0; c0 < nchunks; c0 += kB) {
+      int v[kB];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) v[i] = c0 + i < nchunks ? cc[(int64_t)(c0 + i) * (E + 1) + e] : 0;
+#pragma unroll
+      for (int i = 0; i < kB; ++i)
+        if (c0 + i < nchunks) {
+          cc[(int64_t)(c0 + i) * (E + 1) + e] = run;
+          run += v[i];
+        }
+    }
     s_first[e] = first;
     if (e < E) a.offsets[e] = first;
   }

@@ -3,11 +3,11 @@ qwen35_deploy/operators/int8.py:158-187, and the HF shared expert + gate of
 modeling_qwen3_5_moe.py:781-790).
 
 ``decode_block`` runs the whole block for ``x [1, H]`` as one library call
-(``lmoe_decode_moe``): the descriptor table is built on the device from the
-router's ids (no ``ids.cpu()`` synchronisation and no table upload), then the
-table-driven gate_up GEMV, silu*up, the down GEMV and the ordered combine with
-the gated shared expert.  Nothing synchronises with the host, so a caller can
-capture a whole decode step in a CUDA graph.
+(``lmoe_decode_moe``, one kernel launch): the experts' order is built on the
+device from the router's ids (no ``ids.cpu()`` synchronisation and no table
+upload), then the gate_up GEMV + silu*up, a grid barrier, the down GEMV and the
+ordered combine with the gated shared expert.  Nothing synchronises with the
+host, so a caller can capture a whole decode step in a CUDA graph.
 """
 import torch
 
@@ -41,7 +41,8 @@ def decode_block(x, weights, ids, banks, shared=None, shared_gate_weight=None, r
     gate = shared_gate_weight.to(x.dtype).contiguous() if shared_gate_weight is not None else None
     res = residual.to(x.dtype).contiguous() if residual is not None else None
     out = torch.empty_like(x)
-    ws = N.workspace(dev, N.lib().lmoe_decode_workspace_size(top, h, inter), 'decode')
+    # zero-filled once: the kernel's grid barrier keeps its counter at zero between calls
+    ws = N.workspace(dev, N.lib().lmoe_decode_workspace_size(top, h, inter), 'decode', zeroed=True)
     qg, sg, qd, sd = banks
     N.call('lmoe_decode_moe', N.ptr(x), N.ptr(w), N.ptr(ids), top, N.ptr(qg), N.ptr(sg), N.ptr(qd), N.ptr(sd), e, h,
            inter, *[N.ptr(v) for v in sh], N.ptr(gate), N.ptr(res), N.ptr(out), N.dtype_code(x.dtype),

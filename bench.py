@@ -50,10 +50,11 @@ UNIT = 'tok/s'
 # meta_place_kernel (routing metadata), permute_rows_kernel, grouped_ts_kernel<.., false>
 # (gate_up + SwiGLU), grouped_ts_kernel<.., true> (down + routing weight), moe_combine_kernel.
 LAUNCHES_PER_LAYER = 7
-# expert-parallel layer: ep_plan_kernel, ep_pack_kernel (dispatch), ep_owner_meta_kernel,
+# expert-parallel layer: meta_count_kernel, meta_scan_kernel, meta_place_kernel (this rank's
+# routes sorted by expert), ep_slots_kernel, ep_pack_kernel (dispatch), ep_owner_meta_kernel,
 # ep_owner_scatter_kernel, the two grouped_ts_kernel launches, ep_owner_combine_kernel,
 # ep_fold_kernel (+ two NCCL all-to-all kernels, not counted)
-EP_LAUNCHES_PER_LAYER = 8
+EP_LAUNCHES_PER_LAYER = 11
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
 # `ncu --set full` capture (`python bench.py --layers 2 --steps 1 --warmup 1 --no-cpu-baseline
 # --no-extra`, -k regex:grouped_ts -s 2 -c 2): gate_up 404.2 MB + down 244.1 MB.  Per-layer

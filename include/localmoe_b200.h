@@ -223,7 +223,7 @@ LMOE_API int lmoe_router_topk(const void* logits, int64_t tokens, int64_t expert
  *    with_shared, + residual.
  * hidden % 256 == 0, inter % 128 == 0, 1 <= top <= 16. */
 LMOE_API int64_t lmoe_ep_layer_row_bytes(int64_t hidden, int64_t top, int wire);
-LMOE_API int64_t lmoe_ep_plan_workspace_size(int64_t tokens, int64_t top, int64_t world);
+LMOE_API int64_t lmoe_ep_plan_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t world);
 LMOE_API int64_t lmoe_ep_owner_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t world,
                                               int64_t cap, int64_t hidden, int64_t inter);
 LMOE_API int lmoe_ep_dispatch(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,

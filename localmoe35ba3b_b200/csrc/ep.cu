@@ -8,10 +8,11 @@
 // experts are sharded over W ranks in contiguous blocks of e_loc = E / W and
 // each rank keeps its own T tokens.  One layer:
 //
-//   sender   ep_plan_kernel      per (token, rank): the token's row index in that
-//                                rank's segment (tokens ascending); per route: its
-//                                rank among this sender's routes to the same
-//                                expert (flat route order); the segment headers
+//   sender   the routing metadata kernels: a stable counting sort of this rank's
+//                                routes by expert (a route's rank among this sender's
+//                                routes to its expert, in flat route order)
+//            ep_slots_kernel     per (token, rank): the token's row index in that
+//                                rank's segment (tokens ascending); the segment headers
 //            ep_pack_kernel      one packed row per (token, destination)
 //   ---- all_to_all of W segments of (cap + 1) rows each (row 0 = header) ----
 //   owner    ep_owner_meta_kernel  per local expert: first sorted slot, and per
@@ -92,107 +93,90 @@ struct EpOwnerWs {
   }
 };
 
-// sender plan workspace: slot_of [T, W] int32, rank_of [T, top] int32
+// sender plan workspace: the routing metadata of this rank's routes (the stable
+// counting sort of the multi-CTA metadata kernels: per expert its first sorted slot,
+// per route its sorted slot -- the rank of a route among this sender's routes to the
+// same expert is the difference), then slot_of [T, W] int32
 struct EpPlanWs {
-  int64_t off_slot, off_rank, bytes;
+  int64_t off_meta, off_slot, bytes;
   explicit EpPlanWs(const EpGeom& g) {
-    off_slot = 0;
-    off_rank = MetaLayout::align(g.T * g.W * 4);
-    bytes = MetaLayout::align(off_rank + g.T * g.top * 4);
+    off_meta = 0;
+    off_slot = MetaLayout::align(MetaLayout(g.T, g.top, g.E).bytes);
+    bytes = MetaLayout::align(off_slot + g.T * g.W * 4);
   }
 };
 
 __device__ __forceinline__ bool ep_valid_id(int64_t v, int64_t E) { return v >= 0 && v < E; }
 
 // ---------------------------------------------------------------------------
-// Sender plan (one CTA of kRouteThreads threads).
-//   phase 1: per destination rank g, the exclusive count of earlier tokens sent
-//            to g = the token's row in segment g (slot_of, -1 when not sent)
-//   phase 2: per route, its rank among this sender's routes to the same expert
-//            in flat (token-major) order -- a stable counting sort's rank, as in
-//            route_kernel (32 contiguous warp segments, __match_any_sync ranks)
-//   headers: segment g row 0 = [rows to g, routes per local expert of g]
-__global__ void __launch_bounds__(kRouteThreads) ep_plan_kernel(const int64_t* __restrict__ ids, EpGeom g,
-                                                                int32_t* __restrict__ slot_of,
-                                                                int32_t* __restrict__ rank_of,
-                                                                uint8_t* __restrict__ send, int* err) {
-  extern __shared__ int cw[];  // [kRouteWarps][E]
-  __shared__ int warp_tot[32];
-  __shared__ int s_rows[kEpMaxWorld];
+// Sender slots (one CTA of kRouteThreads threads): per destination rank d, each
+// token's row in segment d = the number of earlier tokens with a route to d (-1 when
+// it has none); the segment headers [rows to d, routes per local expert of d] (the
+// latter from the routing metadata's per-expert offsets).  Warp w takes a contiguous
+// run of tokens, 32 at a time (lane = token); a destination's ballot ranks the
+// batch's tokens.
+__global__ void __launch_bounds__(kRouteThreads) ep_slots_kernel(const int64_t* __restrict__ ids, EpGeom g,
+                                                                 const int32_t* __restrict__ offsets,
+                                                                 int32_t* __restrict__ slot_of,
+                                                                 uint8_t* __restrict__ send) {
+  extern __shared__ uint8_t s_mask[];  // [T] destination bits per token
+  __shared__ int s_cnt[kRouteWarps][kEpMaxWorld];
   const int T = (int)g.T, top = (int)g.top, E = (int)g.E, W = (int)g.W, e_loc = (int)g.e_loc;
-  const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
-
-  // ---- phase 1: token rows per destination
-  const int tpt = (T + kRouteThreads - 1) / kRouteThreads;
-  const int t_lo = min(T, tid * tpt), t_hi = min(T, t_lo + tpt);
+  const int lane = lane_id(), warp = warp_id();
+  const int S = (T + kRouteWarps - 1) / kRouteWarps;
+  const int t_lo = min(T, warp * S), t_hi = min(T, t_lo + S);
+  const unsigned lt = (1u << lane) - 1u;
   int cnt[kEpMaxWorld];
 #pragma unroll
   for (int d = 0; d < kEpMaxWorld; ++d) cnt[d] = 0;
-  for (int t = t_lo; t < t_hi; ++t) {
+  for (int b = t_lo; b < t_hi; b += 32) {
+    const int t = b + lane;
     unsigned mask = 0;
-    for (int j = 0; j < top; ++j) {
-      const int64_t v = ids[(int64_t)t * top + j];
-      if (ep_valid_id(v, E)) mask |= 1u << (int)(v / e_loc);
+    if (t < t_hi) {
+      int64_t v[kEpMaxTop];
+#pragma unroll
+      for (int j = 0; j < kEpMaxTop; ++j) v[j] = j < top ? ids[(int64_t)t * top + j] : -1;
+#pragma unroll
+      for (int j = 0; j < kEpMaxTop; ++j)
+        if (ep_valid_id(v[j], E)) mask |= 1u << (int)(v[j] / e_loc);
+      s_mask[t] = (uint8_t)mask;
     }
 #pragma unroll
-    for (int d = 0; d < kEpMaxWorld; ++d) cnt[d] += (mask >> d) & 1u;
+    for (int d = 0; d < kEpMaxWorld; ++d) cnt[d] += __popc(__ballot_sync(0xffffffffu, (mask >> d) & 1u));
   }
-  int base[kEpMaxWorld];
+  if (lane == 0)
 #pragma unroll
-  for (int d = 0; d < kEpMaxWorld; ++d) {
-    if (d < W) {
-      const int incl = block_incl_scan(cnt[d], warp_tot);
-      base[d] = incl - cnt[d];
-      if (tid == kRouteThreads - 1) s_rows[d] = incl;
-    }
-  }
-  for (int t = t_lo; t < t_hi; ++t) {
-    unsigned mask = 0;
-    for (int j = 0; j < top; ++j) {
-      const int64_t v = ids[(int64_t)t * top + j];
-      if (ep_valid_id(v, E)) mask |= 1u << (int)(v / e_loc);
-    }
-#pragma unroll
-    for (int d = 0; d < kEpMaxWorld; ++d)
-      if (d < W) slot_of[(int64_t)t * W + d] = ((mask >> d) & 1u) ? base[d]++ : -1;
-  }
-
-  // ---- phase 2: per-expert ranks of the routes
-  const int R = T * top;
-  for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) cw[i] = 0;
+    for (int d = 0; d < kEpMaxWorld; ++d) s_cnt[warp][d] = cnt[d];
   __syncthreads();
-  const int L = (R + kRouteWarps - 1) / kRouteWarps;
-  const int seg_lo = min(R, warp * L), seg_hi = min(R, seg_lo + L);
-  for (int f = seg_lo + lane; f < seg_hi; f += 32) {
-    const int64_t v = ids[f];
-    if (ep_valid_id(v, E)) atomicAdd(&cw[warp * E + (int)v], 1);
-    else raise_error(err, LMOE_DEVERR_BAD_EXPERT);
-  }
-  __syncthreads();
-  // exclusive over warps, per expert; the totals go to the headers
-  for (int e = tid; e < E; e += kRouteThreads) {
+  if (threadIdx.x < W) {  // exclusive over warps, per destination
+    const int d = threadIdx.x;
     int run = 0;
     for (int w = 0; w < kRouteWarps; ++w) {
-      const int c = cw[w * E + e];
-      cw[w * E + e] = run;
+      const int c = s_cnt[w][d];
+      s_cnt[w][d] = run;
       run += c;
     }
-    const int d = e / e_loc;
-    int32_t* hdr = reinterpret_cast<int32_t*>(send + (int64_t)d * g.seg_rows * g.row_bytes);
-    hdr[1 + (e - d * e_loc)] = run;
+    reinterpret_cast<int32_t*>(send + (int64_t)d * g.seg_rows * g.row_bytes)[0] = run;
   }
-  if (tid < W) reinterpret_cast<int32_t*>(send + (int64_t)tid * g.seg_rows * g.row_bytes)[0] = s_rows[tid];
+  for (int e = threadIdx.x; e < E; e += kRouteThreads) {
+    const int d = e / e_loc;
+    reinterpret_cast<int32_t*>(send + (int64_t)d * g.seg_rows * g.row_bytes)[1 + (e - d * e_loc)] =
+        offsets[e + 1] - offsets[e];
+  }
   __syncthreads();
-  const unsigned lt = (1u << lane) - 1u;
-  for (int b = seg_lo; b < seg_hi; b += 32) {
-    const int f = b + lane;
-    const int64_t v = f < seg_hi ? ids[f] : -1;
-    const int id = ep_valid_id(v, E) ? (int)v : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, id);
-    if (f < seg_hi) rank_of[f] = id >= 0 ? cw[warp * E + id] + __popc(peers & lt) : -1;
-    __syncwarp();
-    if (id >= 0 && lane == 31 - __clz(peers)) cw[warp * E + id] += __popc(peers);
-    __syncwarp();
+  int base[kEpMaxWorld];
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d) base[d] = d < W ? s_cnt[warp][d] : 0;
+  for (int b = t_lo; b < t_hi; b += 32) {
+    const int t = b + lane;
+    const unsigned mask = t < t_hi ? s_mask[t] : 0u;
+#pragma unroll
+    for (int d = 0; d < kEpMaxWorld; ++d) {
+      if (d >= W) break;
+      const unsigned bal = __ballot_sync(0xffffffffu, (mask >> d) & 1u);
+      if (t < t_hi) slot_of[(int64_t)t * W + d] = ((mask >> d) & 1u) ? base[d] + __popc(bal & lt) : -1;
+      base[d] += __popc(bal);
+    }
   }
 }
 
@@ -203,7 +187,8 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
                                                                 const int64_t* __restrict__ ids,
                                                                 const float* __restrict__ wts, EpGeom g,
                                                                 const int32_t* __restrict__ slot_of,
-                                                                const int32_t* __restrict__ rank_of,
+                                                                const int32_t* __restrict__ inverse,
+                                                                const int32_t* __restrict__ offsets,
                                                                 uint8_t* __restrict__ send) {
   const int lane = lane_id();
   const int64_t task = (int64_t)blockIdx.x * kEpWarps + warp_id();
@@ -213,7 +198,8 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
   if (slot < 0) return;
   uint8_t* row = send + (d * g.seg_rows + 1 + slot) * g.row_bytes;
   const int top = (int)g.top;
-  // the token's routes to rank d, sorted by local expert id
+  // the token's routes to rank d, sorted by local expert id; a route's rank among this
+  // sender's routes to its expert = its sorted slot - the expert's first slot
   int lid = 0x7fffffff;
   bool mine = false;
   float w = 0.f;
@@ -224,7 +210,7 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
       mine = true;
       lid = (int)(v - d * g.e_loc);
       w = wts[t * top + lane];
-      rk = rank_of[t * top + lane];
+      rk = inverse[t * top + lane] - offsets[v];
     }
   }
   int pos = 0;
@@ -528,15 +514,18 @@ static bool ep_geometry_ok(int64_t tokens, int64_t top, int64_t experts, int64_t
 
 using namespace lmoe;
 
+int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
+                         int with_shared, void* meta, int* err, cudaStream_t st);
+
 extern "C" int64_t lmoe_ep_layer_row_bytes(int64_t hidden, int64_t top, int wire) {
   if (hidden <= 0 || hidden % kGroup || top <= 0 || top > kEpMaxTop) return LMOE_ERR_INVALID;
   if (wire != LMOE_WIRE_DTYPE && wire != LMOE_WIRE_INT8) return LMOE_ERR_INVALID;
   return EpGeom(1, top, 1, 1, 1, hidden, kGroup, wire, LMOE_BF16).row_bytes;
 }
 
-extern "C" int64_t lmoe_ep_plan_workspace_size(int64_t tokens, int64_t top, int64_t world) {
-  if (tokens <= 0 || top <= 0 || world <= 0) return LMOE_ERR_INVALID;
-  return EpPlanWs(EpGeom(tokens, top, world, world, tokens, 256, kGroup, LMOE_WIRE_DTYPE, LMOE_BF16)).bytes;
+extern "C" int64_t lmoe_ep_plan_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t world) {
+  if (tokens <= 0 || top <= 0 || experts <= 0 || world <= 0) return LMOE_ERR_INVALID;
+  return EpPlanWs(EpGeom(tokens, top, experts, world, tokens, 256, kGroup, LMOE_WIRE_DTYPE, LMOE_BF16)).bytes;
 }
 
 extern "C" int64_t lmoe_ep_owner_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t world,
@@ -555,28 +544,35 @@ extern "C" int lmoe_ep_dispatch(const void* x, const float* weights, const int64
   cudaStream_t st = (cudaStream_t)stream;
   const EpGeom g(tokens, top, experts, world, cap, hidden, kGroup, wire, dtype);
   const EpPlanWs P(g);
+  const MetaLayout ML(tokens, top, experts);
+  char* meta = (char*)plan_ws + P.off_meta;
   int32_t* slot_of = (int32_t*)((char*)plan_ws + P.off_slot);
-  int32_t* rank_of = (int32_t*)((char*)plan_ws + P.off_rank);
+  const int32_t* offsets = (const int32_t*)(meta + ML.off_offsets);
+  const int32_t* inverse = (const int32_t*)(meta + ML.off_inverse);
   uint8_t* sb = (uint8_t*)send;
-  const size_t smem = (size_t)kRouteWarps * experts * sizeof(int);
-  if (smem > 200 * 1024) return LMOE_ERR_UNSUPPORTED;
-  LMOE_CUDA_CHECK(cudaFuncSetAttribute(ep_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  ep_plan_kernel<<<1, kRouteThreads, smem, st>>>(ids, g, slot_of, rank_of, sb, err);
+  // this rank's routes sorted by expert (stable): per route its sorted slot
+  int rc = lmoe_route_meta_impl(ids, weights, tokens, top, experts, 0, meta, err, st);
+  if (rc) return rc;
+  if (tokens > 200 * 1024) return LMOE_ERR_UNSUPPORTED;  // the destination bits of every token in shared memory
+  const size_t smem = (size_t)tokens;
+  if (smem > 48 * 1024)
+    LMOE_CUDA_CHECK(cudaFuncSetAttribute(ep_slots_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  ep_slots_kernel<<<1, kRouteThreads, smem, st>>>(ids, g, offsets, slot_of, sb);
   LMOE_CUDA_CHECK(cudaGetLastError());
   const unsigned blocks = (unsigned)((tokens * world + kEpWarps - 1) / kEpWarps);
   const dim3 block(32 * kEpWarps);
   if (dtype == LMOE_BF16) {
     const __nv_bfloat16* xp = (const __nv_bfloat16*)x;
     if (wire == LMOE_WIRE_INT8)
-      ep_pack_kernel<LMOE_BF16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, rank_of, sb);
+      ep_pack_kernel<LMOE_BF16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
     else
-      ep_pack_kernel<LMOE_BF16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, rank_of, sb);
+      ep_pack_kernel<LMOE_BF16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
   } else {
     const __half* xp = (const __half*)x;
     if (wire == LMOE_WIRE_INT8)
-      ep_pack_kernel<LMOE_F16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, rank_of, sb);
+      ep_pack_kernel<LMOE_F16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
     else
-      ep_pack_kernel<LMOE_F16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, rank_of, sb);
+      ep_pack_kernel<LMOE_F16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
   }
   LMOE_CUDA_CHECK(cudaGetLastError());
   return LMOE_OK;

@@ -31,7 +31,8 @@ Two implementations of that sequence:
 
 * ``GpuLayer`` / ``moe_forward_gpu`` -- the product path on B200s.  Five steps
   per layer with every exchange size fixed in advance, so a layer has no host
-  synchronisation: ``lmoe_ep_dispatch`` (plan + pack, 2 kernels), an equal-split
+  synchronisation: ``lmoe_ep_dispatch`` (the routing metadata of this rank's
+  routes, the destination slots, the pack: 5 kernels), an equal-split
   ``all_to_all_single`` of W segments of ``cap + 1`` rows (row 0 of a segment
   is its header: row count and routes per local expert), ``lmoe_ep_owner``
   (the owner's metadata, scatter, the two grouped GEMMs with the shared
@@ -305,7 +306,7 @@ class GpuLayer:
         self.row_bytes = lib.lmoe_ep_layer_row_bytes(self.hidden, self.top, self.wire_code)
         ows = lib.lmoe_ep_owner_workspace_size(self.tokens, self.top, self.experts, self.world, self.cap,
                                                self.hidden, self.inter)
-        pws = lib.lmoe_ep_plan_workspace_size(self.tokens, self.top, self.world)
+        pws = lib.lmoe_ep_plan_workspace_size(self.tokens, self.top, self.experts, self.world)
         if min(self.row_bytes, ows, pws) < 0:
             raise ValueError('unsupported expert-parallel geometry')
         seg = (self.cap + 1) * self.row_bytes

@@ -76,7 +76,8 @@ def test_ep_layer_sizes_and_validation():
     assert lib.lmoe_ep_layer_row_bytes(100, 8, 0) == _native.ERR_INVALID
     assert lib.lmoe_ep_layer_row_bytes(2048, 17, 0) == _native.ERR_INVALID
     assert lib.lmoe_ep_layer_row_bytes(2048, 8, 2) == _native.ERR_INVALID
-    assert lib.lmoe_ep_plan_workspace_size(2048, 8, 4) == 2048 * 4 * 4 + 2048 * 8 * 4
+    pws = lib.lmoe_ep_plan_workspace_size(2048, 8, 256, 4)
+    assert pws >= lib.lmoe_route_meta_size(2048, 8, 256) + 2048 * 4 * 4
     ows = lib.lmoe_ep_owner_workspace_size(2048, 8, 256, 8, 2048, 2048, 512)
     routes = 8 * 2048 * 8
     assert ows >= (routes + 2048) * (2048 + 512 + 2048) * 2 + routes * 4 + 8 * 2048 * 8 * 4

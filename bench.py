@@ -81,6 +81,9 @@ def parse(argv=None):
                     help='run one extra leg alone (1 GPU; for profiling) and print its JSON')
     ap.add_argument('--dp', action='store_true', help='with --gpus N > 1: N data-parallel replicas (full weights '
                                                       'per GPU) instead of expert parallelism')
+    ap.add_argument('--ep-transport', choices=('p2p', 'nccl'), default='p2p',
+                    help='expert parallelism: rows stored straight into the peers\' buffers over NVLink (p2p) or '
+                         'moved by NCCL all_to_all between the kernels')
     ap.add_argument('--ep-wire', choices=('bf16', 'int8'), default='bf16',
                     help='expert parallelism: format of the dispatched hidden rows (int8 = W8A8 activation '
                          'quantisation, 2112 instead of 4096 payload bytes per row)')
@@ -249,8 +252,10 @@ def config(a, world):
     """``config`` of the JSON line, the same for both arms."""
     total, per = job_tokens(a, world)
     if use_ep(a, world):
-        par = (f'ep{world} (experts {EXPERTS // world} per GPU, all-to-all over NCCL, {a.ep_wire} dispatch rows, '
-               'fixed-size exchanges)')
+        how = ('rows stored into the peers\' buffers over NVLink by the pack and combine kernels'
+               if a.ep_transport == 'p2p' else 'all-to-all over NCCL')
+        par = f'ep{world} (experts {EXPERTS // world} per GPU, {how}, {a.ep_wire} dispatch rows, fixed-size exchanges)'
+
     else:
         par = f'dp{world} replicas (full weights per GPU)' if world > 1 else 'single'
     return {'workload': workload(a, world), 'tokens': total, 'tokens_per_gpu': per, 'layers': a.layers,
@@ -274,8 +279,8 @@ def run_ours(a, rank, world, local):
     layers = make_layers(a.layers, dev, a.seed, e_loc, shard=rank if ep_mode else 0)
     x0, ids, wts = make_routing(a.layers, tokens, dev, a.seed + 1000 * rank)
     active = [int(torch.unique(ids[l]).numel()) for l in range(a.layers)]
-    layer_ep = ep.GpuLayer(tokens, TOP, EXPERTS, world, HIDDEN, INTER, torch.bfloat16, dev, a.ep_wire) \
-        if ep_mode else None
+    layer_ep = ep.GpuLayer(tokens, TOP, EXPERTS, world, HIDDEN, INTER, torch.bfloat16, dev, a.ep_wire,
+                           transport=a.ep_transport) if ep_mode else None
 
     def step(x, ids, wts, events=None):
         for l, (bank, shared, gate) in enumerate(layers):
@@ -378,11 +383,15 @@ def run_ours(a, rank, world, local):
                        for n, v in zip(('meta_scatter', 'gate_up', 'down', 'combine'), ost_max)})
         seg = (layer_ep.cap + 1) * layer_ep.row_bytes
         cross = (world - 1) * seg
-        a2a_us = phases['all_to_all_dispatch']
+        # with the direct transport the rows cross NVLink inside the dispatch (and the owner's
+        # combine) kernels: their phase time bounds the transfer rate from below
+        xfer_us = phases['all_to_all_dispatch'] if a.ep_transport == 'nccl' else phases['dispatch']
         roof['phase_us_per_layer_max_over_ranks'] = phases
         roof['limiting_phase'] = max(names, key=lambda n: phases[n])
         roof['nvlink'] = {'dispatch_bytes_per_rank': cross, 'return_bytes_per_rank': (world - 1) * layer_ep.cap *
-                          HIDDEN * 2, 'dispatch_gbs': round(cross / (a2a_us * 1e-6) / 1e9, 1) if a2a_us > 0 else None,
+                          HIDDEN * 2, 'dispatch_gbs': round(cross / (xfer_us * 1e-6) / 1e9, 1) if xfer_us > 0 else None,
+                          'dispatch_gbs_timing': ('the all_to_all phase' if a.ep_transport == 'nccl' else
+                                                  'the whole dispatch phase (metadata, slots, pack + NVLink stores)'),
                           'peer_copy_ref_gbs': 770.0}
     else:
         roof['stage_us_per_layer'] = {'route_meta': round(st[0] * 1e3, 2), 'gate_up': round(st[1] * 1e3, 2),
@@ -447,6 +456,8 @@ def run_ours(a, rank, world, local):
         line['extra'] = extra
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if layer_ep is not None:
+        layer_ep.close()
 
 
 def decode_leg(layers, dev, peaks, steps, warmup, seed):

@@ -197,48 +197,75 @@ LMOE_API int lmoe_router_topk(const void* logits, int64_t tokens, int64_t expert
  * inside a layer).  The reference runs the whole block on one GPU
  * (gpu_routes.routed_moe, qwen35_deploy/runtime/gpu_routes.py:66-82, inside the HF
  * block, modeling_qwen3_5_moe.py:781-792): these three calls split that block
- * around two all_to_all exchanges of equal-sized segments, which the caller runs
- * (NCCL).  `experts` is the global expert count E, sharded over `world` ranks
- * (1..8) in contiguous blocks of E / world; every rank uses the same `cap`
- * (>= its tokens) so that all segments have the same size.
+ * around two exchanges of equal-sized segments.  `experts` is the global expert
+ * count E, sharded over `world` ranks (1..8) in contiguous blocks of E / world;
+ * every rank uses the same `cap` (>= its tokens) so that all segments have the
+ * same size.
  *
  * 1. lmoe_ep_dispatch: from this rank's x [tokens, hidden], ids [tokens, top]
- *    (global expert ids) and weights [tokens, top] fp32, fills send
- *    [world][cap + 1][row_bytes]: segment d, row 0 = header (row count, routes
- *    per local expert of rank d), rows 1.. = one packed row per token with a
- *    route to rank d (tokens ascending): [payload | local ids int32 x top |
- *    weights fp32 x top | ranks int32 x top], the payload being the hidden row
- *    (wire LMOE_WIRE_DTYPE) or its W8A8 activation quantisation (LMOE_WIRE_INT8).
- *    plan_ws: lmoe_ep_plan_workspace_size bytes, read again by lmoe_ep_fold.
- * 2. all_to_all(recv, send), equal splits.
+ *    (global expert ids) and weights [tokens, top] fp32, fills W segments of
+ *    [cap + 1][row_bytes]: segment d, row 0 = header (row count, routes per local
+ *    expert of rank d), rows 1.. = one packed row per token with a route to rank d
+ *    (tokens ascending): [payload | local ids int32 x top | weights fp32 x top |
+ *    ranks int32 x top], the payload being the hidden row (wire LMOE_WIRE_DTYPE) or
+ *    its W8A8 activation quantisation (LMOE_WIRE_INT8).  plan_ws:
+ *    lmoe_ep_plan_workspace_size bytes, read again by lmoe_ep_fold.
+ * 2. exchange: segment d of rank s goes to segment s of rank d's `recv`.
  * 3. lmoe_ep_owner: this rank's experts (banks [E/world, ...]) on the received
- *    rows, plus the shared expert on its own x; partial [world][cap][hidden] = per
- *    received row the ordered sum of its routes' round(round(down) * w).
- *    ws: lmoe_ep_owner_workspace_size bytes (256-byte aligned), read again by
- *    lmoe_ep_fold.  stage_events (nullable): 5 cudaEvent_t recorded before the
- *    metadata, after the scatter, after gate_up, after down and after the combine.
- * 4. all_to_all(back, partial), equal splits.
- * 5. lmoe_ep_fold: out [tokens, hidden] = the returned rows in ascending rank
- *    order, + round(sigmoid(round(x . sh_gate_w)) * shared expert) when
- *    with_shared, + residual.
+ *    rows, plus the shared expert on its own x; per received row the ordered sum of
+ *    its routes' round(round(down) * w).  ws: lmoe_ep_owner_workspace_size bytes
+ *    (256-byte aligned), read again by lmoe_ep_fold.  stage_events (nullable): 5
+ *    cudaEvent_t recorded before the metadata, after the scatter, after gate_up, after
+ *    down and after the combine.
+ * 4. exchange: partial segment s of rank d goes to segment d of rank s's `back`.
+ * 5. lmoe_ep_fold: out [tokens, hidden] = the returned rows in ascending rank order,
+ *    + round(sigmoid(round(x . sh_gate_w)) * shared expert) when with_shared,
+ *    + residual.
+ *
+ * Transport.  peers == NULL: the caller runs both exchanges between the calls
+ * (e.g. NCCL all_to_all with equal splits): dispatch fills `send`
+ * [world][cap + 1][row_bytes], the owner reads `recv` and fills `partial`
+ * [world][cap][hidden], the fold reads `back`.  peers != NULL (direct transport over
+ * NVLink): every rank's `recv` and `back` buffers and flag words are mapped into
+ * every process (lmoe_ipc_*); the dispatch stores segment d straight into rank d's
+ * recv, the owner's combine stores straight into the senders' back buffers, and the
+ * owner and the fold wait (bounded; a timeout sets LMOE_DEVERR_TIMEOUT) until every
+ * peer's flag for this rank reaches `epoch`, which the caller increases by one per
+ * layer on every rank alike.  flags[d] points to rank d's 2 * world 32-bit flag words
+ * and counter to this rank's 2 words, all zero before the first layer.  The kernels
+ * of one rank then wait on kernels of the other ranks: run one rank per GPU.
  * hidden % 256 == 0, inter % 128 == 0, 1 <= top <= 16. */
+typedef struct {
+  void* recv[8];  /* rank d's receive buffer, [world][cap + 1][row_bytes] */
+  void* back[8];  /* rank d's return buffer, [world][cap][hidden] */
+  void* flags[8]; /* rank d's flag words, 2 * world uint32 */
+  void* counter;  /* this rank's 2 uint32 counters */
+  int rank;
+  unsigned epoch;
+} lmoe_ep_peers;
 LMOE_API int64_t lmoe_ep_layer_row_bytes(int64_t hidden, int64_t top, int wire);
 LMOE_API int64_t lmoe_ep_plan_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t world);
 LMOE_API int64_t lmoe_ep_owner_workspace_size(int64_t tokens, int64_t top, int64_t experts, int64_t world,
                                               int64_t cap, int64_t hidden, int64_t inter);
 LMOE_API int lmoe_ep_dispatch(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
                               int64_t experts, int64_t world, int64_t cap, int64_t hidden, int wire, int dtype,
-                              void* send, void* plan_ws, int* err, void* stream);
+                              void* send, void* plan_ws, int* err, const lmoe_ep_peers* peers, void* stream);
 LMOE_API int lmoe_ep_owner(const void* recv, const void* x, int64_t tokens, int64_t top, int64_t experts,
                            int64_t world, int64_t cap, int64_t hidden, int64_t inter, int wire, const int8_t* qg,
                            const float* sg, const int8_t* qd, const float* sd, const int8_t* sh_qg,
                            const float* sh_sg, const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd,
                            const float* sh_sd, void* ws, void* partial, int dtype, int* err, void** stage_events,
-                           void* stream);
+                           const lmoe_ep_peers* peers, void* stream);
 LMOE_API int lmoe_ep_fold(const void* back, const void* plan_ws, const void* x, int64_t tokens, int64_t top,
                           int64_t experts, int64_t world, int64_t cap, int64_t hidden, int64_t inter,
                           const void* owner_ws, int with_shared, const void* sh_gate_w, const void* residual,
-                          void* out, int dtype, void* stream);
+                          void* out, int dtype, int* err, const lmoe_ep_peers* peers, void* stream);
+/* CUDA IPC for the direct transport: the handle (64 bytes) of the allocation holding
+ * ptr and ptr's offset in it; opening a peer's handle maps that allocation (base) and
+ * returns the pointer at the offset; close unmaps a base. */
+LMOE_API int lmoe_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
+LMOE_API int lmoe_ipc_open_handle(const void* handle, int64_t offset, void** ptr, void** base);
+LMOE_API int lmoe_ipc_close(void* base);
 
 #ifdef __cplusplus
 }

@@ -49,11 +49,22 @@ SIGNATURES = {
     'lmoe_ep_layer_row_bytes': (_I64, [_I64, _I64, _I]),
     'lmoe_ep_plan_workspace_size': (_I64, [_I64, _I64, _I64, _I64]),
     'lmoe_ep_owner_workspace_size': (_I64, [_I64, _I64, _I64, _I64, _I64, _I64, _I64]),
-    'lmoe_ep_dispatch': (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I, _P, _P, _P, _P]),
+    'lmoe_ep_dispatch': (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I, _P, _P, _P, _P, _P]),
     'lmoe_ep_owner': (_I, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P,
-                           _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
-    'lmoe_ep_fold': (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _P, _I, _P]),
+                           _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
+    'lmoe_ep_fold': (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _P, _I, _P, _P,
+                          _P]),
+    'lmoe_ipc_get_handle': (_I, [_P, _P, _P]),
+    'lmoe_ipc_open_handle': (_I, [_P, _I64, _P, _P]),
+    'lmoe_ipc_close': (_I, [_P]),
 }
+
+class EpPeers(ctypes.Structure):
+    """lmoe_ep_peers (include/localmoe_b200.h): every rank's exchange buffers and flag
+    words as mapped into this process, this rank's counters, rank and layer epoch."""
+    _fields_ = [('recv', _P * 8), ('back', _P * 8), ('flags', _P * 8), ('counter', _P), ('rank', _I),
+                ('epoch', ctypes.c_uint)]
+
 
 _lib = None
 

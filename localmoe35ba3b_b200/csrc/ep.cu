@@ -46,6 +46,8 @@
 // ascending order (= ascending expert order), then the shared expert and the
 // residual (HF :787-790) -- the reference's single chain except that a
 // rank's partial sum is added as one term.
+#include <string.h>
+
 #include "common.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
@@ -108,6 +110,73 @@ struct EpPlanWs {
 
 __device__ __forceinline__ bool ep_valid_id(int64_t v, int64_t E) { return v >= 0 && v < E; }
 
+// Direct transport (p2p != 0): every rank's receive and return buffers and flag words,
+// mapped into this process (peers' through CUDA IPC).  The sender's pack kernel
+// stores its rows straight into the destination's receive buffer and the owner's
+// combine kernel its rows straight into the sender's return buffer, over NVLink;
+// when a kernel's last CTA is done it raises the flag of this rank on each peer to the
+// layer's epoch, and the receiving kernel waits (bounded) for every peer's flag.
+// p2p == 0: the caller moves the segments between the kernels (e.g. NCCL all_to_all).
+struct EpPeers {
+  uint8_t* recv[kEpMaxWorld];
+  uint8_t* back[kEpMaxWorld];
+  unsigned* flags[kEpMaxWorld];  // [0, W): dispatch from rank s arrived; [W, 2W): returns from rank d
+  unsigned* counter;             // this rank's last-CTA counters (pack, combine); zero between calls
+  int rank;
+  unsigned epoch;
+  int p2p;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Called by every thread of every CTA at the end of a kernel whose stores went to the
+// peers: the last CTA to finish raises flag word `slot` on every peer to the epoch.
+__device__ __forceinline__ void ep_signal_peers(const EpPeers& P, int W, int which, int slot) {
+  __shared__ int s_last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(P.counter + which, 1u);
+    s_last = old == gridDim.x - 1;
+    if (s_last) atomicExch(P.counter + which, 0u);
+  }
+  __syncthreads();
+  if (s_last && (int)threadIdx.x < W) {
+    __threadfence_system();
+    st_release_sys(P.flags[threadIdx.x] + slot, P.epoch);
+  }
+}
+
+// Every rank's flag word [base + s] of this rank reaches the epoch (bounded wait by
+// threads 0..W-1); false after a timeout (LMOE_DEVERR_TIMEOUT raised).
+__device__ __forceinline__ bool ep_wait_peers(const EpPeers& P, int W, int base, int* err) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if ((int)threadIdx.x < W) {
+    const unsigned* f = P.flags[P.rank] + base + threadIdx.x;
+    const uint64_t t0 = gtime_ns();
+    while ((int)(ld_acquire_sys(f) - P.epoch) < 0) {
+      if (gtime_ns() - t0 > LMOE_WAIT_NS) {
+        raise_error(err, LMOE_DEVERR_TIMEOUT);
+        s_ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+
+
 // ---------------------------------------------------------------------------
 // Sender slots (one CTA of kRouteThreads threads): per destination rank d, each
 // token's row in segment d = the number of earlier tokens with a route to d (-1 when
@@ -118,7 +187,12 @@ __device__ __forceinline__ bool ep_valid_id(int64_t v, int64_t E) { return v >= 
 __global__ void __launch_bounds__(kRouteThreads) ep_slots_kernel(const int64_t* __restrict__ ids, EpGeom g,
                                                                  const int32_t* __restrict__ offsets,
                                                                  int32_t* __restrict__ slot_of,
-                                                                 uint8_t* __restrict__ send) {
+                                                                 uint8_t* __restrict__ send, const EpPeers P) {
+  // segment d of this rank: the local send buffer, or (direct transport) segment
+  // `rank` of rank d's receive buffer
+  auto seg = [&](int64_t d) -> uint8_t* {
+    return P.p2p ? P.recv[d] + (int64_t)P.rank * g.seg_rows * g.row_bytes : send + d * g.seg_rows * g.row_bytes;
+  };
   extern __shared__ uint8_t s_mask[];  // [T] destination bits per token
   __shared__ int s_cnt[kRouteWarps][kEpMaxWorld];
   const int T = (int)g.T, top = (int)g.top, E = (int)g.E, W = (int)g.W, e_loc = (int)g.e_loc;
@@ -156,12 +230,11 @@ __global__ void __launch_bounds__(kRouteThreads) ep_slots_kernel(const int64_t* 
       s_cnt[w][d] = run;
       run += c;
     }
-    reinterpret_cast<int32_t*>(send + (int64_t)d * g.seg_rows * g.row_bytes)[0] = run;
+    reinterpret_cast<int32_t*>(seg(d))[0] = run;
   }
   for (int e = threadIdx.x; e < E; e += kRouteThreads) {
     const int d = e / e_loc;
-    reinterpret_cast<int32_t*>(send + (int64_t)d * g.seg_rows * g.row_bytes)[1 + (e - d * e_loc)] =
-        offsets[e + 1] - offsets[e];
+    reinterpret_cast<int32_t*>(seg(d))[1 + (e - d * e_loc)] = offsets[e + 1] - offsets[e];
   }
   __syncthreads();
   int base[kEpMaxWorld];
@@ -189,14 +262,14 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
                                                                 const int32_t* __restrict__ slot_of,
                                                                 const int32_t* __restrict__ inverse,
                                                                 const int32_t* __restrict__ offsets,
-                                                                uint8_t* __restrict__ send) {
+                                                                uint8_t* __restrict__ send, const EpPeers P) {
   const int lane = lane_id();
   const int64_t task = (int64_t)blockIdx.x * kEpWarps + warp_id();
-  if (task >= g.T * g.W) return;
   const int64_t t = task / g.W, d = task - t * g.W;
-  const int slot = slot_of[task];
-  if (slot < 0) return;
-  uint8_t* row = send + (d * g.seg_rows + 1 + slot) * g.row_bytes;
+  const int slot = task < g.T * g.W ? slot_of[task] : -1;
+  if (slot >= 0) {
+  uint8_t* row = (P.p2p ? P.recv[d] + (int64_t)P.rank * g.seg_rows * g.row_bytes : send + d * g.seg_rows * g.row_bytes) +
+                 (1 + slot) * g.row_bytes;
   const int top = (int)g.top;
   // the token's routes to rank d, sorted by local expert id; a route's rank among this
   // sender's routes to its expert = its sorted slot - the expert's first slot
@@ -245,6 +318,8 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
     const int64_t n = g.H / 8;
     for (int64_t c = lane; c < n; c += 32) dst[c] = src[c];
   }
+  }
+  if (P.p2p) ep_signal_peers(P, (int)g.W, 0, P.rank);
 }
 
 // ---------------------------------------------------------------------------
@@ -254,20 +329,23 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
 __global__ void __launch_bounds__(kRouteThreads) ep_owner_meta_kernel(const uint8_t* __restrict__ recv, EpGeom g,
                                                                       int with_shared, int32_t* __restrict__ hdr,
                                                                       Tile* __restrict__ tiles,
-                                                                      int32_t* __restrict__ base, int* err) {
+                                                                      int32_t* __restrict__ base, int* err,
+                                                                      const EpPeers P) {
   __shared__ int warp_tot[32];
   __shared__ int s_first[kRouteThreads + 1];
   __shared__ int s_bad;
   const int E = (int)g.e_loc, W = (int)g.W;
   const int e = threadIdx.x;
-  if (e == 0) s_bad = 0;
+  // direct transport: every sender's segment has landed (a timeout empties the layer)
+  const bool arrived = P.p2p ? ep_wait_peers(P, W, 0, err) : true;
+  if (e == 0) s_bad = arrived ? 0 : 1;
   __syncthreads();
   int n = 0;
   if (e < E) {
     for (int s = 0; s < W; ++s) {
       const int32_t* h = reinterpret_cast<const int32_t*>(recv + (int64_t)s * g.seg_rows * g.row_bytes);
-      const int c = h[1 + e];
-      const int rows = h[0];
+      const int c = __ldcg(h + 1 + e);
+      const int rows = __ldcg(h);
       if (c < 0 || c > rows || rows < 0 || rows > g.cap) s_bad = 1;
       n += max(0, c);
     }
@@ -285,7 +363,7 @@ __global__ void __launch_bounds__(kRouteThreads) ep_owner_meta_kernel(const uint
     for (int s = 0; s < W; ++s) {
       const int32_t* h = reinterpret_cast<const int32_t*>(recv + (int64_t)s * g.seg_rows * g.row_bytes);
       base[s * E + e] = run;
-      run += s_bad ? 0 : h[1 + e];
+      run += s_bad ? 0 : __ldcg(h + 1 + e);
     }
   }
   if (e == 0 && s_bad) raise_error(err, LMOE_DEVERR_BAD_INDEX);
@@ -383,35 +461,41 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_owner_scatter_kernel(
 template <int DT>
 __global__ void __launch_bounds__(kEpCombineThreads) ep_owner_combine_kernel(
     const uint8_t* __restrict__ recv, EpGeom g, const int32_t* __restrict__ ordered,
-    const typename Act<DT>::T* __restrict__ down, typename Act<DT>::T* __restrict__ partial) {
+    const typename Act<DT>::T* __restrict__ down, typename Act<DT>::T* __restrict__ partial, const EpPeers P) {
   using A = Act<DT>;
   const int64_t task = blockIdx.x;
   const int64_t s = task / g.cap, i = task - s * g.cap;
-  if (i >= reinterpret_cast<const int32_t*>(recv + s * g.seg_rows * g.row_bytes)[0]) return;
-  const int top = (int)g.top;
-  const int32_t* ord = ordered + task * top;
-  for (int64_t c = threadIdx.x * 8; c < g.H; c += kEpCombineThreads * 8) {
-    float acc[8];
+  if (i < reinterpret_cast<const int32_t*>(recv + s * g.seg_rows * g.row_bytes)[0]) {
+    const int top = (int)g.top;
+    const int32_t* ord = ordered + task * top;
+    // the row's partial sum goes to the local buffer or (direct transport) straight into
+    // row (rank, i) of its sender's return buffer
+    typename A::T* dst = P.p2p ? reinterpret_cast<typename A::T*>(P.back[s]) + ((int64_t)P.rank * g.cap + i) * g.H
+                               : partial + task * g.H;
+    for (int64_t c = threadIdx.x * 8; c < g.H; c += kEpCombineThreads * 8) {
+      float acc[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    for (int k = 0; k < top; ++k) {
-      const int r = ord[k];
-      if (r < 0) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(down + (int64_t)r * g.H + c);
-      const uint32_t va[4] = {v.x, v.y, v.z, v.w};
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int k = 0; k < top; ++k) {
+        const int r = ord[k];
+        if (r < 0) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(down + (int64_t)r * g.H + c);
+        const uint32_t va[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc[2 * j] = A::round(__fadd_rn(acc[2 * j], A::lo_f(va[j])));
-        acc[2 * j + 1] = A::round(__fadd_rn(acc[2 * j + 1], A::hi_f(va[j])));
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] = A::round(__fadd_rn(acc[2 * j], A::lo_f(va[j])));
+          acc[2 * j + 1] = A::round(__fadd_rn(acc[2 * j + 1], A::hi_f(va[j])));
+        }
       }
+      uint4 o;
+      o.x = A::pack(acc[0], acc[1]);
+      o.y = A::pack(acc[2], acc[3]);
+      o.z = A::pack(acc[4], acc[5]);
+      o.w = A::pack(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(dst + c) = o;
     }
-    uint4 o;
-    o.x = A::pack(acc[0], acc[1]);
-    o.y = A::pack(acc[2], acc[3]);
-    o.z = A::pack(acc[4], acc[5]);
-    o.w = A::pack(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(partial + task * g.H + c) = o;
   }
+  if (P.p2p) ep_signal_peers(P, (int)g.W, 1, (int)g.W + P.rank);
 }
 
 // ---------------------------------------------------------------------------
@@ -423,11 +507,14 @@ __global__ void __launch_bounds__(kEpCombineThreads) ep_fold_kernel(
     const typename Act<DT>::T* __restrict__ back, EpGeom g, const int32_t* __restrict__ slot_of,
     const typename Act<DT>::T* __restrict__ x, const typename Act<DT>::T* __restrict__ gate_w, int with_shared,
     const int32_t* __restrict__ hdr, const typename Act<DT>::T* __restrict__ down,
-    const typename Act<DT>::T* __restrict__ residual, typename Act<DT>::T* __restrict__ out) {
+    const typename Act<DT>::T* __restrict__ residual, typename Act<DT>::T* __restrict__ out, const EpPeers P,
+    int* err) {
   using A = Act<DT>;
   __shared__ float red[kEpCombineThreads / 32];
   const int64_t t = blockIdx.x;
   const int64_t H = g.H;
+  // direct transport: every owner's returned rows have landed
+  if (P.p2p && !ep_wait_peers(P, (int)g.W, (int)g.W, err)) return;
   float sig = 1.f;
   if (with_shared && gate_w != nullptr) {
     float part = 0.f;
@@ -459,7 +546,7 @@ __global__ void __launch_bounds__(kEpCombineThreads) ep_fold_kernel(
     for (int64_t d = 0; d < g.W; ++d) {
       const int slot = slot_of[t * g.W + d];
       if (slot < 0) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(back + (d * g.cap + slot) * H + c);
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(back + (d * g.cap + slot) * H + c));
       const uint32_t va[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -494,6 +581,30 @@ __global__ void __launch_bounds__(kEpCombineThreads) ep_fold_kernel(
     o.w = A::pack(acc[6], acc[7]);
     *reinterpret_cast<uint4*>(out + t * H + c) = o;
   }
+}
+
+static EpPeers make_peers(const lmoe_ep_peers* pp, int64_t world) {
+  EpPeers P = {};
+  if (pp == nullptr) return P;
+  for (int64_t d = 0; d < world; ++d) {
+    P.recv[d] = (uint8_t*)pp->recv[d];
+    P.back[d] = (uint8_t*)pp->back[d];
+    P.flags[d] = (unsigned*)pp->flags[d];
+  }
+  P.counter = (unsigned*)pp->counter;
+  P.rank = pp->rank;
+  P.epoch = pp->epoch;
+  P.p2p = 1;
+  return P;
+}
+
+static bool peers_ok(const lmoe_ep_peers* pp, int64_t world) {
+  if (pp == nullptr) return true;
+  if (pp->rank < 0 || pp->rank >= world || pp->counter == nullptr) return false;
+  for (int64_t d = 0; d < world; ++d)
+    if (!pp->recv[d] || !pp->back[d] || !pp->flags[d] || ((uintptr_t)pp->recv[d] & 15) || ((uintptr_t)pp->back[d] & 15))
+      return false;
+  return true;
 }
 
 static bool ep_geometry_ok(int64_t tokens, int64_t top, int64_t experts, int64_t world, int64_t cap, int64_t hidden,
@@ -537,16 +648,17 @@ extern "C" int64_t lmoe_ep_owner_workspace_size(int64_t tokens, int64_t top, int
 
 extern "C" int lmoe_ep_dispatch(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
                                 int64_t experts, int64_t world, int64_t cap, int64_t hidden, int wire, int dtype,
-                                void* send, void* plan_ws, int* err, void* stream) {
-  if (!x || !weights || !ids || !send || !plan_ws) return LMOE_ERR_INVALID;
+                                void* send, void* plan_ws, int* err, const lmoe_ep_peers* peers, void* stream) {
+  if (!x || !weights || !ids || (!send && !peers) || !plan_ws || !peers_ok(peers, world)) return LMOE_ERR_INVALID;
+  const EpPeers P = make_peers(peers, world);
   if (!ep_geometry_ok(tokens, top, experts, world, cap, hidden, kGroup, wire, dtype)) return LMOE_ERR_INVALID;
   if (((uintptr_t)x & 15) || ((uintptr_t)send & 15)) return LMOE_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
   const EpGeom g(tokens, top, experts, world, cap, hidden, kGroup, wire, dtype);
-  const EpPlanWs P(g);
+  const EpPlanWs PW(g);
   const MetaLayout ML(tokens, top, experts);
-  char* meta = (char*)plan_ws + P.off_meta;
-  int32_t* slot_of = (int32_t*)((char*)plan_ws + P.off_slot);
+  char* meta = (char*)plan_ws + PW.off_meta;
+  int32_t* slot_of = (int32_t*)((char*)plan_ws + PW.off_slot);
   const int32_t* offsets = (const int32_t*)(meta + ML.off_offsets);
   const int32_t* inverse = (const int32_t*)(meta + ML.off_inverse);
   uint8_t* sb = (uint8_t*)send;
@@ -557,22 +669,22 @@ extern "C" int lmoe_ep_dispatch(const void* x, const float* weights, const int64
   const size_t smem = (size_t)tokens;
   if (smem > 48 * 1024)
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(ep_slots_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  ep_slots_kernel<<<1, kRouteThreads, smem, st>>>(ids, g, offsets, slot_of, sb);
+  ep_slots_kernel<<<1, kRouteThreads, smem, st>>>(ids, g, offsets, slot_of, sb, P);
   LMOE_CUDA_CHECK(cudaGetLastError());
   const unsigned blocks = (unsigned)((tokens * world + kEpWarps - 1) / kEpWarps);
   const dim3 block(32 * kEpWarps);
   if (dtype == LMOE_BF16) {
     const __nv_bfloat16* xp = (const __nv_bfloat16*)x;
     if (wire == LMOE_WIRE_INT8)
-      ep_pack_kernel<LMOE_BF16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
+      ep_pack_kernel<LMOE_BF16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb, P);
     else
-      ep_pack_kernel<LMOE_BF16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
+      ep_pack_kernel<LMOE_BF16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb, P);
   } else {
     const __half* xp = (const __half*)x;
     if (wire == LMOE_WIRE_INT8)
-      ep_pack_kernel<LMOE_F16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
+      ep_pack_kernel<LMOE_F16, true><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb, P);
     else
-      ep_pack_kernel<LMOE_F16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb);
+      ep_pack_kernel<LMOE_F16, false><<<blocks, block, 0, st>>>(xp, ids, weights, g, slot_of, inverse, offsets, sb, P);
   }
   LMOE_CUDA_CHECK(cudaGetLastError());
   return LMOE_OK;
@@ -582,7 +694,7 @@ template <int DT>
 static int ep_owner_launch(const EpGeom& g, const uint8_t* recv, const void* x, const int8_t* qg, const float* sg,
                            const int8_t* qd, const float* sd, const int8_t* sh_qg, const float* sh_sg,
                            const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd, const float* sh_sd,
-                           char* ws, void* partial, int* err, void** events, cudaStream_t st) {
+                           char* ws, void* partial, int* err, void** events, const EpPeers& P, cudaStream_t st) {
   using T = typename Act<DT>::T;
   const EpOwnerWs O(g);
   const bool with_shared = sh_qg != nullptr;
@@ -600,7 +712,7 @@ static int ep_owner_launch(const EpGeom& g, const uint8_t* recv, const void* x, 
   };
   int rc = mark(0);
   if (rc) return rc;
-  ep_owner_meta_kernel<<<1, kRouteThreads, 0, st>>>(recv, g, with_shared ? 1 : 0, hdr, tiles, base, err);
+  ep_owner_meta_kernel<<<1, kRouteThreads, 0, st>>>(recv, g, with_shared ? 1 : 0, hdr, tiles, base, err, P);
   LMOE_CUDA_CHECK(cudaGetLastError());
   const int64_t tasks = g.W * g.cap + g.T;
   const unsigned blocks = (unsigned)((tasks + kEpWarps - 1) / kEpWarps);
@@ -664,7 +776,7 @@ static int ep_owner_launch(const EpGeom& g, const uint8_t* recv, const void* x, 
   if ((rc = mark(3))) return rc;
   // plain launch: reads the down kernel's output
   ep_owner_combine_kernel<DT><<<(unsigned)(g.W * g.cap), kEpCombineThreads, 0, st>>>(recv, g, ordered, dn,
-                                                                                      (T*)partial);
+                                                                                      (T*)partial, P);
   LMOE_CUDA_CHECK(cudaGetLastError());
   return mark(4);
 }
@@ -674,43 +786,93 @@ extern "C" int lmoe_ep_owner(const void* recv, const void* x, int64_t tokens, in
                              const float* sg, const int8_t* qd, const float* sd, const int8_t* sh_qg,
                              const float* sh_sg, const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd,
                              const float* sh_sd, void* ws, void* partial, int dtype, int* err, void** stage_events,
-                             void* stream) {
-  if (!recv || !x || !qg || !sg || !qd || !sd || !ws || !partial) return LMOE_ERR_INVALID;
+                             const lmoe_ep_peers* peers, void* stream) {
+  if (!peers_ok(peers, world)) return LMOE_ERR_INVALID;
+  if (peers) recv = peers->recv[peers->rank];
+  if (!recv || !x || !qg || !sg || !qd || !sd || !ws || (!partial && !peers)) return LMOE_ERR_INVALID;
   if (!ep_geometry_ok(tokens, top, experts, world, cap, hidden, inter, wire, dtype)) return LMOE_ERR_INVALID;
   if (sh_qg && (!sh_sg || !sh_qu || !sh_su || !sh_qd || !sh_sd)) return LMOE_ERR_INVALID;
   if (((uintptr_t)recv & 15) || ((uintptr_t)x & 15) || ((uintptr_t)partial & 15) || ((uintptr_t)ws & 255))
     return LMOE_ERR_INVALID;
   const EpGeom g(tokens, top, experts, world, cap, hidden, inter, wire, dtype);
+  const EpPeers P = make_peers(peers, world);
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == LMOE_BF16)
     return ep_owner_launch<LMOE_BF16>(g, (const uint8_t*)recv, x, qg, sg, qd, sd, sh_qg, sh_sg, sh_qu, sh_su, sh_qd,
-                                      sh_sd, (char*)ws, partial, err, stage_events, st);
+                                      sh_sd, (char*)ws, partial, err, stage_events, P, st);
   return ep_owner_launch<LMOE_F16>(g, (const uint8_t*)recv, x, qg, sg, qd, sd, sh_qg, sh_sg, sh_qu, sh_su, sh_qd,
-                                   sh_sd, (char*)ws, partial, err, stage_events, st);
+                                   sh_sd, (char*)ws, partial, err, stage_events, P, st);
 }
 
 extern "C" int lmoe_ep_fold(const void* back, const void* plan_ws, const void* x, int64_t tokens, int64_t top,
                             int64_t experts, int64_t world, int64_t cap, int64_t hidden, int64_t inter,
                             const void* owner_ws, int with_shared, const void* sh_gate_w, const void* residual,
-                            void* out, int dtype, void* stream) {
+                            void* out, int dtype, int* err, const lmoe_ep_peers* peers, void* stream) {
+  if (!peers_ok(peers, world)) return LMOE_ERR_INVALID;
+  if (peers) back = peers->back[peers->rank];
   if (!back || !plan_ws || !x || !out || (with_shared && !owner_ws)) return LMOE_ERR_INVALID;
   if (!ep_geometry_ok(tokens, top, experts, world, cap, hidden, inter, LMOE_WIRE_DTYPE, dtype))
     return LMOE_ERR_INVALID;
   const EpGeom g(tokens, top, experts, world, cap, hidden, inter, LMOE_WIRE_DTYPE, dtype);
-  const EpPlanWs P(g);
+  const EpPlanWs Pw(g);
   const EpOwnerWs O(g);
-  const int32_t* slot_of = (const int32_t*)((const char*)plan_ws + P.off_slot);
+  const EpPeers P = make_peers(peers, world);
+  const int32_t* slot_of = (const int32_t*)((const char*)plan_ws + Pw.off_slot);
   const int32_t* hdr = with_shared ? (const int32_t*)((const char*)owner_ws + O.off_hdr) : nullptr;
   const char* dn = with_shared ? (const char*)owner_ws + O.off_down : nullptr;
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == LMOE_BF16)
     ep_fold_kernel<LMOE_BF16><<<(unsigned)tokens, kEpCombineThreads, 0, st>>>(
         (const __nv_bfloat16*)back, g, slot_of, (const __nv_bfloat16*)x, (const __nv_bfloat16*)sh_gate_w,
-        with_shared ? 1 : 0, hdr, (const __nv_bfloat16*)dn, (const __nv_bfloat16*)residual, (__nv_bfloat16*)out);
+        with_shared ? 1 : 0, hdr, (const __nv_bfloat16*)dn, (const __nv_bfloat16*)residual, (__nv_bfloat16*)out, P,
+        err);
   else
     ep_fold_kernel<LMOE_F16><<<(unsigned)tokens, kEpCombineThreads, 0, st>>>(
         (const __half*)back, g, slot_of, (const __half*)x, (const __half*)sh_gate_w, with_shared ? 1 : 0, hdr,
-        (const __half*)dn, (const __half*)residual, (__half*)out);
+        (const __half*)dn, (const __half*)residual, (__half*)out, P, err);
   LMOE_CUDA_CHECK(cudaGetLastError());
+  return LMOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Mapping the exchange buffers of the other ranks (CUDA IPC).  A handle names the
+// whole allocation that holds `ptr`; the offset locates ptr inside it.
+typedef CUresult (*MemRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+extern "C" int lmoe_ipc_get_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset) return LMOE_ERR_INVALID;
+  static MemRangeFn range = []() -> MemRangeFn {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return (MemRangeFn)f;
+    return nullptr;
+  }();
+  if (range == nullptr) return LMOE_ERR_UNSUPPORTED;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, (CUdeviceptr)ptr) != CUDA_SUCCESS) return LMOE_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  LMOE_CUDA_CHECK(cudaIpcGetMemHandle(&h, (void*)base));
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)((CUdeviceptr)ptr - base);
+  return LMOE_OK;
+}
+
+extern "C" int lmoe_ipc_open_handle(const void* handle, int64_t offset, void** ptr, void** base) {
+  if (!handle || !ptr || !base || offset < 0) return LMOE_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  LMOE_CUDA_CHECK(cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess));
+  *base = b;
+  *ptr = (char*)b + offset;
+  return LMOE_OK;
+}
+
+extern "C" int lmoe_ipc_close(void* base) {
+  if (!base) return LMOE_ERR_INVALID;
+  LMOE_CUDA_CHECK(cudaIpcCloseMemHandle(base));
   return LMOE_OK;
 }

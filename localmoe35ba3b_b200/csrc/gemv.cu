@@ -208,7 +208,7 @@ __global__ void routed_reduce_kernel(const typename Act<DT>::T* __restrict__ dow
 using namespace lmoe;
 
 // ============================================================================ C ABI
-extern "C" int lmoe_abi_version(void) { return 2; }
+extern "C" int lmoe_abi_version(void) { return 3; }
 
 extern "C" int lmoe_quantize_rows(const void* x, int8_t* q, float* s, int64_t rows, int64_t k, int dtype,
                                   void* stream) {

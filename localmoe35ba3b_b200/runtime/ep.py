@@ -29,20 +29,24 @@ stay within the 1e-2 bar.
 
 Two implementations of that sequence:
 
-* ``GpuLayer`` / ``moe_forward_gpu`` -- the product path on B200s.  Five steps
-  per layer with every exchange size fixed in advance, so a layer has no host
-  synchronisation: ``lmoe_ep_dispatch`` (the routing metadata of this rank's
-  routes, the destination slots, the pack: 5 kernels), an equal-split
-  ``all_to_all_single`` of W segments of ``cap + 1`` rows (row 0 of a segment
-  is its header: row count and routes per local expert), ``lmoe_ep_owner``
-  (the owner's metadata, scatter, the two grouped GEMMs with the shared
-  expert's own-token tiles folded in, the ordered combine: 5 kernels), the
-  return ``all_to_all_single``, ``lmoe_ep_fold`` (1 kernel).
+* ``GpuLayer`` / ``moe_forward_gpu`` -- the product path on B200s.  Every
+  exchange size is fixed in advance (W segments of ``cap + 1`` rows; row 0 of a
+  segment is its header: row count and routes per local expert), so a layer has
+  no host synchronisation: ``lmoe_ep_dispatch`` (the routing metadata of this
+  rank's routes, the destination slots, the pack: 5 kernels), ``lmoe_ep_owner``
+  (the owner's metadata, scatter, the two grouped GEMMs with the shared expert's
+  own-token tiles folded in, the ordered combine: 5 kernels), ``lmoe_ep_fold``
+  (1 kernel).  With the direct transport (default for W > 1) the pack and
+  combine kernels store their rows straight into the peers' buffers over
+  NVLink; with 'nccl' two ``all_to_all_single`` calls move them between the
+  kernels.
 * ``moe_forward`` -- the same sequence with variable-size exchanges and
   injected compute (``local_moe(x, weights, ids)``, ``shared_part(x)``), which
   the CPU multi-process tests (gloo) run with oracle functions to check the
   orchestration and the rounding sequence.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -287,20 +291,31 @@ class GpuLayer:
     ``tokens`` rows per rank (every rank must use the same ``cap`` >= its token
     count, default ``tokens``: the exchanges are equal-split), ``experts`` global
     experts sharded over ``world`` ranks, ``top`` routes per token.  The buffers
-    are allocated once and reused by every layer and step of the same geometry:
-    ``send``/``recv`` ``[world * (cap + 1) * row_bytes]`` bytes, ``partial``/``back``
-    ``[world * cap, hidden]``, the plan and owner workspaces.
+    are allocated once and reused by every layer and step of the same geometry.
+
+    ``transport``: 'p2p' (the default with more than one rank) -- the dispatch and
+    combine kernels store straight into the peers' buffers over NVLink, mapped once
+    through CUDA IPC (a collective over ``group``: every rank constructs its layer
+    together), and the receiving kernels wait on per-layer epoch flags; 'nccl' --
+    two ``all_to_all_single`` calls between the kernels.  One rank per GPU.
     """
 
-    def __init__(self, tokens, top, experts, world, hidden, inter, dtype, device, wire='bf16', cap=None):
+    FLAG_BYTES = 4096
+
+    def __init__(self, tokens, top, experts, world, hidden, inter, dtype, device, wire='bf16', cap=None,
+                 transport=None, group=None):
         from .. import _native as N
         if wire not in WIRES:
             raise ValueError("wire must be 'bf16' or 'int8'")
+        transport = transport or ('p2p' if world > 1 else 'nccl')
+        if transport not in ('p2p', 'nccl'):
+            raise ValueError("transport must be 'p2p' or 'nccl'")
         self.N = N
         self.tokens, self.top, self.experts, self.world = int(tokens), int(top), int(experts), int(world)
         self.hidden, self.inter, self.dtype, self.wire = int(hidden), int(inter), dtype, wire
         self.cap = int(cap if cap is not None else tokens)
         self.device = torch.device(device)
+        self.transport, self.group = transport, group
         self.wire_code = N.WIRE_INT8 if wire == 'int8' else N.WIRE_DTYPE
         lib = N.lib()
         self.row_bytes = lib.lmoe_ep_layer_row_bytes(self.hidden, self.top, self.wire_code)
@@ -311,12 +326,70 @@ class GpuLayer:
             raise ValueError('unsupported expert-parallel geometry')
         seg = (self.cap + 1) * self.row_bytes
         dev = self.device
-        self.send = torch.empty(self.world * seg, dtype=torch.uint8, device=dev)
-        self.recv = self.send if self.world == 1 else torch.empty_like(self.send)
         self.plan_ws = torch.empty(pws, dtype=torch.uint8, device=dev)
         self.owner_ws = torch.empty(ows, dtype=torch.uint8, device=dev)
-        self.partial = torch.empty((self.world * self.cap, self.hidden), dtype=dtype, device=dev)
-        self.back = self.partial if self.world == 1 else torch.empty_like(self.partial)
+        self.epoch = 0
+        self._bases = []
+        if transport == 'nccl':
+            self.peers = None
+            self.send = torch.empty(self.world * seg, dtype=torch.uint8, device=dev)
+            self.recv = self.send if self.world == 1 else torch.empty_like(self.send)
+            self.partial = torch.empty((self.world * self.cap, self.hidden), dtype=dtype, device=dev)
+            self.back = self.partial if self.world == 1 else torch.empty_like(self.partial)
+            return
+        # one allocation: [flag words | receive buffer | return buffer], shared with the peers
+        back_bytes = self.world * self.cap * self.hidden * torch.empty((), dtype=dtype).element_size()
+        self.exbuf = torch.zeros(self.FLAG_BYTES + self.world * seg + back_bytes, dtype=torch.uint8, device=dev)
+        self.counter = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.send = None
+        self.recv = self.exbuf[self.FLAG_BYTES:self.FLAG_BYTES + self.world * seg]
+        self.back = self.exbuf[self.FLAG_BYTES + self.world * seg:].view(dtype).view(self.world * self.cap,
+                                                                                     self.hidden)
+        self.partial = None
+        rank = dist.get_rank(group) if self.world > 1 else 0
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_int64()
+        N.call('lmoe_ipc_get_handle', ctypes.c_void_p(self.exbuf.data_ptr()), handle, ctypes.byref(off))
+        mine = torch.tensor(list(bytes(handle)) + list(int(off.value).to_bytes(8, 'little')), dtype=torch.uint8,
+                            device=dev)
+        everyone = torch.empty((self.world, 72), dtype=torch.uint8, device=dev)
+        if self.world > 1:
+            dist.all_gather_into_tensor(everyone, mine, group=group)
+        else:
+            everyone[0] = mine
+        table = everyone.cpu().numpy()
+        p = N.EpPeers()
+        for d in range(self.world):
+            if d == rank:
+                ptr = self.exbuf.data_ptr()
+            else:
+                h = (ctypes.c_uint8 * 64)(*table[d, :64].tolist())
+                o = int.from_bytes(bytes(table[d, 64:].tolist()), 'little')
+                out, base = ctypes.c_void_p(), ctypes.c_void_p()
+                N.call('lmoe_ipc_open_handle', h, o, ctypes.byref(out), ctypes.byref(base))
+                self._bases.append(base)
+                ptr = out.value
+            p.flags[d] = ptr
+            p.recv[d] = ptr + self.FLAG_BYTES
+            p.back[d] = ptr + self.FLAG_BYTES + self.world * seg
+        p.counter = self.counter.data_ptr()
+        p.rank = rank
+        self.peers = p
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def close(self):
+        """Unmap the peers' buffers (direct transport; every rank calls it together)."""
+        if self._bases:
+            torch.cuda.synchronize(self.device)
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            for b in self._bases:
+                self.N.call('lmoe_ipc_close', b)
+            self._bases = []
+
+    def _peers_arg(self):
+        return None if self.peers is None else ctypes.byref(self.peers)
 
     def _check(self, x, weights, ids):
         if x.shape != (self.tokens, self.hidden) or x.dtype != self.dtype or not x.is_contiguous():
@@ -325,19 +398,23 @@ class GpuLayer:
             raise ValueError('routing does not match the layer geometry')
 
     def dispatch(self, x, weights, ids):
-        """Fill ``send`` from this rank's tokens and their routing."""
+        """This rank's tokens and their routing into the send segments (direct
+        transport: into the peers' receive buffers).  Starts a new layer epoch."""
         N = self.N
         self._check(x, weights, ids)
         ids = ids if ids.dtype == torch.int64 else ids.long()
         weights = weights if weights.dtype == torch.float32 else weights.float()
+        if self.peers is not None:
+            self.epoch = (self.epoch + 1) & 0xffffffff
+            self.peers.epoch = self.epoch
         N.call('lmoe_ep_dispatch', N.ptr(x), N.ptr(weights.contiguous()), N.ptr(ids.contiguous()), self.tokens,
                self.top, self.experts, self.world, self.cap, self.hidden, self.wire_code, N.dtype_code(self.dtype),
-               N.ptr(self.send), N.ptr(self.plan_ws), N.ptr(N.error_word(self.device)), N.stream(self.device))
+               N.ptr(self.send), N.ptr(self.plan_ws), N.ptr(N.error_word(self.device)), self._peers_arg(),
+               N.stream(self.device))
 
     def owner(self, x, banks, shared=None, stage_events=None):
-        """This rank's experts on ``recv`` (+ the shared expert on its own ``x``)
-        into ``partial``; ``banks`` hold the local experts ``[E / world, ...]``."""
-        import ctypes
+        """This rank's experts on the received rows (+ the shared expert on its own
+        ``x``); ``banks`` hold the local experts ``[E / world, ...]``."""
         N = self.N
         qg, sg, qd, sd = banks
         if qg.shape != (self.experts // self.world, 2 * self.inter, self.hidden):
@@ -354,7 +431,7 @@ class GpuLayer:
         N.call('lmoe_ep_owner', N.ptr(self.recv), N.ptr(x), self.tokens, self.top, self.experts, self.world,
                self.cap, self.hidden, self.inter, self.wire_code, N.ptr(qg), N.ptr(sg), N.ptr(qd), N.ptr(sd),
                *[N.ptr(v) for v in sh], N.ptr(self.owner_ws), N.ptr(self.partial), N.dtype_code(self.dtype),
-               N.ptr(N.error_word(self.device)), evs, N.stream(self.device))
+               N.ptr(N.error_word(self.device)), evs, self._peers_arg(), N.stream(self.device))
         self.with_shared = shared is not None
 
     def fold(self, x, shared_gate_weight=None, residual=None):
@@ -365,18 +442,22 @@ class GpuLayer:
         gate = None if shared_gate_weight is None else shared_gate_weight.to(self.dtype).contiguous()
         N.call('lmoe_ep_fold', N.ptr(self.back), N.ptr(self.plan_ws), N.ptr(x), self.tokens, self.top, self.experts,
                self.world, self.cap, self.hidden, self.inter, N.ptr(self.owner_ws), 1 if self.with_shared else 0,
-               N.ptr(gate), N.ptr(residual), N.ptr(out), N.dtype_code(self.dtype), N.stream(self.device))
+               N.ptr(gate), N.ptr(residual), N.ptr(out), N.dtype_code(self.dtype), N.ptr(N.error_word(self.device)),
+               self._peers_arg(), N.stream(self.device))
         return out
 
     def exchange(self, out, inp, group=None):
-        if self.world > 1:
-            dist.all_to_all_single(out, inp, group=group)
+        """The caller-run exchange of the 'nccl' transport (nothing to do with 'p2p')."""
+        if self.peers is None and self.world > 1:
+            dist.all_to_all_single(out, inp, group=group if group is not None else self.group)
 
     def forward(self, x, weights, ids, banks, shared=None, shared_gate_weight=None, residual=None, group=None,
                 events=None):
         """One expert-parallel layer for this rank's ``x [tokens, hidden]``.  ``events``
         (optional): 6 CUDA events recorded around dispatch, the first exchange, the
-        owner, the return exchange and the fold."""
+        owner, the return exchange and the fold (with the direct transport the
+        exchanges happen inside dispatch and owner, and the waits for them inside
+        owner and fold)."""
         def mark(i):
             if events is not None:
                 events[i].record()
@@ -398,15 +479,16 @@ _layers = {}
 
 
 def moe_forward_gpu(x, weights, ids, experts, banks, shared=None, shared_gate_weight=None, residual=None,
-                    group=None, wire='bf16', cap=None):
+                    group=None, wire='bf16', cap=None, transport=None):
     """Expert-parallel MoE block on this rank's GPU (``GpuLayer``, cached per
-    geometry): ``banks`` are this rank's experts ``[experts / world, ...]``,
-    ``shared``/``shared_gate_weight`` the replicated shared expert and its gate."""
+    geometry; its first call is a collective when the transport is 'p2p'): ``banks``
+    are this rank's experts ``[experts / world, ...]``, ``shared``/``shared_gate_weight``
+    the replicated shared expert and its gate."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     t, top = ids.shape
-    key = (x.device, t, top, experts, world, x.shape[1], banks[2].shape[2], x.dtype, wire, cap)
+    key = (x.device, t, top, experts, world, x.shape[1], banks[2].shape[2], x.dtype, wire, cap, transport, group)
     layer = _layers.get(key)
     if layer is None:
         layer = _layers[key] = GpuLayer(t, top, experts, world, x.shape[1], banks[2].shape[2], x.dtype, x.device,
-                                        wire, cap)
+                                        wire, cap, transport, group)
     return layer.forward(x.contiguous(), weights, ids, banks, shared, shared_gate_weight, residual, group)

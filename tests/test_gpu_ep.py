@@ -100,7 +100,8 @@ def _emulate_ranks(x, w, ids, bank, shared, gate, res, world, wire):
     T, H = x.shape
     E, I = bank[0].shape[0], bank[2].shape[2]
     tr, e_loc = T // world, E // world
-    L = [ep.GpuLayer(tr, ids.shape[1], E, world, H, I, x.dtype, x.device, wire) for _ in range(world)]
+    L = [ep.GpuLayer(tr, ids.shape[1], E, world, H, I, x.dtype, x.device, wire, transport='nccl')
+         for _ in range(world)]
     sl = [slice(r * tr, (r + 1) * tr) for r in range(world)]
     for r in range(world):
         L[r].dispatch(x[sl[r]].contiguous(), w[sl[r]].contiguous(), ids[sl[r]].contiguous())
@@ -144,9 +145,12 @@ def test_expert_parallel_layer_emulated_ranks(world, wire):
     assert rel_maxabs(to_np(got), _wire_ref(x, ids, w, bank, shared, gate, res, wire)) < 1e-2
 
 
-def test_expert_parallel_layer_world1_equals_block():
-    """At world 1 (NCCL, one process) the layer's sequence is the block's own: the
-    result equals gpu_routes.moe_block bit for bit."""
+@pytest.mark.parametrize('transport', ['nccl', 'p2p'])
+def test_expert_parallel_layer_world1_equals_block(transport):
+    """At world 1 (one process) the layer's sequence is the block's own: the result
+    equals gpu_routes.moe_block bit for bit, with either transport (the direct one
+    stores to and waits on this rank's own buffers and flags), over several layers
+    (the flag epochs advance)."""
     import torch.distributed as dist
     from localmoe35ba3b_b200.runtime import ep, gpu_routes
     x, ids, w, bank, shared, gate, res = _case()
@@ -162,15 +166,20 @@ def test_expert_parallel_layer_world1_equals_block():
         sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
         xd, wd, idd, gd, rd = (to_dev(x, BF16), torch.from_numpy(w).cuda(), torch.from_numpy(ids).cuda(),
                                to_dev(gate, BF16), to_dev(res, BF16))
-        out = ep.moe_forward_gpu(xd, wd, idd, bank[0].shape[0], bd, sh, gd, residual=rd)
+        outs = [ep.moe_forward_gpu(xd, wd, idd, bank[0].shape[0], bd, sh, gd, residual=rd, transport=transport)
+                for _ in range(3)]
         blk = gpu_routes.moe_block(xd, wd, idd, bd, shared=sh, shared_gate_weight=gd, residual=rd)
         torch.cuda.synchronize()
+        from localmoe35ba3b_b200 import _native
+        _native.check_device_errors()
     finally:
+        ep._layers.clear()
         dist.destroy_process_group()
-    assert torch.equal(out.float(), blk.float())
+    for out in outs:
+        assert torch.equal(out.float(), blk.float())
 
 
-def _ep2_worker(rank, wire, port, out_dir):
+def _ep2_worker(rank, wire, transport, port, out_dir):
     import torch.distributed as dist
     from localmoe35ba3b_b200.runtime import ep
     os.environ['MASTER_ADDR'] = '127.0.0.1'
@@ -184,10 +193,17 @@ def _ep2_worker(rank, wire, port, out_dir):
         e_loc = bank[0].shape[0] // 2
         lb = [torch.from_numpy(b[rank * e_loc:(rank + 1) * e_loc]).cuda() for b in bank]
         sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
-        out = ep.moe_forward_gpu(to_dev(x[sl], BF16), torch.from_numpy(w[sl]).cuda(),
-                                 torch.from_numpy(ids[sl]).cuda(), bank[0].shape[0], lb, sh, to_dev(gate, BF16),
-                                 residual=to_dev(res[sl], BF16), wire=wire)
+        # three layers in a row (the direct transport's flag epochs advance, its buffers are reused)
+        for _ in range(3):
+            out = ep.moe_forward_gpu(to_dev(x[sl], BF16), torch.from_numpy(w[sl]).cuda(),
+                                     torch.from_numpy(ids[sl]).cuda(), bank[0].shape[0], lb, sh, to_dev(gate, BF16),
+                                     residual=to_dev(res[sl], BF16), wire=wire, transport=transport)
         torch.cuda.synchronize()
+        from localmoe35ba3b_b200 import _native
+        _native.check_device_errors()
+        for layer in ep._layers.values():
+            layer.close()
+        ep._layers.clear()
         np.save(os.path.join(out_dir, f'ep2_{rank}.npy'), to_np(out))
         if rank == 0:
             bd = [torch.from_numpy(b).cuda() for b in bank]
@@ -199,16 +215,19 @@ def _ep2_worker(rank, wire, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+@pytest.mark.parametrize('transport', ['p2p', 'nccl'])
 @pytest.mark.parametrize('wire', ['bf16', 'int8'])
-def test_expert_parallel_two_gpus_matches_oracle(tmp_path, wire):
-    """Two processes, one GPU each, NCCL exchanges: bit-exact against the EP
-    sequence built from single-GPU block calls, and within 1e-2 of the oracle."""
+def test_expert_parallel_two_gpus_matches_oracle(tmp_path, wire, transport):
+    """Two processes, one GPU each, direct NVLink stores or NCCL exchanges: bit-exact
+    against the EP sequence built from single-GPU block calls, and within 1e-2 of the
+    oracle."""
     import torch.multiprocessing as mp
     s = socket.socket()
     s.bind(('127.0.0.1', 0))
     port = s.getsockname()[1]
     s.close()
-    mp.start_processes(_ep2_worker, args=(wire, port, str(tmp_path)), nprocs=2, join=True, start_method='spawn')
+    mp.start_processes(_ep2_worker, args=(wire, transport, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method='spawn')
     x, ids, w, bank, shared, gate, res = _case()
     ref = _wire_ref(x, ids, w, bank, shared, gate, res, wire)
     got = np.concatenate([np.load(tmp_path / f'ep2_{r}.npy') for r in range(2)])

@@ -40,7 +40,7 @@ def test_binding_covers_header():
 def test_host_only_entry_points():
     from localmoe35ba3b_b200 import _native
     lib = _native.lib()
-    assert lib.lmoe_abi_version() == 2
+    assert lib.lmoe_abi_version() == 3
     a = lib.lmoe_route_meta_size(2048, 8, 256)
     b = lib.lmoe_route_meta_size(4096, 8, 256)
     assert 0 < a < b and a % 256 == 0
@@ -85,14 +85,23 @@ def test_ep_layer_sizes_and_validation():
     assert lib.lmoe_ep_owner_workspace_size(2048, 8, 256, 16, 2048, 2048, 512) == _native.ERR_INVALID  # world > 8
     assert lib.lmoe_ep_owner_workspace_size(2048, 8, 256, 2, 1024, 2048, 512) == _native.ERR_INVALID  # cap < tokens
     p = ctypes.c_void_p(256)
-    assert lib.lmoe_ep_dispatch(p, p, p, 64, 8, 256, 2, 64, 2000, 0, 0, p, p, None, None) == _native.ERR_INVALID
-    assert lib.lmoe_ep_dispatch(None, p, p, 64, 8, 256, 2, 64, 2048, 0, 0, p, p, None, None) == _native.ERR_INVALID
-    assert lib.lmoe_ep_dispatch(ctypes.c_void_p(264), p, p, 64, 8, 256, 2, 64, 2048, 0, 0, p, p, None,
+    assert lib.lmoe_ep_dispatch(p, p, p, 64, 8, 256, 2, 64, 2000, 0, 0, p, p, None, None, None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_dispatch(None, p, p, 64, 8, 256, 2, 64, 2048, 0, 0, p, p, None, None,
+                                None) == _native.ERR_INVALID
+    assert lib.lmoe_ep_dispatch(ctypes.c_void_p(264), p, p, 64, 8, 256, 2, 64, 2048, 0, 0, p, p, None, None,
                                 None) == _native.ERR_INVALID
     assert lib.lmoe_ep_owner(p, p, 64, 8, 256, 2, 64, 2048, 512, 0, p, p, p, p, *([None] * 6), ctypes.c_void_p(272),
-                             p, 0, None, None, None) == _native.ERR_INVALID  # workspace not 256-byte aligned
-    assert lib.lmoe_ep_fold(p, p, p, 64, 8, 256, 2, 64, 2048, 512, None, 1, None, None, p, 0,
+                             p, 0, None, None, None, None) == _native.ERR_INVALID  # workspace not 256-byte aligned
+    assert lib.lmoe_ep_fold(p, p, p, 64, 8, 256, 2, 64, 2048, 512, None, 1, None, None, p, 0, None, None,
                             None) == _native.ERR_INVALID  # shared expert without the owner workspace
+    # the direct transport: a peer table with a rank outside [0, world) or a null buffer is refused
+    peers = _native.EpPeers()
+    peers.rank = 2
+    assert lib.lmoe_ep_dispatch(p, p, p, 64, 8, 256, 2, 64, 2048, 0, 0, None, p, None, ctypes.byref(peers),
+                                None) == _native.ERR_INVALID
+    peers.rank = 0
+    assert lib.lmoe_ep_fold(p, p, p, 64, 8, 256, 2, 64, 2048, 512, p, 1, None, None, p, 0, None,
+                            ctypes.byref(peers), None) == _native.ERR_INVALID
 
 
 def test_operator_validation_errors_match_reference():
@@ -171,4 +180,4 @@ int main(void) {
     assert cc.returncode == 0, cc.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0, run.stderr
-    assert run.stdout.split() == ['2', '2208', str(_native.ERR_INVALID), str(_native.ERR_INVALID)]
+    assert run.stdout.split() == ['3', '2208', str(_native.ERR_INVALID), str(_native.ERR_INVALID)]

@@ -264,9 +264,12 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
                                                                 const int32_t* __restrict__ offsets,
                                                                 uint8_t* __restrict__ send, const EpPeers P) {
   const int lane = lane_id();
-  const int64_t task = (int64_t)blockIdx.x * kEpWarps + warp_id();
+  // a persistent grid: each warp takes (token, destination) pairs in turn, so that the
+  // direct transport's end-of-kernel fence and signal run once per CTA, not per row
+  for (int64_t task = (int64_t)blockIdx.x * kEpWarps + warp_id(); task < g.T * g.W;
+       task += (int64_t)gridDim.x * kEpWarps) {
   const int64_t t = task / g.W, d = task - t * g.W;
-  const int slot = task < g.T * g.W ? slot_of[task] : -1;
+  const int slot = slot_of[task];
   if (slot >= 0) {
   uint8_t* row = (P.p2p ? P.recv[d] + (int64_t)P.rank * g.seg_rows * g.row_bytes : send + d * g.seg_rows * g.row_bytes) +
                  (1 + slot) * g.row_bytes;
@@ -317,6 +320,7 @@ __global__ void __launch_bounds__(32 * kEpWarps) ep_pack_kernel(const typename A
     uint4* dst = reinterpret_cast<uint4*>(row);
     const int64_t n = g.H / 8;
     for (int64_t c = lane; c < n; c += 32) dst[c] = src[c];
+  }
   }
   }
   if (P.p2p) ep_signal_peers(P, (int)g.W, 0, P.rank);
@@ -463,7 +467,8 @@ __global__ void __launch_bounds__(kEpCombineThreads) ep_owner_combine_kernel(
     const uint8_t* __restrict__ recv, EpGeom g, const int32_t* __restrict__ ordered,
     const typename Act<DT>::T* __restrict__ down, typename Act<DT>::T* __restrict__ partial, const EpPeers P) {
   using A = Act<DT>;
-  const int64_t task = blockIdx.x;
+  // a persistent grid over the received rows (one signal per CTA with the direct transport)
+  for (int64_t task = blockIdx.x; task < g.W * g.cap; task += gridDim.x) {
   const int64_t s = task / g.cap, i = task - s * g.cap;
   if (i < reinterpret_cast<const int32_t*>(recv + s * g.seg_rows * g.row_bytes)[0]) {
     const int top = (int)g.top;
@@ -494,6 +499,7 @@ __global__ void __launch_bounds__(kEpCombineThreads) ep_owner_combine_kernel(
       o.w = A::pack(acc[6], acc[7]);
       *reinterpret_cast<uint4*>(dst + c) = o;
     }
+  }
   }
   if (P.p2p) ep_signal_peers(P, (int)g.W, 1, (int)g.W + P.rank);
 }
@@ -671,7 +677,8 @@ extern "C" int lmoe_ep_dispatch(const void* x, const float* weights, const int64
     LMOE_CUDA_CHECK(cudaFuncSetAttribute(ep_slots_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   ep_slots_kernel<<<1, kRouteThreads, smem, st>>>(ids, g, offsets, slot_of, sb, P);
   LMOE_CUDA_CHECK(cudaGetLastError());
-  const unsigned blocks = (unsigned)((tokens * world + kEpWarps - 1) / kEpWarps);
+  const int64_t want = (tokens * world + kEpWarps - 1) / kEpWarps;
+  const unsigned blocks = (unsigned)(want < 4 * sm_count() ? want : 4 * sm_count());
   const dim3 block(32 * kEpWarps);
   if (dtype == LMOE_BF16) {
     const __nv_bfloat16* xp = (const __nv_bfloat16*)x;
@@ -775,8 +782,9 @@ static int ep_owner_launch(const EpGeom& g, const uint8_t* recv, const void* x, 
   if ((rc = launch_down_ts(dw, st))) return rc;
   if ((rc = mark(3))) return rc;
   // plain launch: reads the down kernel's output
-  ep_owner_combine_kernel<DT><<<(unsigned)(g.W * g.cap), kEpCombineThreads, 0, st>>>(recv, g, ordered, dn,
-                                                                                      (T*)partial, P);
+  const int64_t rows_in = g.W * g.cap;
+  const unsigned cblocks = (unsigned)(rows_in < 8 * sm_count() ? rows_in : 8 * sm_count());
+  ep_owner_combine_kernel<DT><<<cblocks, kEpCombineThreads, 0, st>>>(recv, g, ordered, dn, (T*)partial, P);
   LMOE_CUDA_CHECK(cudaGetLastError());
   return mark(4);
 }

@@ -190,6 +190,14 @@ LMOE_API int lmoe_decode_moe(const void* x, const float* weights, const int64_t*
 LMOE_API int lmoe_router_topk(const void* logits, int64_t tokens, int64_t experts, int64_t top, float* weights,
                               int64_t* ids, float* probs, int dtype, void* stream);
 
+/* Diagnostic (no reference counterpart): the SwiGLU epilogue of the routed gate_up
+ * (torch.nn.functional.silu(gate) * up, qwen35_deploy/runtime/gpu_routes.py:75) evaluates silu
+ * with a branch-free correctly rounded division; this counts, over all 65,536 16-bit
+ * patterns of `dtype` taken as the gate value, the inputs where that SiLU differs from
+ * fp32 g / (1 + expf(-g)) with an IEEE division.  *mismatches (device int32) is added to;
+ * 0 after the stream means every input agrees bit for bit. */
+LMOE_API int lmoe_selftest_silu(int dtype, int* mismatches, void* stream);
+
 #define LMOE_WIRE_DTYPE 0 /* expert-parallel dispatch payload: the hidden row in the activation dtype */
 #define LMOE_WIRE_INT8 1  /* ... or its W8A8 activation quantisation (w8a8.quantize, operators/w8a8.py:8-22) */
 

@@ -39,6 +39,8 @@ int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st);
 // TMEM-operand kernel (gemm_ts.cu)
 int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st);
 int launch_down_ts(const GemmLaunch& L, cudaStream_t st);
+// the SwiGLU epilogue's SiLU against the exact division over every 16-bit gate value
+int selftest_silu(int dtype, int* mismatches, cudaStream_t st);
 
 // tensor maps (grouped_gemm.cu): int8 [rows, K] with a 64-row x 128-byte, 128B-swizzled box;
 // 16-bit activations [rows, K] with a box_rows x 64-element, 128B-swizzled box

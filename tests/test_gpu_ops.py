@@ -371,3 +371,13 @@ def test_routed_moe_golden_fp16():
                                 torch.from_numpy(rr['ids']).cuda(), dev)
     ref = f16bits(GOLD['rmoe_gpuplan'])
     assert rel_maxabs(to_np(out), ref) < 4e-3
+
+
+@pytest.mark.parametrize('dtype', [BF16, F16])
+def test_swiglu_silu_matches_exact_division_for_every_input(dtype):
+    """The gate_up epilogue's branch-free SiLU (a Markstein-corrected reciprocal) equals
+    fp32 g / (1 + expf(-g)) with an IEEE division for all 65,536 16-bit gate values."""
+    from localmoe35ba3b_b200 import _native as N
+    cnt = torch.zeros(1, dtype=torch.int32, device='cuda')
+    N.call('lmoe_selftest_silu', N.dtype_code(TORCH_DT[dtype]), N.ptr(cnt), N.stream(cnt.device))
+    assert int(cnt.item()) == 0

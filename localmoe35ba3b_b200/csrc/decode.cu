@@ -163,6 +163,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   __shared__ int64_t s_eid[kDecodeMaxTop];
   __shared__ float s_w[kDecodeMaxTop];
   __shared__ float red[kDecWarps];
+  __shared__ float s_t[kDecWarps][32];  // phase 2: per warp, its lanes' group terms
   const int lane = lane_id(), warp = warp_id();
   const int top = a.top;
   const int64_t H = a.H, I = a.I;
@@ -186,50 +187,66 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   }
   __syncthreads();
 
-  // copies of one block, spread over the lanes of warp 0 (one bulk copy per lane):
+  // Copies of one block.  A warp's bulk copies issue one after another (tens of ns
+  // each), so a block's copies are spread over the warps: expect_* (warp 0, its lanes)
+  // arms the barriers, copy_*(blk, k) issues copy k from the calling thread.  A copy
+  // that lands before its barrier is armed is fine: the barrier's phase cannot complete
+  // before the arming arrival.
   // gate_up block blk = pieces of 8 columns, each on its own barrier (gate rows, up
   // rows, their scales: 4 copies per piece), so warps start as their rows land
-  auto issue_gu = [&](int blk) {
+  const int n_gu_copies = 4 * npieces, n_dn_copies = 2 * rows;
+  auto expect_gu = [&]() {
+    const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
+    if (lane < npieces) mbar_arrive_expect_tx(sb + (uint32_t)G.bars + 8u * lane, 2 * (wbytes + sbytes));
+  };
+  auto copy_gu = [&](int blk, int k) {
     const int r = blk / nblk;
     const int64_t c0 = (int64_t)(blk % nblk) * a.CB;
     const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
-    if (lane < npieces) mbar_arrive_expect_tx(sb + (uint32_t)G.bars + 8u * lane, 2 * (wbytes + sbytes));
-    __syncwarp();
-    for (int k = lane; k < 4 * npieces; k += 32) {
-      const int p = k >> 2, which = k & 3;
-      const uint32_t bar = sb + (uint32_t)G.bars + 8u * p;
-      const int64_t row = c0 + p * 8 + ((which & 1) ? I : 0);  // gate rows, then up rows
-      if (r < top) {
-        const int64_t e = s_eid[r];
-        if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), a.qg + (e * 2 * I + row) * H, wbytes, bar);
-        else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), a.sg + (e * 2 * I + row) * GH, sbytes, bar);
-      } else {
-        const int64_t srow = c0 + p * 8;
-        const int8_t* q = (which & 1) ? a.sh_qu : a.sh_qg;
-        const float* sc = (which & 1) ? a.sh_su : a.sh_sg;
-        if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), q + srow * H, wbytes, bar);
-        else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), sc + srow * GH, sbytes, bar);
-      }
+    const int p = k >> 2, which = k & 3;
+    const uint32_t bar = sb + (uint32_t)G.bars + 8u * p;
+    const int64_t row = c0 + p * 8 + ((which & 1) ? I : 0);  // gate rows, then up rows
+    if (r < top) {
+      const int64_t e = s_eid[r];
+      if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), a.qg + (e * 2 * I + row) * H, wbytes, bar);
+      else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), a.sg + (e * 2 * I + row) * GH, sbytes, bar);
+    } else {
+      const int64_t srow = c0 + p * 8;
+      const int8_t* q = (which & 1) ? a.sh_qu : a.sh_qg;
+      const float* sc = (which & 1) ? a.sh_su : a.sh_sg;
+      if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), q + srow * H, wbytes, bar);
+      else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), sc + srow * GH, sbytes, bar);
     }
   };
   // down block blk: per row (routed experts in ascending order, then the shared
   // expert) its CBd weight rows and their scales, all on one barrier
-  auto issue_dn = [&](int blk) {
+  auto expect_dn = [&]() {
+    const uint32_t wb = (uint32_t)(a.CBd * I), sbt = (uint32_t)(a.CBd * GI * 4);
+    if (lane == 0) mbar_arrive_expect_tx(sd0 + (uint32_t)D.bar, (uint32_t)rows * (wb + sbt));
+  };
+  auto copy_dn = [&](int blk, int k) {
     const int64_t n0 = (int64_t)blk * a.CBd;
     const uint32_t wb = (uint32_t)(a.CBd * I), sbt = (uint32_t)(a.CBd * GI * 4);
     const uint32_t bar = sd0 + (uint32_t)D.bar;
-    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)rows * (wb + sbt));
-    __syncwarp();
-    for (int k = lane; k < 2 * rows; k += 32) {
-      const int rr = k >> 1;
-      if ((k & 1) == 0) {
-        const int8_t* q = rr < top ? a.qd + (s_eid[rr] * H + n0) * I : a.sh_qd + n0 * I;
-        bulk_g2s(sd0 + (uint32_t)(D.w + (int64_t)rr * a.CBd * I), q, wb, bar);
-      } else {
-        const float* sc = rr < top ? a.sd + (s_eid[rr] * H + n0) * GI : a.sh_sd + n0 * GI;
-        bulk_g2s(sd0 + (uint32_t)(D.sc + (int64_t)rr * a.CBd * GI * 4), sc, sbt, bar);
-      }
+    const int rr = k >> 1;
+    if ((k & 1) == 0) {
+      const int8_t* q = rr < top ? a.qd + (s_eid[rr] * H + n0) * I : a.sh_qd + n0 * I;
+      bulk_g2s(sd0 + (uint32_t)(D.w + (int64_t)rr * a.CBd * I), q, wb, bar);
+    } else {
+      const float* sc = rr < top ? a.sd + (s_eid[rr] * H + n0) * GI : a.sh_sd + n0 * GI;
+      bulk_g2s(sd0 + (uint32_t)(D.sc + (int64_t)rr * a.CBd * GI * 4), sc, sbt, bar);
     }
+  };
+  // one warp issues all of a block's copies (later blocks, which are rare)
+  auto issue_gu = [&](int blk) {
+    expect_gu();
+    __syncwarp();
+    for (int k = lane; k < n_gu_copies; k += 32) copy_gu(blk, k);
+  };
+  auto issue_dn = [&](int blk) {
+    expect_dn();
+    __syncwarp();
+    for (int k = lane; k < n_dn_copies; k += 32) copy_dn(blk, k);
   };
 
   // launched so that it may start before the previous kernel ends: the ids, the
@@ -238,26 +255,41 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   grid_dep_wait();
   int8_t* xq = reinterpret_cast<int8_t*>(smem + G.xq);
   float* xs = reinterpret_cast<float*>(smem + G.xs);
+  const bool has_gu = (int)blockIdx.x < a.n_gu, first_dn = !has_gu && (int)blockIdx.x < a.n_dn;
   if (warp == 0) {
-    // the experts' order, their routing weights, then both phases' first blocks
+    // the experts' order and their routing weights; arm the first block's barriers
     expert_ranks_w(a.ids, a.weights, top, a.E, s_eid, s_w, a.err, blockIdx.x == 0);
     __syncwarp();
-    if ((int)blockIdx.x < a.n_gu) issue_gu(blockIdx.x);
+    if (has_gu) expect_gu();
     // a CTA with no gate_up block streams its down rows at once; the others once their
     // gate_up rows have landed, so that the two phases do not share the HBM stream
-    else if ((int)blockIdx.x < a.n_dn) issue_dn(blockIdx.x);
+    else if (first_dn) expect_dn();
   } else {
-    // meanwhile the other warps quantise x (W8A8) and form the shared gate's logit
-    if (W8A8)
-      for (int g = warp - 1; g < GH; g += kDecWarps - 1) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
-    if (gated) {
-      const T* gw = (const T*)a.gate_w;
-      float part = 0.f;
-      for (int64_t c = threadIdx.x - 32; c < H; c += kDecThreads - 32) part = fmaf(A::to_f(x[c]), A::to_f(gw[c]), part);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      if (lane == 0) red[warp] = part;
+    // meanwhile the other warps pull x (and the shared gate's weight) towards L1
+    for (int64_t c = (int64_t)(threadIdx.x - 32) * 64; c < H; c += (int64_t)(kDecThreads - 32) * 64) {
+      prefetch_l1(x + c);
+      if (gated) prefetch_l1((const T*)a.gate_w + c);
     }
+  }
+  __syncthreads();
+  // the first block's copies, one warp each
+  if (lane == 0) {
+    if (has_gu)
+      for (int k = warp; k < n_gu_copies; k += kDecWarps) copy_gu(blockIdx.x, k);
+    else if (first_dn)
+      for (int k = warp; k < n_dn_copies; k += kDecWarps) copy_dn(blockIdx.x, k);
+  }
+  __syncwarp();
+  // every warp quantises groups of x (W8A8) and forms part of the shared gate's logit
+  if (W8A8)
+    for (int g = warp; g < GH; g += kDecWarps) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
+  if (gated && warp > 0) {
+    const T* gw = (const T*)a.gate_w;
+    float part = 0.f;
+    for (int64_t c = threadIdx.x - 32; c < H; c += kDecThreads - 32) part = fmaf(A::to_f(x[c]), A::to_f(gw[c]), part);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0) red[warp] = part;
   }
   __syncthreads();
 
@@ -288,11 +320,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
       }
       if (lane == 0) hid[(int64_t)r * I + c0 + j] = A::from_f(__fmul_rn(A::round(silu_exact(A::round(g))), A::round(u)));
     }
-    if (it == 0 && warp == 0 && (int)blockIdx.x < a.n_dn) {
-      // all of this CTA's first gate_up pieces have landed: its down rows go out now
+    if (it == 0 && (int)blockIdx.x < a.n_dn && warp < n_dn_copies) {
+      // all of this CTA's first gate_up pieces have landed: its down rows go out now,
+      // from each warp that has a down copy to issue once its own columns are done
       for (int p = 0; p < npieces; ++p)
         if (!mbar_wait_drain(sb + (uint32_t)G.bars + 8u * p, 0, a.err)) ok = 0;
-      issue_dn(blockIdx.x);
+      if (warp == 0) expect_dn();
+      if (lane == 0)
+        for (int k = warp; k < n_dn_copies; k += kDecWarps) copy_dn(blockIdx.x, k);
+      __syncwarp();
     }
     ok = __syncthreads_and(ok);  // every warp is done with this block's rows
     if (warp == 0 && ok && blk + (int)gridDim.x < a.n_gu) issue_gu(blk + gridDim.x);
@@ -308,18 +344,51 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   // ---- phase 2: down + ordered combine + gated shared expert + residual
   int8_t* hq = reinterpret_cast<int8_t*>(dsm + D.hq);
   float* hs = reinterpret_cast<float*>(dsm + D.hs);
-  if ((int)blockIdx.x < a.n_dn && W8A8) {
-    for (int t = warp; t < top * GI; t += kDecWarps) {
-      const int rr = t / GI, g = t % GI;
-      // the hidden rows come from other CTAs: read through L2
-      const T* src = hid + (int64_t)rr * I + g * kGroup;
-      float v[4];
-      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(src + lane * 4));
-      v[0] = A::lo_f(raw.x);
-      v[1] = A::hi_f(raw.x);
-      v[2] = A::lo_f(raw.y);
-      v[3] = A::hi_f(raw.y);
-      quant_vals(v, hq + (int64_t)rr * I + g * kGroup, hs + rr * GI + g, lane);
+  // the hidden rows (routed and shared, activation dtype) in the phase-1 region, whose
+  // reads and copies are all complete
+  const T* hx = reinterpret_cast<const T*>(smem + G.wg);
+  if ((int)blockIdx.x < a.n_dn) {
+    // every hidden row into shared memory in one L2 round trip (the rows come from
+    // other CTAs: read through L2), then the W8A8 quantisation from there
+    const int n16 = (int)(rows * I * 2 / 16);
+    const uint32_t hx0 = sb + (uint32_t)G.wg;
+    for (int b0 = 0; b0 < n16; b0 += 2 * kDecThreads) {
+      uint4 v[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int idx = b0 + i * kDecThreads + (int)threadIdx.x;
+        if (idx < n16) v[i] = __ldcg(reinterpret_cast<const uint4*>(hid) + idx);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int idx = b0 + i * kDecThreads + (int)threadIdx.x;
+        if (idx < n16) sts128(hx0 + (uint32_t)idx * 16u, v[i]);
+      }
+    }
+    __syncthreads();
+    if (W8A8) {
+      // two (row, group) quantisations per pass, independent so that they overlap
+      for (int t0 = warp; t0 < top * GI; t0 += 2 * kDecWarps) {
+        float v[2][4];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int t = min(t0 + u * kDecWarps, top * GI - 1);
+          const int rr = t / GI, g = t % GI;
+          const uint2 raw = *reinterpret_cast<const uint2*>(hx + (int64_t)rr * I + g * kGroup + lane * 4);
+          v[u][0] = A::lo_f(raw.x);
+          v[u][1] = A::hi_f(raw.x);
+          v[u][2] = A::lo_f(raw.y);
+          v[u][3] = A::hi_f(raw.y);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int t = t0 + u * kDecWarps;
+          if (t < top * GI) {
+            const int rr = t / GI, g = t % GI;
+            quant_vals(v[u], hq + (int64_t)rr * I + g * kGroup, hs + rr * GI + g, lane);
+          }
+        }
+      }
     }
   }
   __syncthreads();
@@ -348,6 +417,41 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
       const int64_t n = n0 + j;
       if (j != j0 && res != nullptr) resv = A::to_f(res[n]);
       float acc = 0.f;
+      if (W8A8 && top * GI <= 32) {
+        // one lane per (routed row rr = lane / GI, 128-group g = lane % GI): the group's
+        // exact int32 dot (8 chunks, visited from a lane-dependent start so that the 8
+        // lanes of a shared-memory phase read different banks), t = (dot * xs) * ws;
+        // then lane 0 adds each row's groups in group order and folds the rows in
+        // ascending expert order, as row_dot_w8a8 and the combine below do
+        const int rr = lane / GI, g = lane - rr * GI;
+        float t = 0.f;
+        if (rr < top) {
+          const uint32_t wrow = sd0 + (uint32_t)(D.w + ((int64_t)rr * a.CBd + j) * I + g * kGroup);
+          const uint32_t xrow = smem_u32(hq + (int64_t)rr * I + g * kGroup);
+          int dsum = 0;
+#pragma unroll
+          for (int c = 0; c < kGroup / 16; ++c) {
+            const uint32_t off = (uint32_t)(((c + lane) & 7) * 16);
+            const uint4 wv = lds128(wrow + off), xv = lds128(xrow + off);
+            dsum = dp4a(wv.x, xv.x, dsum);
+            dsum = dp4a(wv.y, xv.y, dsum);
+            dsum = dp4a(wv.z, xv.z, dsum);
+            dsum = dp4a(wv.w, xv.w, dsum);
+          }
+          t = __fmul_rn(__fmul_rn((float)dsum, hs[rr * GI + g]), scs[((int64_t)rr * a.CBd + j) * GI + g]);
+        }
+        s_t[warp][lane] = t;
+        __syncwarp();
+        if (lane == 0) {
+          for (int r = 0; r < top; ++r) {
+            float v = 0.f;
+            for (int q = 0; q < GI; ++q) v = __fadd_rn(v, s_t[warp][r * GI + q]);
+            acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::round(v), s_w[r]))));
+          }
+        }
+        acc = __shfl_sync(0xffffffffu, acc, 0);
+        __syncwarp();
+      } else {
       constexpr int kDecRows = MAXD == 1 ? kDecRowsMax : 1;  // keep the rows' chunks in registers
       for (int r0 = 0; r0 < top; r0 += kDecRows) {
         uint4 w[kDecRows][MAXD];
@@ -368,17 +472,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
         } else {
 #pragma unroll
           for (int k = 0; k < kDecRows; ++k)
-            v[k] = row_dot_w16<DT, MAXD, true>(w[k], srow[k], hid + (int64_t)min(r0 + k, top - 1) * I, chunks2, lane);
+            v[k] = row_dot_w16<DT, MAXD>(w[k], srow[k], hx + (int64_t)min(r0 + k, top - 1) * I, chunks2, lane);
         }
 #pragma unroll
         for (int k = 0; k < kDecRows; ++k)
           if (r0 + k < top) acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::round(v[k]), s_w[r0 + k]))));
       }
+      }
       if (with_shared) {
         uint4 w[MAXD];
         row_lds(sd0 + (uint32_t)(D.w + ((int64_t)top * a.CBd + j) * I), chunks2, lane, w);
         const float sv = A::round(
-            row_dot_w16<DT, MAXD, true>(w, scs + ((int64_t)top * a.CBd + j) * GI, hid + (int64_t)top * I, chunks2, lane));
+            row_dot_w16<DT, MAXD>(w, scs + ((int64_t)top * a.CBd + j) * GI, hx + (int64_t)top * I, chunks2, lane));
         acc = A::round(__fadd_rn(acc, gated ? A::round(__fmul_rn(sig, sv)) : sv));
       }
       if (res != nullptr) acc = A::round(__fadd_rn(resv, acc));
@@ -410,7 +515,9 @@ static bool pick_blocks(int64_t rows, int64_t top, int64_t H, int64_t I, int& cb
   for (cb = 32; cb >= 8; cb >>= 1) {
     if (I % cb) continue;
     for (cbd = 16; cbd >= 4; cbd >>= 1)
-      if (H % cbd == 0 && a128(GuSmem(cb, H).bytes) + DnSmem(rows, top, cbd, I).bytes <= kDecSmemMax) return true;
+      if (H % cbd == 0 && a128(GuSmem(cb, H).bytes) + DnSmem(rows, top, cbd, I).bytes <= kDecSmemMax &&
+          rows * I * 2 <= GuSmem(cb, H).bytes)  // phase 2 stages the hidden rows in the phase-1 region
+        return true;
   }
   return false;
 }

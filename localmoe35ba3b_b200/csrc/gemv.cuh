@@ -207,16 +207,17 @@ __device__ __forceinline__ float row_dot_w16(const uint4 (&w)[MAXI], const float
     const uint4 xb = CG ? __ldcg(xp + 1) : xp[1];
     const uint32_t wv[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
     const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    const uint64_t sc2 = splat2(sc);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float f0, f1, f2, f3;
-      i8x4_to_f32(wv[j], f0, f1, f2, f3);
-      const float w0 = Act<DT>::round(__fmul_rn(f0, sc)), w1 = Act<DT>::round(__fmul_rn(f1, sc));
-      const float w2 = Act<DT>::round(__fmul_rn(f2, sc)), w3 = Act<DT>::round(__fmul_rn(f3, sc));
-      acc = fmaf(Act<DT>::lo_f(xw[2 * j]), w0, acc);
-      acc = fmaf(Act<DT>::hi_f(xw[2 * j]), w1, acc);
-      acc = fmaf(Act<DT>::lo_f(xw[2 * j + 1]), w2, acc);
-      acc = fmaf(Act<DT>::hi_f(xw[2 * j + 1]), w3, acc);
+      // round_dtype(q * s) for the word's 4 weights, two to a register (deq4: packed
+      // f32x2 products, the same bits as one product and one rounding per weight)
+      uint32_t lo, hi;
+      deq4<DT>(wv[j], sc2, lo, hi);
+      acc = fmaf(Act<DT>::lo_f(xw[2 * j]), Act<DT>::lo_f(lo), acc);
+      acc = fmaf(Act<DT>::hi_f(xw[2 * j]), Act<DT>::hi_f(lo), acc);
+      acc = fmaf(Act<DT>::lo_f(xw[2 * j + 1]), Act<DT>::lo_f(hi), acc);
+      acc = fmaf(Act<DT>::hi_f(xw[2 * j + 1]), Act<DT>::hi_f(hi), acc);
     }
   }
 #pragma unroll

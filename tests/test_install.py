@@ -35,10 +35,10 @@ def _quant(r, shape):
     return torch.from_numpy(q), torch.from_numpy(s)
 
 
-def _model(r, layers=2, float_experts=False):
+def _model(r, layers=2, float_experts=False, experts=E):
     hf = pytest.importorskip('transformers.models.qwen3_5_moe.modeling_qwen3_5_moe')
     cfg_mod = pytest.importorskip('transformers.models.qwen3_5_moe.configuration_qwen3_5_moe')
-    cfg = cfg_mod.Qwen3_5MoeTextConfig(hidden_size=H, num_experts=E, num_experts_per_tok=TOP,
+    cfg = cfg_mod.Qwen3_5MoeTextConfig(hidden_size=H, num_experts=experts, num_experts_per_tok=TOP,
                                        moe_intermediate_size=I, shared_expert_intermediate_size=I,
                                        hidden_act='silu')
     cfg._experts_implementation = 'eager'
@@ -50,8 +50,8 @@ def _model(r, layers=2, float_experts=False):
         layer.self_attn.o_proj = RefInt8Linear(*_quant(r, (H, 2 * H)))
         mlp = hf.Qwen3_5MoeSparseMoeBlock(cfg).to(torch.bfloat16)
         if not float_experts:
-            gq, gs = _quant(r, (E, 2 * I, H))
-            dq, ds = _quant(r, (E, H, I))
+            gq, gs = _quant(r, (experts, 2 * I, H))
+            dq, ds = _quant(r, (experts, H, I))
             mlp.experts = RefInt8Experts({'q': gq, 'scale': gs}, {'q': dq, 'scale': ds})
         for p in ('gate_proj', 'up_proj', 'down_proj'):
             setattr(mlp.shared_expert, p, RefInt8Linear(*_quant(r, (I, H) if p != 'down_proj' else (H, I))))
@@ -92,3 +92,46 @@ def test_install_refuses_float_experts_and_bad_arguments():
         install(torch.nn.Module(), activation='fp8')
     with pytest.raises(ValueError, match='pass the model'):
         install(RefInt8Linear(*_quant(np.random.default_rng(9), (128, 256))))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize('T', [1, 37])
+def test_installed_model_forward_matches_oracle(T):
+    """After install(model) on cuda, each layer's replaced modules run the B200 kernels:
+    the o_proj Int8Linear against the oracle's W8A16 linear, and the sparse-MoE block
+    (router on the GPU, then the prefill block or, for one token, the W8A8 decode chain)
+    against the oracle block on the same routing.  32 experts: the smallest count the
+    device router takes."""
+    import torch.nn.functional as F
+    from localmoe35ba3b_b200.runtime.install import install
+    r = np.random.default_rng(31 + T)
+    model = _model(r, experts=32)
+    truth = []
+    for layer in model.layers:
+        m = layer.mlp
+        truth.append(((m.experts.gate_up['q'].numpy(), m.experts.gate_up['scale'].numpy(),
+                       m.experts.down['q'].numpy(), m.experts.down['scale'].numpy()),
+                      [(getattr(m.shared_expert, p).q.numpy(), getattr(m.shared_expert, p).scale.numpy())
+                       for p in ('gate_proj', 'up_proj', 'down_proj')],
+                      m.shared_expert_gate.weight.detach().float().numpy().reshape(1, -1),
+                      (layer.self_attn.o_proj.q.numpy(), layer.self_attn.o_proj.scale.numpy())))
+    activation = 'w8a8' if T == 1 else 'w8a16'
+    assert install(model, activation=activation, device='cuda') == {'blocks': 2, 'linears': 2}
+    x = O.to_bf16(r.standard_normal((T, H), dtype=np.float32))
+    x2 = O.to_bf16(r.standard_normal((T, 2 * H), dtype=np.float32))
+    for layer, (bank, shared, gate_w, (oq, os_)) in zip(model.layers, truth):
+        xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+        out = layer.mlp(xd.reshape(1, T, H))
+        y = layer.self_attn.o_proj(torch.from_numpy(x2).to(torch.bfloat16).cuda())
+        torch.cuda.synchronize()
+        logits = F.linear(xd, layer.mlp.gate.weight).float().cpu().numpy()
+        ids, w = O.route(logits, TOP)
+        if T == 1:
+            ref = O.decode_block(x, ids, w, bank, shared, O.to_bf16(gate_w), activation, 'bf16')
+        else:
+            ref = O.moe_block(x, w, ids, bank, shared, O.to_bf16(gate_w), 'bf16')
+        got = out.float().cpu().numpy().reshape(T, H)
+        assert np.abs(got - ref).max() / np.abs(ref).max() < 1e-2
+        ref_y = O.linear_w8a16(x2, oq, os_, 'bf16')
+        got_y = y.float().cpu().numpy()
+        assert np.abs(got_y - ref_y).max() / np.abs(ref_y).max() < 1e-2

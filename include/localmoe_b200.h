@@ -58,9 +58,19 @@ LMOE_API int lmoe_quantize_rows(const void* x, int8_t* q, float* s, int64_t rows
 
 /* Replaces int8.linear / int8._linear (qwen35_deploy/operators/int8.py:9-37).
  * y[m, n] = sum_k x[m, k] * round_dtype(q[n, k] * scale[n, k/128]), fp32 accumulation.
- * Small m runs an HBM-streaming GEMV; large m a tcgen05 tensor-core GEMM. */
+ * One row runs an HBM-streaming GEMV; more rows a tcgen05 tensor-core GEMM (the weights
+ * on the MMA's M side when n % 128 == 0). */
 LMOE_API int lmoe_linear_w8a16(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n,
                       int64_t k, int dtype, int* err, void* stream);
+
+/* The same linear with a scratch workspace (no reference counterpart beyond int8.linear):
+ * when its (128-row tile, 128-column block) units would not fill the GPU, the
+ * tensor-core kernel splits K over lmoe_linear_w8a16_workspace_size(m, n, k) bytes of ws
+ * (fp32 partial sums, added in split order, rounded once).  A size of 0 means no split;
+ * ws may then be NULL.  With a smaller ws the call runs without splitting. */
+LMOE_API int64_t lmoe_linear_w8a16_workspace_size(int64_t m, int64_t n, int64_t k);
+LMOE_API int lmoe_linear_w8a16_ws(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n,
+                                  int64_t k, int dtype, void* ws, int64_t ws_bytes, int* err, void* stream);
 
 /* Replaces int8.grouped_linear / int8._grouped_linear (qwen35_deploy/operators/int8.py:213-237).
  * table is a device int64 [experts, 5] of (gate_up.q, gate_up.scale, down.q, down.scale, slot);

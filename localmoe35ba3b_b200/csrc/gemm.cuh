@@ -32,6 +32,8 @@ struct GemmLaunch {
   int mode;
   int dtype;
   int* err;
+  int ksplit;             // TS down kernel, dense mode: K splits (fp32 sums to partial)
+  float* partial;
 };
 
 int launch_grouped_gemm(const GemmLaunch& L, cudaStream_t st);
@@ -41,6 +43,12 @@ int launch_swiglu_ts(const GemmLaunch& L, cudaStream_t st);
 int launch_down_ts(const GemmLaunch& L, cudaStream_t st);
 // the SwiGLU epilogue's SiLU against the exact division over every 16-bit gate value
 int selftest_silu(int dtype, int* mismatches, cudaStream_t st);
+// dense W8A16 linear on the TS kernel (gemm_ts.cu): n % 128 == 0, k % 128 == 0; K split over
+// dense_ts_workspace bytes of ws when the units would not fill the SMs (ws == nullptr: no split)
+bool dense_ts_ok(int64_t m, int64_t n, int64_t k);
+int64_t dense_ts_workspace(int64_t m, int64_t n, int64_t k);
+int launch_dense_ts(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n, int64_t k,
+                    int dtype, void* ws, int64_t ws_bytes, int* err, cudaStream_t st);
 
 // tensor maps (grouped_gemm.cu): int8 [rows, K] with a 64-row x 128-byte, 128B-swizzled box;
 // 16-bit activations [rows, K] with a box_rows x 64-element, 128B-swizzled box

@@ -98,10 +98,18 @@ struct Params {
   void* y;                 // gate_up: hidden [rows, I]; down: weighted rows [rows, hidden]
   int64_t ldy;
   int* err;
+  // dense linear (tiles == nullptr): tiles of <= 128 of the dense_rows rows, expert 0
+  int64_t dense_rows;
+  // split K: unit u covers K stages [ks * gs, min(G, (ks + 1) * gs)) of its tile and block,
+  // ks = u % ksplit; with ksplit > 1 (down only) the epilogue stores the fp32 sums to
+  // partial[ks][row][ldy] instead of y
+  int ksplit;
+  float* partial;
 };
 
 struct Unit {
   int start, count, nb, expert;
+  int ks, g0, g1;  // K split and its stage range
   bool shared;
   int64_t rlo, rhi;  // tensor-map rows of the unit's two 64-row halves (gate_up: gate, up)
 };
@@ -111,9 +119,23 @@ struct Unit {
 // (128 consecutive rows of the expert's down weight).
 template <bool DOWN>
 __device__ __forceinline__ bool get_unit(const Params& p, int u, int nblocks, Unit& o) {
+  const int S = p.ksplit;
+  o.ks = u % S;
+  u /= S;
   const int t = u / nblocks;
-  if (t >= p.hdr[kHdrNumTiles]) return false;
-  const Tile tl = p.tiles[t];
+  Tile tl;
+  if (p.tiles == nullptr) {
+    if ((int64_t)t * kTileRoutes >= p.dense_rows) return false;
+    tl.expert = 0;
+    tl.start = t * kTileRoutes;
+    tl.count = (int)min((int64_t)kTileRoutes, p.dense_rows - (int64_t)t * kTileRoutes);
+  } else {
+    if (t >= p.hdr[kHdrNumTiles]) return false;
+    tl = p.tiles[t];
+  }
+  const int G = (int)(p.K / kBK8), gs = (G + S - 1) / S;
+  o.g0 = o.ks * gs;
+  o.g1 = min(G, o.g0 + gs);
   o.nb = u - t * nblocks;
   o.expert = tl.expert;
   o.start = tl.start;
@@ -243,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; ok; u += stride) {
         Unit un;
         if (!get_unit<DOWN>(p, u, nblocks, un)) break;
-        for (int g = 0; g < G; ++g, ++it) {
+        for (int g = un.g0; g < un.g1; ++g, ++it) {
           if ((it & 1) != mine) continue;
           const int s8 = it % kNS8;
           if (!mbar_wait(empty8(s8), ((it / kNS8) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
@@ -285,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(tempty(b), ((ui >> 1) & 1) ^ 1, sAbort, p.err)) break;
         tc_fence_after();
         const uint32_t dt = tmem + (uint32_t)(b * kAccCols);
-        for (int g = 0; g < G; ++g, ++it) {
+        for (int g = un.g0; g < un.g1; ++g, ++it) {
           const int s = it % kNA;
           if (!mbar_wait(ready(s), (it / kNA) & 1, sAbort, p.err)) { ok = false; break; }
           tc_fence_after();
@@ -296,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kBKB / 16; ++kk)
               mma_f16_ts(dt, acol + (uint32_t)(h * 32 + kk * 8), bd + (uint64_t)(((h * kBBytes) >> 4) + kk * 2), idesc,
-                         (g | h | kk) != 0);
+                         (g != un.g0) || ((h | kk) != 0));
           mma_commit(freed(s));
           issued = true;
         }
@@ -331,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool big = un.count > 3 * kBoxRows;
         const int nbox = big ? 1 : (un.count + kBoxRows - 1) / kBoxRows;
         const uint32_t bytes = kBChunks * (big ? (uint32_t)kBBytes : (uint32_t)(nbox * kBoxRows * kBKB * 2));
-        for (int g = 0; g < G; ++g, ++ib) {
+        for (int g = un.g0; g < un.g1; ++g, ++ib) {
           const int s = ib % kNA;
           if (!mbar_wait(freed(s), ((ib / kNA) & 1) ^ 1, sAbort, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(ready(s), bytes);
@@ -378,10 +400,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t rmax = un.shared ? p.rows_sh : p.rows_bank;
       const float* sp = (un.shared ? (up ? p.s_u : p.s_g) : p.s_bank) + grow * G;
       const bool valid = grow < rmax;
-      float sc = valid ? __ldg(sp) : 0.f;
-      float sn = (G > 1 && valid) ? __ldg(sp + 1) : 0.f;
-      float sm = (G > 2 && valid) ? __ldg(sp + 2) : 0.f;
-      for (int g = 0; g < G; ++g, ++it8) {
+      float sc = valid ? __ldg(sp + un.g0) : 0.f;
+      float sn = (un.g0 + 1 < un.g1 && valid) ? __ldg(sp + un.g0 + 1) : 0.f;
+      float sm = (un.g0 + 2 < un.g1 && valid) ? __ldg(sp + un.g0 + 2) : 0.f;
+      for (int g = un.g0; g < un.g1; ++g, ++it8) {
         const int s8 = it8 % kNS8;
         const int a = it8 % kNA;
         if (!warp_wait(full8(s8), (it8 / kNS8) & 1, sAbort, p.err)) { ok = false; break; }
@@ -408,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         sc = sn;
         sn = sm;
-        sm = (g + 3 < G && valid) ? __ldg(sp + g + 3) : 0.f;
+        sm = (g + 3 < un.g1 && valid) ? __ldg(sp + g + 3) : 0.f;
       }
     }
   } else if (warp >= 12) {
@@ -430,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // down: this thread's route weight loads before the accumulator wait, so its
       // latency overlaps it (shared-expert rows are not weighted)
       float wrow = 1.f;
-      if (DOWN && !un.shared && row < un.count) wrow = __ldg(p.rweight + un.start + row);
+      if (DOWN && p.rweight != nullptr && !un.shared && row < un.count) wrow = __ldg(p.rweight + un.start + row);
       if (q == 0 && lane == 0) *sHave = mbar_wait_drain(tfull(b), (ui >> 1) & 1, p.err) ? 1u : 0u;
       named_barrier(1, 128);
       const bool have = *sHave != 0;
@@ -452,6 +474,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!have) continue;
         if constexpr (DOWN) {
+          if (p.partial != nullptr) {
+            // split K: this split's fp32 sums, route rows of ldy floats (a warp stores 32
+            // consecutive columns of one route at a time)
+            const int ntok = min(32, un.count - c * 32);
+            float* dst = p.partial + ((int64_t)un.ks * p.dense_rows + un.start + c * 32) * p.ldy + col0 + row;
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj)
+              if (jj < ntok) dst[(int64_t)jj * p.ldy] = __uint_as_float(acc[jj]);
+            continue;
+          }
           // lane = output column col0 + row of the unit; per route j of the chunk
           // v = round(round(acc) * w_route) (shared-expert rows: round(acc)), written
           // transposed to a [32 routes][128 columns] 16-bit stage, then 16-byte row
@@ -472,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
             float v = A::round(__uint_as_float(acc[jj]));
-            if (!un.shared) v = __fmul_rn(v, w[jj]);
+            if (p.rweight != nullptr && !un.shared) v = __fmul_rn(v, w[jj]);
             st[jj * kDPitch + row] = A::bits(v);
           }
           named_barrier(2, 128);
@@ -592,7 +624,10 @@ static int launch_ts(const GemmLaunch& L, cudaStream_t st) {
   p.y = L.y;
   p.ldy = L.ldy;
   p.err = L.err;
-  const int64_t units = (DOWN ? L.N / 128 : L.inter / 64) * L.grid_tiles;
+  p.dense_rows = L.tiles == nullptr ? L.dense_rows : 0;
+  p.ksplit = L.ksplit > 1 ? L.ksplit : 1;
+  p.partial = L.partial;
+  const int64_t units = (DOWN ? L.N / 128 : L.inter / 64) * L.grid_tiles * p.ksplit;
   const int64_t sms = sm_count();
   const int64_t ctas = units < sms ? units : sms;
   const size_t smem = ts::Smem::alloc;
@@ -654,7 +689,7 @@ int selftest_silu(int dtype, int* mismatches, cudaStream_t st) {
 }
 
 int launch_down_ts(const GemmLaunch& L, cudaStream_t st) {
-  if (L.mode != kWeighted || L.tiles == nullptr || L.rweight == nullptr) return LMOE_ERR_INVALID;
+  if (L.mode != kWeighted || L.tiles == nullptr || L.rweight == nullptr || L.ksplit > 1) return LMOE_ERR_INVALID;
   if (L.K % kGroup || L.K <= 0 || L.N % 128 || L.N <= 0) return LMOE_ERR_INVALID;
   return launch_ts<true>(L, st);
 }
@@ -664,3 +699,110 @@ int launch_down_ts(const GemmLaunch& L, cudaStream_t st) {
 extern "C" int lmoe_selftest_silu(int dtype, int* mismatches, void* stream) {
   return lmoe::selftest_silu(dtype, mismatches, (cudaStream_t)stream);
 }
+
+// ============================================================================
+// Dense W8A16 linear on the TMEM-operand kernel (the down kernel's geometry with no
+// routing weight): y[m, n] = sum_k x[m, k] * round(q[n, k] * s[n, k/128]), the MMA's M
+// side 128 weight rows, its N side up to 128 of the m rows, so that small m still
+// streams the weights at full width.  When the (row tile, 128-column block) units are
+// fewer than the SMs, K is split: each split stores fp32 sums to the workspace and
+// dense_reduce_kernel adds the splits in order and rounds once.
+namespace lmoe {
+namespace {
+// The split that minimises an estimate of the call's time: rounds of units on the busiest
+// SM x (stages per unit + about one stage of per-unit fill and epilogue) x ~0.45 us per
+// 128-K stage, plus the fp32 partial sums written and read back (8 bytes per output per
+// split) at ~6 TB/s.  Every split is non-empty.
+int dense_ksplit(int64_t m, int64_t n, int64_t k) {
+  const int64_t units = ((m + kTileRoutes - 1) / kTileRoutes) * (n / 128);
+  const int G = (int)(k / kGroup);
+  const int64_t sms = sm_count();
+  const double stage_us = 0.45, part_us_per_byte = 1.0 / 6.0e6;
+  int best = 1;
+  double best_cost = (double)((units + sms - 1) / sms) * (G + 1) * stage_us;
+  for (int want = 2; want <= G; ++want) {
+    const int gs = (G + want - 1) / want;
+    const int S = (G + gs - 1) / gs;
+    const double cost = (double)((units * S + sms - 1) / sms) * (gs + 1) * stage_us +
+                        (double)S * (double)m * (double)n * 8.0 * part_us_per_byte;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = S;
+    }
+  }
+  return best;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) dense_reduce_kernel(const float* __restrict__ part, typename Act<DT>::T* y,
+                                                           int64_t total, int splits) {
+  grid_dep_wait();
+  const int64_t i4 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i4 >= total) return;
+  if (i4 + 4 <= total) {
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(part + i4));
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)s * total + i4));
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    uint2 o;
+    o.x = Act<DT>::pack(acc.x, acc.y);
+    o.y = Act<DT>::pack(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(y + i4) = o;
+  } else {
+    for (int64_t i = i4; i < total; ++i) {
+      float acc = part[i];
+      for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, part[(int64_t)s * total + i]);
+      y[i] = Act<DT>::from_f(acc);
+    }
+  }
+}
+}  // namespace
+
+bool dense_ts_ok(int64_t m, int64_t n, int64_t k) { return m >= 1 && n % 128 == 0 && n > 0 && k % kGroup == 0 && k > 0; }
+
+int64_t dense_ts_workspace(int64_t m, int64_t n, int64_t k) {
+  if (!dense_ts_ok(m, n, k)) return 0;
+  const int S = dense_ksplit(m, n, k);
+  return S > 1 ? (int64_t)S * m * n * 4 : 0;
+}
+
+int launch_dense_ts(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n, int64_t k,
+                    int dtype, void* ws, int64_t ws_bytes, int* err, cudaStream_t st) {
+  if (!dense_ts_ok(m, n, k) || (((uintptr_t)x) & 15) || (((uintptr_t)y) & 15) || (n % 8)) return LMOE_ERR_INVALID;
+  int S = dense_ksplit(m, n, k);
+  if (S > 1 && (ws == nullptr || ws_bytes < (int64_t)S * m * n * 4 || (((uintptr_t)ws) & 15))) S = 1;
+  GemmLaunch L = {};
+  L.x = x;
+  L.x_rows = m;
+  L.K = k;
+  L.grid_tiles = (m + kTileRoutes - 1) / kTileRoutes;
+  L.dense_rows = m;
+  L.q_bank = q;
+  L.s_bank = scale;
+  L.experts = 1;
+  L.N = n;
+  L.y = y;
+  L.ldy = n;
+  L.mode = kWeighted;
+  L.dtype = dtype;
+  L.err = err;
+  L.ksplit = S;
+  L.partial = S > 1 ? (float*)ws : nullptr;
+  int rc = launch_ts<true>(L, st);
+  if (rc || S == 1) return rc;
+  const int64_t total = m * n;
+  const unsigned blocks = (unsigned)((total / 4 + 255) / 256 + 1);
+  if (dtype == LMOE_BF16) {
+    LMOE_CUDA_CHECK(launch_pdl(dense_reduce_kernel<LMOE_BF16>, dim3(blocks), dim3(256), 0, st, (const float*)ws,
+                               (__nv_bfloat16*)y, total, S));
+  } else {
+    LMOE_CUDA_CHECK(launch_pdl(dense_reduce_kernel<LMOE_F16>, dim3(blocks), dim3(256), 0, st, (const float*)ws,
+                               (__half*)y, total, S));
+  }
+  return LMOE_OK;
+}
+}  // namespace lmoe

@@ -643,6 +643,11 @@ extern "C" int lmoe_linear_w8a16(const void* x, const int8_t* q, const float* sc
   if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_ERR_INVALID;
   if (m == 0) return LMOE_OK;
   cudaStream_t st = (cudaStream_t)stream;
+  // one row: the HBM-streaming GEMV; more rows: the TMEM-operand tensor-core kernel (weights
+  // on the MMA's M side, the rows on its N side), else (n not a multiple of 128) the GEMV up
+  // to 16 rows and the shared-memory-operand GEMM above
+  if (m >= 2 && dense_ts_ok(m, n, k) && (((uintptr_t)x) & 15) == 0 && (((uintptr_t)y) & 15) == 0)
+    return launch_dense_ts(x, q, scale, y, m, n, k, dtype, nullptr, 0, err, st);
   if (m <= 16) return lmoe_dense_gemv_w8a16(x, q, scale, y, m, n, k, dtype, st);
   GemmLaunch L = {};
   L.x = x;
@@ -660,6 +665,20 @@ extern "C" int lmoe_linear_w8a16(const void* x, const int8_t* q, const float* sc
   L.dtype = dtype;
   L.err = err;
   return launch_grouped_gemm(L, st);
+}
+
+extern "C" int64_t lmoe_linear_w8a16_workspace_size(int64_t m, int64_t n, int64_t k) {
+  if (m < 2 || n <= 0 || k <= 0) return 0;
+  return dense_ts_workspace(m, n, k);
+}
+
+extern "C" int lmoe_linear_w8a16_ws(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n,
+                                    int64_t k, int dtype, void* ws, int64_t ws_bytes, int* err, void* stream) {
+  if (!x || !q || !scale || !y || m < 0 || n <= 0 || k <= 0 || k % kGroup || ws_bytes < 0) return LMOE_ERR_INVALID;
+  if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_ERR_INVALID;
+  if (m >= 2 && dense_ts_ok(m, n, k) && (((uintptr_t)x) & 15) == 0 && (((uintptr_t)y) & 15) == 0)
+    return launch_dense_ts(x, q, scale, y, m, n, k, dtype, ws, ws_bytes, err, (cudaStream_t)stream);
+  return lmoe_linear_w8a16(x, q, scale, y, m, n, k, dtype, err, stream);
 }
 
 extern "C" int64_t lmoe_routed_linear_workspace_size(int64_t tokens, int64_t top, int64_t k) {

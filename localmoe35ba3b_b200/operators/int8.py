@@ -2,7 +2,8 @@
 
 Same call signatures, shapes, dtypes and ``ValueError`` texts as the
 reference; the arithmetic runs in ``liblocalmoe_b200.so``:
-* ``linear``/``Int8Linear`` -- int8.py:26-48 (GEMV for m <= 16 rows, tcgen05 GEMM above);
+* ``linear``/``Int8Linear`` -- int8.py:26-48 (GEMV for one row, tcgen05 GEMM above, K split over a
+  cached workspace when the output alone would not fill the GPU);
 * ``grouped_linear``        -- int8.py:233-237 (table-driven decode GEMV);
 * ``ordered_reduce``        -- the launch of ``_ordered_reduce`` at int8.py:185-186;
 * ``Int8Experts``           -- int8.py:127-210, with the expert bank resident in HBM.
@@ -30,8 +31,10 @@ def linear(x, q, scale, large_tile=False):
     x = x.contiguous()
     m = x.numel() // k
     out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=x.dtype)
-    N.call('lmoe_linear_w8a16', N.ptr(x), N.ptr(q), N.ptr(scale), N.ptr(out), m, n, k, N.dtype_code(x.dtype),
-           N.ptr(N.error_word(x.device)), N.stream(x.device))
+    wsb = N.lib().lmoe_linear_w8a16_workspace_size(m, n, k)
+    ws = N.workspace(x.device, wsb, 'linear') if wsb > 0 else None
+    N.call('lmoe_linear_w8a16_ws', N.ptr(x), N.ptr(q), N.ptr(scale), N.ptr(out), m, n, k, N.dtype_code(x.dtype),
+           N.ptr(ws), wsb, N.ptr(N.error_word(x.device)), N.stream(x.device))
     return out
 
 

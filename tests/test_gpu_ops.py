@@ -228,8 +228,9 @@ def test_routed_reduce_bit_exact(dtype):
 
 # ---------------------------------------------------------------- a1 dense linear
 @pytest.mark.parametrize('dtype', [BF16, F16])
-@pytest.mark.parametrize('M,N,K', [(1, 2048, 2048), (5, 512, 2048), (16, 4096, 512), (17, 512, 2048),
-                                   (256, 2048, 2048), (300, 1000, 384), (2048, 512, 2048)])
+@pytest.mark.parametrize('M,N,K', [(1, 2048, 2048), (2, 8192, 2048), (5, 512, 2048), (16, 4096, 512),
+                                   (17, 512, 2048), (130, 8192, 2048), (256, 2048, 2048), (300, 1000, 384),
+                                   (2048, 512, 2048)])
 def test_linear_w8a16(dtype, M, N, K):
     from localmoe35ba3b_b200.operators import int8
     r = rng(7 + M)
@@ -241,6 +242,31 @@ def test_linear_w8a16(dtype, M, N, K):
     ok, info = ulp_close(to_np(y), ref, dtype)
     assert ok, info
     assert rel_maxabs(to_np(y), O.linear_fp32_reference(x, q, s)) < 1e-2
+
+
+@pytest.mark.parametrize('M,N,K', [(3, 1024, 2048), (64, 512, 1024)])
+def test_linear_w8a16_without_workspace_matches_split_k(M, N, K):
+    """lmoe_linear_w8a16 (no workspace: K not split) and lmoe_linear_w8a16_ws (K split over
+    the workspace) both stay within 1 ulp of the oracle's exact sum."""
+    from localmoe35ba3b_b200 import _native as nat
+    r = rng(70 + M)
+    q, s = rand_q(r, (N, K))
+    x = act(r, (M, K), BF16)
+    xd, qd, sd = to_dev(x, BF16), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    assert nat.lib().lmoe_linear_w8a16_workspace_size(M, N, K) > 0
+    y0 = torch.empty((M, N), dtype=torch.bfloat16, device='cuda')
+    nat.call('lmoe_linear_w8a16', nat.ptr(xd), nat.ptr(qd), nat.ptr(sd), nat.ptr(y0), M, N, K, nat.BF16, None,
+             nat.stream())
+    wsb = nat.lib().lmoe_linear_w8a16_workspace_size(M, N, K)
+    ws = torch.empty(wsb, dtype=torch.uint8, device='cuda')
+    y1 = torch.empty_like(y0)
+    nat.call('lmoe_linear_w8a16_ws', nat.ptr(xd), nat.ptr(qd), nat.ptr(sd), nat.ptr(y1), M, N, K, nat.BF16,
+             nat.ptr(ws), wsb, None, nat.stream())
+    torch.cuda.synchronize()
+    ref = O.linear_w8a16(x, q, s, BF16)
+    for y in (y0, y1):
+        ok, info = ulp_close(to_np(y), ref, BF16)
+        assert ok, info
 
 
 @pytest.mark.parametrize('tile', ['16x32', '32x64'])

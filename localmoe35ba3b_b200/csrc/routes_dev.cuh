@@ -47,18 +47,33 @@ __device__ __forceinline__ void write_tile_list(int E, int tokens, int with_shar
   __shared__ int s_total_tiles;
   __shared__ int s_by_rank[kRouteThreads + 1];
   __shared__ int s_tile_first[kRouteThreads + 1];
+  __shared__ int s_cnt[kRouteThreads + 1];
+  __shared__ int s_rank[kRouteThreads + 1];
   const int Es = E + (with_shared ? 1 : 0);
   const int valid = s_first[E];
   const int e = threadIdx.x;
+  const int lane = lane_id(), warp = warp_id();
   int cnt = 0, ntl = 0, rank = 0;
   if (e < Es) {
     cnt = (e < E) ? (s_first[e + 1] - s_first[e]) : tokens;
     ntl = (cnt + kTileRoutes - 1) / kTileRoutes;
-    for (int o = 0; o < Es; ++o) {
-      const int co = (o < E) ? (s_first[o + 1] - s_first[o]) : tokens;
-      rank += (co > cnt) || (co == cnt && o < e);
-    }
+    s_cnt[e] = cnt;
   }
+  __syncthreads();
+  // rank of expert x among all: the number of experts with more routes, or as many and a
+  // lower id; one warp per expert, its lanes counting over strided subsets of the others
+  for (int x = warp; x < Es; x += kRouteWarps) {
+    const int cx = s_cnt[x];
+    int r = 0;
+    for (int o = lane; o < Es; o += 32) {
+      const int co = s_cnt[o];
+      r += (co > cx) || (co == cx && o < x);
+    }
+    r = __reduce_add_sync(0xffffffffu, r);
+    if (lane == 0) s_rank[x] = r;
+  }
+  __syncthreads();
+  if (e < Es) rank = s_rank[e];
   if (e < Es) s_by_rank[rank] = ntl;
   __syncthreads();
   const int r_ntl = (e < Es) ? s_by_rank[e] : 0;  // thread e now holds rank e's tile count

@@ -57,9 +57,9 @@ LAUNCHES_PER_LAYER = 7
 EP_LAUNCHES_PER_LAYER = 11
 # DRAM bytes (read + write) of the two grouped-GEMM launches of one 2048-token layer, from one
 # `ncu --set full` capture (`python bench.py --layers 2 --steps 1 --warmup 1 --no-cpu-baseline
-# --no-extra`, -k regex:grouped_ts -s 2 -c 2): gate_up 404.2 MB + down 244.1 MB.  Per-layer
+# --no-extra`, -k regex:grouped_ts -s 2 -c 2): gate_up 404.2 MB + down 244.9 MB.  Per-layer
 # work does not depend on the layer count, so no scaling is applied.
-NCU_TRAFFIC_PER_LAYER = 648.3e6
+NCU_TRAFFIC_PER_LAYER = 649.1e6
 NCU_TRAFFIC_SOURCE = ('ncu dram__bytes_read.sum + dram__bytes_write.sum, gate_up + down launches of one '
                       '2048-token layer; bytes per layer like alg_bytes_per_layer')
 

@@ -176,10 +176,11 @@ LMOE_API int lmoe_routed_moe_noalloc(const void* x, const float* weights, const 
  * order is built on the device from ids: no host synchronisation, so the call can be
  * captured in a CUDA graph.  hidden and inter up to 4096 (else LMOE_ERR_UNSUPPORTED);
  * weights, scales, x and ws 16-byte aligned.  ws: lmoe_decode_workspace_size() bytes whose
- * first 8 bytes are zero before the first call (the kernel's grid barrier keeps its two
- * words there, at the same offset for every geometry, and leaves them usable after every
- * call; after a call that set LMOE_DEVERR_TIMEOUT, zero them again).  Calls that share a workspace must not overlap on the GPU.  An id outside
- * [0, experts) sets LMOE_DEVERR_BAD_EXPERT in *err. */
+ * first 8 KiB are zero before the first call (the kernel's grid barrier keeps one counter
+ * per grid size there, at the same offset for every geometry, and leaves them usable after
+ * every call; after a call that set LMOE_DEVERR_TIMEOUT, zero them again).  Calls that
+ * share a workspace must not overlap on the GPU.  An id outside [0, experts) sets
+ * LMOE_DEVERR_BAD_EXPERT in *err. */
 LMOE_API int64_t lmoe_decode_workspace_size(int64_t top, int64_t hidden, int64_t inter);
 LMOE_API int lmoe_decode_moe(const void* x, const float* weights, const int64_t* ids, int64_t top,
                              const int8_t* qg, const float* sg, const int8_t* qd, const float* sd,

@@ -40,6 +40,7 @@ constexpr int kDecThreads = 512;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecRowsMax = 8;  // down rows whose dots are computed together (one chunk per lane)
 constexpr int kDecSmemMax = 220 * 1024;  // both phases' shared-memory regions
+constexpr int kDecMaxS = 64;             // shared-expert columns per gate_up block
 
 // Warp 0: s_eid[r] = the r-th smallest expert id (ties by slot) and s_w[r] the
 // routing weight of its slot.  An id outside [0, E) becomes expert 0 (no read leaves
@@ -74,60 +75,79 @@ __device__ __forceinline__ void row_lds(uint32_t srow, int chunks, int lane, uin
     if (lane + 32 * i < chunks) w[i] = lds128(srow + (uint32_t)(lane + 32 * i) * 16u);
 }
 
+// Shared memory: the phase-1 region (gate_up) and the phase-2 region (down) overlap,
+// both from offset 0 -- the down rows are copied in once every gate_up read is done (their
+// HBM bytes were prefetched into L2 meanwhile) -- and the mbarriers sit after both.
+// Phase 1: a routed block of CB columns (its CB gate and CB up rows) and a slice of S
+// columns of the shared expert (S gate and S up rows), their group scales, and x
+// quantised (W8A8).
 struct GuSmem {
-  int64_t wg, wu, sg, su, xq, xs, bars, bytes;
-  __host__ __device__ GuSmem(int64_t CB, int64_t H) {
+  int64_t wg, wu, sg, su, shg, shu, ssg, ssu, xq, xs, bytes;
+  __host__ __device__ GuSmem(int64_t CB, int64_t S, int64_t H) {
     const int64_t GH = H / kGroup;
     wg = 0;
     wu = CB * H;
     sg = 2 * CB * H;
     su = sg + CB * GH * 4;
-    xq = su + CB * GH * 4;
+    shg = su + CB * GH * 4;
+    shu = shg + S * H;
+    ssg = shu + S * H;
+    ssu = ssg + S * GH * 4;
+    xq = ssu + S * GH * 4;
     xs = xq + H;
-    bars = (xs + GH * 4 + 15) & ~int64_t(15);
-    bytes = bars + (CB / 8) * 8;
+    bytes = (xs + GH * 4 + 127) & ~int64_t(127);
   }
 };
 
+// Phase 2: CBd down rows of every selected expert and of the shared expert, their
+// scales, the hidden rows quantised (W8A8) and in the activation dtype.
 struct DnSmem {
-  int64_t w, sc, hq, hs, bar, bytes;
+  int64_t w, sc, hq, hs, hx, bytes;
   __host__ __device__ DnSmem(int64_t rows, int64_t top, int64_t CBd, int64_t I) {
     const int64_t GI = I / kGroup;
     w = 0;
     sc = rows * CBd * I;
     hq = sc + rows * CBd * GI * 4;
     hs = hq + top * I;
-    bar = (hs + top * GI * 4 + 15) & ~int64_t(15);
-    bytes = bar + 8;
+    hx = (hs + top * GI * 4 + 15) & ~int64_t(15);
+    bytes = (hx + rows * I * 2 + 127) & ~int64_t(127);
   }
 };
 
-// Grid barrier over all CTAs of a launch (every CTA resident), on one 64-bit word:
-// the low half counts arrivals, the high half is the generation.  Each CTA adds 1;
-// the last to arrive adds (1 << 32) - nctas, which restores the count to 0 and
-// advances the generation in the same atomic; the others wait for the generation
-// their own arrival returned to change.  The word's low half must be 0 before the
-// first launch on a workspace, and every completed barrier leaves it 0.  The wait
-// is bounded.
-__device__ __forceinline__ bool grid_barrier(unsigned long long* bar, unsigned nctas, int* err) {
-  __shared__ int s_ok;
+// barriers: one per 8-column piece of the routed block, one for the shared slice, one
+// for the down rows
+__host__ __device__ inline int64_t dec_bars_bytes(int64_t CB) { return (CB / 8 + 2) * 8; }
+
+// Grid barrier over all CTAs of a launch (every CTA resident), on a 64-bit counter that
+// only grows: each CTA adds 1 and waits until the counter reaches the next multiple of
+// the grid size, so the last arrival releases everyone with no second write.  That
+// needs the counter to start every launch at a multiple of the grid size, so each grid
+// size has its own counter (slot gridDim.x of kDecBarSlots); the workspace's counters
+// start at zero.  Arrival and wait are split so that a CTA can issue work that needs no
+// other CTA in between; the wait is bounded.
+constexpr int kDecBarSlots = 1024;
+__device__ __forceinline__ unsigned long long grid_arrive(unsigned long long* ctr, unsigned nctas) {
+  __shared__ unsigned long long s_target;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned long long v = atomicAdd(bar, 1ull);
-    const unsigned gen = (unsigned)(v >> 32);
+    const unsigned long long v = atomicAdd(ctr, 1ull);
+    s_target = (v / nctas + 1) * nctas;
+  }
+  __syncthreads();
+  return s_target;
+}
+__device__ __forceinline__ bool grid_wait(unsigned long long* ctr, unsigned long long target, int* err) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    volatile unsigned long long* c = ctr;
     int ok = 1;
-    if ((unsigned)v == nctas - 1) {
-      atomicAdd(bar, (1ull << 32) - nctas);
-    } else {
-      volatile unsigned* hi = reinterpret_cast<volatile unsigned*>(bar) + 1;
-      const uint64_t t0 = gtime_ns();
-      while (*hi == gen) {
-        if (gtime_ns() - t0 > LMOE_WAIT_NS) {
-          raise_error(err, LMOE_DEVERR_TIMEOUT);
-          ok = 0;
-          break;
-        }
+    const uint64_t t0 = gtime_ns();
+    while (*c < target) {
+      if (gtime_ns() - t0 > LMOE_WAIT_NS) {
+        raise_error(err, LMOE_DEVERR_TIMEOUT);
+        ok = 0;
+        break;
       }
     }
     __threadfence();
@@ -151,8 +171,8 @@ struct LayerArgs {
   void* out;
   unsigned long long* bar;
   int* err;
-  int CB, CBd, n_gu, n_dn;
-  int64_t gu_bytes;  // shared-memory bytes of the phase-1 region (the phase-2 region follows)
+  int CB, CBd, S, n_gu, n_dn;  // S: shared-expert columns per gate_up block (multiple of 4)
+  int64_t bar_off;             // shared-memory offset of the mbarriers (after both regions)
 };
 
 template <int DT, bool W8A8, int MAXG, int MAXD>
@@ -164,6 +184,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   __shared__ float s_w[kDecodeMaxTop];
   __shared__ float red[kDecWarps];
   __shared__ float s_t[kDecWarps][32];  // phase 2: per warp, its lanes' group terms
+  __shared__ float s_sh[2][kDecMaxS];    // phase 1: the shared slice's gate and up dots
   const int lane = lane_id(), warp = warp_id();
   const int top = a.top;
   const int64_t H = a.H, I = a.I;
@@ -173,16 +194,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   const int rows = top + (with_shared ? 1 : 0);
   const T* x = (const T*)a.x;
   T* hid = (T*)a.hid;
-  const GuSmem G(a.CB, H);
+  const GuSmem G(a.CB, a.S, H);
   const DnSmem D(rows, top, a.CBd, I);
   const uint32_t sb = smem_u32(smem);
-  const uint32_t sd0 = sb + (uint32_t)a.gu_bytes;  // phase-2 region
-  uint8_t* dsm = smem + a.gu_bytes;
   const int npieces = a.CB / 8;
+  const uint32_t bars = sb + (uint32_t)a.bar_off;
+  const uint32_t bar_sh = bars + 8u * npieces, bar_dn = bars + 8u * (npieces + 1);
   const int nblk = (int)(I / a.CB);
   if (threadIdx.x == 0) {
-    for (int p = 0; p < npieces; ++p) mbar_init(sb + (uint32_t)G.bars + 8u * p, 1);
-    mbar_init(sd0 + (uint32_t)D.bar, 1);
+    for (int p = 0; p < npieces + 2; ++p) mbar_init(bars + 8u * p, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -192,54 +212,76 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   // arms the barriers, copy_*(blk, k) issues copy k from the calling thread.  A copy
   // that lands before its barrier is armed is fine: the barrier's phase cannot complete
   // before the arming arrival.
-  // gate_up block blk = pieces of 8 columns, each on its own barrier (gate rows, up
-  // rows, their scales: 4 copies per piece), so warps start as their rows land
-  const int n_gu_copies = 4 * npieces, n_dn_copies = 2 * rows;
-  auto expect_gu = [&]() {
+  // gate_up block blk: the routed rows in pieces of 8 columns, each on its own barrier
+  // (gate rows, up rows, their scales: 4 copies per piece), so warps start as their rows
+  // land, and the shared expert's slice of ns(blk) columns on one barrier (4 copies)
+  auto sh_cols = [&](int blk) -> int {
+    const int64_t c0 = (int64_t)blk * a.S;
+    return with_shared && c0 < I ? (int)min((int64_t)a.S, I - c0) : 0;
+  };
+  const int n_gu_copies = 4 * npieces + 4, n_dn_copies = 2 * rows;
+  auto expect_gu = [&](int blk) {
     const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
-    if (lane < npieces) mbar_arrive_expect_tx(sb + (uint32_t)G.bars + 8u * lane, 2 * (wbytes + sbytes));
+    if (lane < npieces) mbar_arrive_expect_tx(bars + 8u * lane, 2 * (wbytes + sbytes));
+    const int ns = sh_cols(blk);
+    if (lane == 0 && ns > 0) mbar_arrive_expect_tx(bar_sh, (uint32_t)(2 * ns * (H + GH * 4)));
   };
   auto copy_gu = [&](int blk, int k) {
     const int r = blk / nblk;
     const int64_t c0 = (int64_t)(blk % nblk) * a.CB;
-    const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
-    const int p = k >> 2, which = k & 3;
-    const uint32_t bar = sb + (uint32_t)G.bars + 8u * p;
-    const int64_t row = c0 + p * 8 + ((which & 1) ? I : 0);  // gate rows, then up rows
-    if (r < top) {
+    if (k < 4 * npieces) {
+      const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
+      const int p = k >> 2, which = k & 3;
+      const uint32_t bar = bars + 8u * p;
+      const int64_t row = c0 + p * 8 + ((which & 1) ? I : 0);  // gate rows, then up rows
       const int64_t e = s_eid[r];
       if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), a.qg + (e * 2 * I + row) * H, wbytes, bar);
       else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), a.sg + (e * 2 * I + row) * GH, sbytes, bar);
     } else {
-      const int64_t srow = c0 + p * 8;
+      const int ns = sh_cols(blk), which = k - 4 * npieces;
+      if (ns == 0) return;
+      const int64_t s0 = (int64_t)blk * a.S;
       const int8_t* q = (which & 1) ? a.sh_qu : a.sh_qg;
       const float* sc = (which & 1) ? a.sh_su : a.sh_sg;
-      if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.wu : G.wg) + p * 8 * H), q + srow * H, wbytes, bar);
-      else bulk_g2s(sb + (uint32_t)((which & 1 ? G.su : G.sg) + p * 8 * GH * 4), sc + srow * GH, sbytes, bar);
+      if (which < 2) bulk_g2s(sb + (uint32_t)((which ? G.shu : G.shg)), q + s0 * H, (uint32_t)(ns * H), bar_sh);
+      else bulk_g2s(sb + (uint32_t)((which & 1 ? G.ssu : G.ssg)), sc + s0 * GH, (uint32_t)(ns * GH * 4), bar_sh);
     }
   };
   // down block blk: per row (routed experts in ascending order, then the shared
-  // expert) its CBd weight rows and their scales, all on one barrier
-  auto expect_dn = [&]() {
-    const uint32_t wb = (uint32_t)(a.CBd * I), sbt = (uint32_t)(a.CBd * GI * 4);
-    if (lane == 0) mbar_arrive_expect_tx(sd0 + (uint32_t)D.bar, (uint32_t)rows * (wb + sbt));
-  };
-  auto copy_dn = [&](int blk, int k) {
+  // expert) its CBd weight rows and their scales, all on one barrier; prefetch_dn pulls
+  // the same bytes into L2 (no shared memory) while phase 1 runs
+  auto dn_src = [&](int blk, int k, const void*& src, uint32_t& bytes, uint32_t& dst) {
     const int64_t n0 = (int64_t)blk * a.CBd;
-    const uint32_t wb = (uint32_t)(a.CBd * I), sbt = (uint32_t)(a.CBd * GI * 4);
-    const uint32_t bar = sd0 + (uint32_t)D.bar;
     const int rr = k >> 1;
     if ((k & 1) == 0) {
-      const int8_t* q = rr < top ? a.qd + (s_eid[rr] * H + n0) * I : a.sh_qd + n0 * I;
-      bulk_g2s(sd0 + (uint32_t)(D.w + (int64_t)rr * a.CBd * I), q, wb, bar);
+      src = rr < top ? a.qd + (s_eid[rr] * H + n0) * I : a.sh_qd + n0 * I;
+      bytes = (uint32_t)(a.CBd * I);
+      dst = sb + (uint32_t)(D.w + (int64_t)rr * a.CBd * I);
     } else {
-      const float* sc = rr < top ? a.sd + (s_eid[rr] * H + n0) * GI : a.sh_sd + n0 * GI;
-      bulk_g2s(sd0 + (uint32_t)(D.sc + (int64_t)rr * a.CBd * GI * 4), sc, sbt, bar);
+      src = rr < top ? a.sd + (s_eid[rr] * H + n0) * GI : a.sh_sd + n0 * GI;
+      bytes = (uint32_t)(a.CBd * GI * 4);
+      dst = sb + (uint32_t)(D.sc + (int64_t)rr * a.CBd * GI * 4);
     }
+  };
+  auto expect_dn = [&]() {
+    const uint32_t wb = (uint32_t)(a.CBd * I), sbt = (uint32_t)(a.CBd * GI * 4);
+    if (lane == 0) mbar_arrive_expect_tx(bar_dn, (uint32_t)rows * (wb + sbt));
+  };
+  auto copy_dn = [&](int blk, int k) {
+    const void* src;
+    uint32_t bytes, dst;
+    dn_src(blk, k, src, bytes, dst);
+    bulk_g2s(dst, src, bytes, bar_dn);
+  };
+  auto prefetch_dn = [&](int blk, int k) {
+    const void* src;
+    uint32_t bytes, dst;
+    dn_src(blk, k, src, bytes, dst);
+    bulk_prefetch_l2(src, bytes);
   };
   // one warp issues all of a block's copies (later blocks, which are rare)
   auto issue_gu = [&](int blk) {
-    expect_gu();
+    expect_gu(blk);
     __syncwarp();
     for (int k = lane; k < n_gu_copies; k += 32) copy_gu(blk, k);
   };
@@ -255,15 +297,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   grid_dep_wait();
   int8_t* xq = reinterpret_cast<int8_t*>(smem + G.xq);
   float* xs = reinterpret_cast<float*>(smem + G.xs);
-  const bool has_gu = (int)blockIdx.x < a.n_gu, first_dn = !has_gu && (int)blockIdx.x < a.n_dn;
+  const bool has_gu = (int)blockIdx.x < a.n_gu, has_dn = (int)blockIdx.x < a.n_dn;
   if (warp == 0) {
     // the experts' order and their routing weights; arm the first block's barriers
     expert_ranks_w(a.ids, a.weights, top, a.E, s_eid, s_w, a.err, blockIdx.x == 0);
     __syncwarp();
-    if (has_gu) expect_gu();
-    // a CTA with no gate_up block streams its down rows at once; the others once their
-    // gate_up rows have landed, so that the two phases do not share the HBM stream
-    else if (first_dn) expect_dn();
+    if (has_gu) expect_gu(blockIdx.x);
   } else {
     // meanwhile the other warps pull x (and the shared gate's weight) towards L1
     for (int64_t c = (int64_t)(threadIdx.x - 32) * 64; c < H; c += (int64_t)(kDecThreads - 32) * 64) {
@@ -273,16 +312,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   }
   __syncthreads();
   // the first block's copies, one warp each
-  if (lane == 0) {
-    if (has_gu)
-      for (int k = warp; k < n_gu_copies; k += kDecWarps) copy_gu(blockIdx.x, k);
-    else if (first_dn)
-      for (int k = warp; k < n_dn_copies; k += kDecWarps) copy_dn(blockIdx.x, k);
-  }
+  if (lane == 0 && has_gu)
+    for (int k = warp; k < n_gu_copies; k += kDecWarps) copy_gu(blockIdx.x, k);
   __syncwarp();
-  // every warp quantises groups of x (W8A8) and forms part of the shared gate's logit
+  // every warp quantises groups of x (W8A8) and forms part of the shared gate's logit;
+  // then the first down block's L2 prefetches (needed only after the grid barrier)
   if (W8A8)
     for (int g = warp; g < GH; g += kDecWarps) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
+  if (lane == 0 && has_dn)
+    for (int k = warp; k < n_dn_copies; k += kDecWarps) prefetch_dn(blockIdx.x, k);
+  __syncwarp();
   if (gated && warp > 0) {
     const T* gw = (const T*)a.gate_w;
     float part = 0.f;
@@ -301,7 +340,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
     const int r = blk / nblk;
     const int64_t c0 = (int64_t)(blk % nblk) * a.CB;
     for (int j = warp; j < a.CB; j += kDecWarps) {
-      if (!mbar_wait_drain(sb + (uint32_t)G.bars + 8u * (j / 8), it & 1, a.err)) {
+      if (!mbar_wait_drain(bars + 8u * (j / 8), it & 1, a.err)) {
         ok = 0;
         break;
       }
@@ -311,47 +350,68 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
       const float* gsr = reinterpret_cast<const float*>(smem + G.sg) + j * GH;
       const float* usr = reinterpret_cast<const float*>(smem + G.su) + j * GH;
       float g, u;
-      if (W8A8 && r < top) {
+      if (W8A8) {
         g = row_dot_w8a8_ilp(wg, gsr, xq, xs, chunks1, lane);
         u = row_dot_w8a8_ilp(wu, usr, xq, xs, chunks1, lane);
-      } else {  // W8A16 routed experts, and the shared expert (Int8Linear arithmetic)
+      } else {
         g = row_dot_w16<DT>(wg, gsr, x, chunks1, lane);
         u = row_dot_w16<DT>(wu, usr, x, chunks1, lane);
       }
       if (lane == 0) hid[(int64_t)r * I + c0 + j] = A::from_f(__fmul_rn(A::round(silu_exact(A::round(g))), A::round(u)));
     }
-    if (it == 0 && (int)blockIdx.x < a.n_dn && warp < n_dn_copies) {
-      // all of this CTA's first gate_up pieces have landed: its down rows go out now,
-      // from each warp that has a down copy to issue once its own columns are done
-      for (int p = 0; p < npieces; ++p)
-        if (!mbar_wait_drain(sb + (uint32_t)G.bars + 8u * p, 0, a.err)) ok = 0;
-      if (warp == 0) expect_dn();
-      if (lane == 0)
-        for (int k = warp; k < n_dn_copies; k += kDecWarps) copy_dn(blockIdx.x, k);
-      __syncwarp();
+    // the shared expert's slice (W8A16, the reference's Int8Linear arithmetic): one row dot
+    // per warp, from the last warp down (the first warps took the extra routed columns)
+    const int ns = sh_cols(blk);
+    if (ns > 0) {
+      for (int rd = kDecWarps - 1 - warp; rd < 2 * ns && ok; rd += kDecWarps) {
+        if (!mbar_wait_drain(bar_sh, it & 1, a.err)) {
+          ok = 0;
+          break;
+        }
+        const int jj = rd % ns, up = rd / ns;
+        uint4 w[MAXG];
+        row_lds(sb + (uint32_t)((up ? G.shu : G.shg) + jj * H), chunks1, lane, w);
+        const float* srow = reinterpret_cast<const float*>(smem + (up ? G.ssu : G.ssg)) + jj * GH;
+        const float v = row_dot_w16<DT>(w, srow, x, chunks1, lane);
+        if (lane == 0) s_sh[up][jj] = v;
+      }
     }
     ok = __syncthreads_and(ok);  // every warp is done with this block's rows
+    if (ns > 0 && ok)
+      for (int jj = threadIdx.x; jj < ns; jj += kDecThreads)
+        hid[(int64_t)top * I + (int64_t)blk * a.S + jj] =
+            A::from_f(__fmul_rn(A::round(silu_exact(A::round(s_sh[0][jj]))), A::round(s_sh[1][jj])));
     if (warp == 0 && ok && blk + (int)gridDim.x < a.n_gu) issue_gu(blk + gridDim.x);
+    __syncthreads();  // s_sh is read before the next block's dots write it
   }
-  const bool passed = grid_barrier(a.bar, gridDim.x, a.err);
+  // arrive at the grid barrier, then (needing no other CTA) bring this CTA's first down
+  // block from L2 into the now free shared memory, then wait for every CTA's hidden rows
+  unsigned long long* const ctr = a.bar + gridDim.x;  // this grid size's counter
+  const unsigned long long target = grid_arrive(ctr, gridDim.x);
   grid_dep_launch();  // every CTA of this launch is resident: a dependent may take SMs as they leave
+  if (has_dn && ok) {
+    if (warp == 0) expect_dn();
+    __syncwarp();
+    if (lane == 0)
+      for (int k = warp; k < n_dn_copies; k += kDecWarps) copy_dn(blockIdx.x, k);
+    __syncwarp();
+  }
+  const bool passed = grid_wait(ctr, target, a.err);
   if (!passed || !ok) {
     // never leave this CTA with its phase-2 copies still in flight
-    if ((int)blockIdx.x < a.n_dn) mbar_wait_drain(sd0 + (uint32_t)D.bar, 0, a.err);
+    if (has_dn && ok) mbar_wait_drain(bar_dn, 0, a.err);
     return;
   }
 
   // ---- phase 2: down + ordered combine + gated shared expert + residual
-  int8_t* hq = reinterpret_cast<int8_t*>(dsm + D.hq);
-  float* hs = reinterpret_cast<float*>(dsm + D.hs);
-  // the hidden rows (routed and shared, activation dtype) in the phase-1 region, whose
-  // reads and copies are all complete
-  const T* hx = reinterpret_cast<const T*>(smem + G.wg);
-  if ((int)blockIdx.x < a.n_dn) {
+  int8_t* hq = reinterpret_cast<int8_t*>(smem + D.hq);
+  float* hs = reinterpret_cast<float*>(smem + D.hs);
+  const T* hx = reinterpret_cast<const T*>(smem + D.hx);
+  if (has_dn) {
     // every hidden row into shared memory in one L2 round trip (the rows come from
     // other CTAs: read through L2), then the W8A8 quantisation from there
     const int n16 = (int)(rows * I * 2 / 16);
-    const uint32_t hx0 = sb + (uint32_t)G.wg;
+    const uint32_t hx0 = sb + (uint32_t)D.hx;
     for (int b0 = 0; b0 < n16; b0 += 2 * kDecThreads) {
       uint4 v[2];
 #pragma unroll
@@ -400,7 +460,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
     sig = A::round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-A::round(tot)))));
   }
   const int chunks2 = (int)(I / 16);
-  const float* scs = reinterpret_cast<const float*>(dsm + D.sc);
+  const float* scs = reinterpret_cast<const float*>(smem + D.sc);
   const T* res = (const T*)a.residual;
   T* out = (T*)a.out;
   int it2 = 0;
@@ -412,10 +472,19 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
     const bool have_col = j0 < a.CBd;
     float resv = 0.f;
     if (have_col && res != nullptr) resv = A::to_f(res[n0 + j0]);
-    if (!__syncthreads_and(mbar_wait_drain(sd0 + (uint32_t)D.bar, it2 & 1, a.err) ? 1 : 0)) return;
+    if (!__syncthreads_and(mbar_wait_drain(bar_dn, it2 & 1, a.err) ? 1 : 0)) return;
     for (int j = warp; j < a.CBd; j += kDecWarps) {
       const int64_t n = n0 + j;
       if (j != j0 && res != nullptr) resv = A::to_f(res[n]);
+      // the shared expert's down row first (it needs nothing from the routed rows, and its
+      // latency then overlaps theirs)
+      float sv = 0.f;
+      if (with_shared) {
+        uint4 w[MAXD];
+        row_lds(sb + (uint32_t)(D.w + ((int64_t)top * a.CBd + j) * I), chunks2, lane, w);
+        sv = A::round(
+            row_dot_w16<DT, MAXD>(w, scs + ((int64_t)top * a.CBd + j) * GI, hx + (int64_t)top * I, chunks2, lane));
+      }
       float acc = 0.f;
       if (W8A8 && top * GI <= 32) {
         // one lane per (routed row rr = lane / GI, 128-group g = lane % GI): the group's
@@ -426,7 +495,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
         const int rr = lane / GI, g = lane - rr * GI;
         float t = 0.f;
         if (rr < top) {
-          const uint32_t wrow = sd0 + (uint32_t)(D.w + ((int64_t)rr * a.CBd + j) * I + g * kGroup);
+          const uint32_t wrow = sb + (uint32_t)(D.w + ((int64_t)rr * a.CBd + j) * I + g * kGroup);
           const uint32_t xrow = smem_u32(hq + (int64_t)rr * I + g * kGroup);
           int dsum = 0;
 #pragma unroll
@@ -462,7 +531,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
 #pragma unroll
         for (int k = 0; k < kDecRows; ++k) {
           const int rr = min(r0 + k, top - 1);  // rows past top repeat the last one (unused)
-          row_lds(sd0 + (uint32_t)(D.w + ((int64_t)rr * a.CBd + j) * I), chunks2, lane, w[k]);
+          row_lds(sb + (uint32_t)(D.w + ((int64_t)rr * a.CBd + j) * I), chunks2, lane, w[k]);
           srow[k] = scs + ((int64_t)rr * a.CBd + j) * GI;
           xr[k] = hq + (int64_t)rr * I;
           xsr[k] = hs + rr * GI;
@@ -479,13 +548,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
           if (r0 + k < top) acc = A::round(__fadd_rn(acc, A::round(__fmul_rn(A::round(v[k]), s_w[r0 + k]))));
       }
       }
-      if (with_shared) {
-        uint4 w[MAXD];
-        row_lds(sd0 + (uint32_t)(D.w + ((int64_t)top * a.CBd + j) * I), chunks2, lane, w);
-        const float sv = A::round(
-            row_dot_w16<DT, MAXD>(w, scs + ((int64_t)top * a.CBd + j) * GI, hx + (int64_t)top * I, chunks2, lane));
-        acc = A::round(__fadd_rn(acc, gated ? A::round(__fmul_rn(sig, sv)) : sv));
-      }
+      if (with_shared) acc = A::round(__fadd_rn(acc, gated ? A::round(__fmul_rn(sig, sv)) : sv));
       if (res != nullptr) acc = A::round(__fadd_rn(resv, acc));
       if (lane == 0) out[n] = A::from_f(acc);
     }
@@ -495,29 +558,37 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
 
 }
 
-// The grid barrier's two words come first, at a fixed offset, so that a workspace
-// reused for another geometry keeps them where the previous calls left them (zero).
+// The grid barrier's counters come first, at a fixed offset, so that a workspace reused
+// for another geometry keeps them where the previous calls left them (each a multiple of
+// its grid size; zero in a new workspace).
 struct DecodeWs {
   int64_t off_bar, off_h, bytes;
   static int64_t align(int64_t v) { return (v + 255) & ~int64_t(255); }
   DecodeWs(int64_t top, int64_t H, int64_t I) {
     (void)H;
     off_bar = 0;
-    off_h = 256;                                  // hidden rows: routed + shared
+    off_h = kDecBarSlots * 8;                     // hidden rows: routed + shared
     bytes = off_h + align((top + 1) * I * 2);
   }
 };
 
-static int64_t a128(int64_t v) { return (v + 127) & ~int64_t(127); }
-
-// columns per CTA: the largest blocks whose rows fit both phases' shared memory
-static bool pick_blocks(int64_t rows, int64_t top, int64_t H, int64_t I, int& cb, int& cbd) {
+// gate_up blocks of cb routed columns (top * I / cb of them), each with a slice of s
+// shared-expert columns (s a multiple of 4, so that a slice's scale rows copy in 16-byte
+// units), and down blocks of cbd columns: the largest blocks whose phases fit in shared
+// memory (both regions overlap)
+static int64_t dec_smem(int64_t rows, int64_t top, int64_t H, int64_t I, int cb, int s, int cbd) {
+  const int64_t p1 = GuSmem(cb, s, H).bytes, p2 = DnSmem(rows, top, cbd, I).bytes;
+  return (p1 > p2 ? p1 : p2) + dec_bars_bytes(cb);
+}
+static bool pick_blocks(int64_t rows, int64_t top, int64_t H, int64_t I, bool with_shared, int& cb, int& s,
+                        int& cbd) {
   for (cb = 32; cb >= 8; cb >>= 1) {
     if (I % cb) continue;
+    const int64_t n_gu = top * (I / cb);
+    s = with_shared ? (int)((((I + n_gu - 1) / n_gu) + 3) & ~int64_t(3)) : 0;
+    if (s > kDecMaxS) continue;
     for (cbd = 16; cbd >= 4; cbd >>= 1)
-      if (H % cbd == 0 && a128(GuSmem(cb, H).bytes) + DnSmem(rows, top, cbd, I).bytes <= kDecSmemMax &&
-          rows * I * 2 <= GuSmem(cb, H).bytes)  // phase 2 stages the hidden rows in the phase-1 region
-        return true;
+      if (H % cbd == 0 && dec_smem(rows, top, H, I, cb, s, cbd) <= kDecSmemMax) return true;
   }
   return false;
 }
@@ -525,8 +596,9 @@ static bool pick_blocks(int64_t rows, int64_t top, int64_t H, int64_t I, int& cb
 template <int DT, bool W8A8, int MAXG, int MAXD>
 static int launch_layer(LayerArgs& a, int rows, cudaStream_t st) {
   auto k = decode_layer_kernel<DT, W8A8, MAXG, MAXD>;
-  a.gu_bytes = a128(GuSmem(a.CB, a.H).bytes);
-  const int64_t smem = a.gu_bytes + DnSmem(rows, a.top, a.CBd, a.I).bytes;
+  const int64_t p1 = GuSmem(a.CB, a.S, a.H).bytes, p2 = DnSmem(rows, a.top, a.CBd, a.I).bytes;
+  a.bar_off = p1 > p2 ? p1 : p2;
+  const int64_t smem = dec_smem(rows, a.top, a.H, a.I, a.CB, a.S, a.CBd);
   LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   LMOE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
                                        (int)cudaSharedmemCarveoutMaxShared));
@@ -537,14 +609,15 @@ static int launch_layer(LayerArgs& a, int rows, cudaStream_t st) {
   if (resident <= 0) return LMOE_ERR_UNSUPPORTED;
   const int64_t want = a.n_gu > a.n_dn ? a.n_gu : a.n_dn;
   const unsigned grid = (unsigned)(want < resident ? want : resident);
+  if (grid >= (unsigned)kDecBarSlots) return LMOE_ERR_UNSUPPORTED;
   LMOE_CUDA_CHECK(launch_pdl(k, dim3(grid), dim3(kDecThreads), (size_t)smem, st, a));
   return LMOE_OK;
 }
 
 template <int DT, bool W8A8>
 static int launch_decode(LayerArgs& a, int rows, cudaStream_t st) {
-  if (!pick_blocks(rows, a.top, a.H, a.I, a.CB, a.CBd)) return LMOE_ERR_UNSUPPORTED;
-  a.n_gu = (int)(rows * (a.I / a.CB));
+  if (!pick_blocks(rows, a.top, a.H, a.I, a.sh_qg != nullptr, a.CB, a.S, a.CBd)) return LMOE_ERR_UNSUPPORTED;
+  a.n_gu = (int)(a.top * (a.I / a.CB));
   a.n_dn = (int)(a.H / a.CBd);
   // MAXI = 16-byte chunks per lane of one row: H / 512 (gate_up), I / 512 (down)
   if (a.H <= 2048) {

@@ -209,6 +209,34 @@ LMOE_API int lmoe_router_topk(const void* logits, int64_t tokens, int64_t expert
  * 0 after the stream means every input agrees bit for bit. */
 LMOE_API int lmoe_selftest_silu(int dtype, int* mismatches, void* stream);
 
+/* The router on tensor cores (replaces the HF Qwen3_5MoeTopKRouter.forward,
+ * transformers qwen3_5_moe/modeling_qwen3_5_moe.py:762-770, that the reference keeps,
+ * qwen35_deploy/model.py:57-68): logits = x [tokens, hidden] . router_w [experts, hidden]^T
+ * with fp32 accumulation rounded to the activation dtype, then lmoe_router_topk's tail on
+ * them in the same kernel.  logits (nullable) receives them [tokens, experts], probs
+ * (nullable) the fp32 softmax.  experts 64, 128 or 256, hidden % 64 == 0, 1 <= top <=
+ * min(32, experts) (else LMOE_ERR_INVALID); x, router_w, logits, ws 16-byte aligned; ws:
+ * lmoe_router_gemm_workspace_size(tokens, experts) bytes (fp32 partial sums of K). */
+LMOE_API int64_t lmoe_router_gemm_workspace_size(int64_t tokens, int64_t experts);
+LMOE_API int lmoe_router_gemm_topk(const void* x, const void* router_w, int64_t tokens, int64_t hidden,
+                                   int64_t experts, int64_t top, float* weights, int64_t* ids, float* probs,
+                                   void* logits, void* ws, int dtype, int* err, void* stream);
+
+/* The whole sparse-MoE block from the hidden states: lmoe_router_gemm_topk (which also
+ * counts each 128-token tile's routes per expert when top == 8, the first step of the
+ * routing metadata) and then lmoe_routed_moe's launches on the routing it produced; the
+ * routing is returned in weights [tokens, top] fp32 and ids [tokens, top] int64.  HF
+ * Qwen3_5MoeSparseMoeBlock.forward (modeling_qwen3_5_moe.py:781-792) with the experts the
+ * reference installs.  ws: lmoe_moe_workspace_size(tokens, top, experts, hidden, inter)
+ * bytes.  Geometry outside lmoe_router_gemm_topk's: LMOE_ERR_UNSUPPORTED. */
+LMOE_API int lmoe_moe_block_router(const void* x, const void* router_w, int64_t tokens, int64_t top,
+                                   const int8_t* qg, const float* sg, const int8_t* qd, const float* sd,
+                                   int64_t experts, int64_t hidden, int64_t inter, const int8_t* sh_qg,
+                                   const float* sh_sg, const int8_t* sh_qu, const float* sh_su,
+                                   const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w,
+                                   const void* residual, void* out, float* weights, int64_t* ids, int dtype,
+                                   void* ws, int* err, void* stream);
+
 #define LMOE_WIRE_DTYPE 0 /* expert-parallel dispatch payload: the hidden row in the activation dtype */
 #define LMOE_WIRE_INT8 1  /* ... or its W8A8 activation quantisation (w8a8.quantize, operators/w8a8.py:8-22) */
 

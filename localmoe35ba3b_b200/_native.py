@@ -49,6 +49,10 @@ SIGNATURES = {
                              _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
     'lmoe_router_topk': (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _I, _P]),
     'lmoe_selftest_silu': (_I, [_I, _P, _P]),
+    'lmoe_router_gemm_workspace_size': (_I64, [_I64, _I64]),
+    'lmoe_router_gemm_topk': (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I, _P, _P]),
+    'lmoe_moe_block_router': (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P,
+                                   _P, _P, _P, _P, _I, _P, _P, _P]),
     'lmoe_ep_layer_row_bytes': (_I64, [_I64, _I64, _I]),
     'lmoe_ep_plan_workspace_size': (_I64, [_I64, _I64, _I64, _I64]),
     'lmoe_ep_owner_workspace_size': (_I64, [_I64, _I64, _I64, _I64, _I64, _I64, _I64]),

@@ -126,12 +126,67 @@ extern "C" int64_t lmoe_moe_workspace_size(int64_t tokens, int64_t top, int64_t 
   return MoeWs(tokens, top, experts, hidden, inter).bytes;
 }
 
+int lmoe_route_meta_after_counts(const int64_t* ids, const float* weights, int64_t tokens, int64_t top,
+                                 int64_t experts, int with_shared, void* meta, int* err, cudaStream_t st);
+namespace lmoe {
+bool router_gemm_ok(int64_t tokens, int64_t hidden, int64_t experts, int64_t top);
+int launch_router_gemm_topk(const void* x, const void* w, int64_t tokens, int64_t hidden, int64_t experts,
+                            int64_t top, float* weights, int64_t* ids, float* probs, void* logits, int32_t* counts,
+                            void* ws, int dtype, int* err, cudaStream_t st);
+int64_t router_gemm_workspace(int64_t tokens, int64_t experts);
+}  // namespace lmoe
+
+// The block after the routing: metadata (router_counts: the per-chunk expert counts are
+// already in the metadata's scratch), permute, gate_up, down, combine.
+static int moe_block_body(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
+                          const int8_t* qg, const float* sg, const int8_t* qd, const float* sd, int64_t experts,
+                          int64_t hidden, int64_t inter, const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu,
+                          const float* sh_su, const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w,
+                          const void* residual, void* out, int dtype, void* ws, int* err, void** stage_events,
+                          cudaStream_t st, bool router_counts);
+
 extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
                                const int8_t* qg, const float* sg, const int8_t* qd, const float* sd, int64_t experts,
                                int64_t hidden, int64_t inter, const int8_t* sh_qg, const float* sh_sg,
                                const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd, const float* sh_sd,
                                const void* sh_gate_w, const void* residual, void* out, int dtype, void* ws, int* err,
                                void** stage_events, void* stream) {
+  return moe_block_body(x, weights, ids, tokens, top, qg, sg, qd, sd, experts, hidden, inter, sh_qg, sh_sg, sh_qu,
+                        sh_su, sh_qd, sh_sd, sh_gate_w, residual, out, dtype, ws, err, stage_events,
+                        (cudaStream_t)stream, false);
+}
+
+extern "C" int lmoe_moe_block_router(const void* x, const void* router_w, int64_t tokens, int64_t top,
+                                     const int8_t* qg, const float* sg, const int8_t* qd, const float* sd,
+                                     int64_t experts, int64_t hidden, int64_t inter, const int8_t* sh_qg,
+                                     const float* sh_sg, const int8_t* sh_qu, const float* sh_su, const int8_t* sh_qd,
+                                     const float* sh_sd, const void* sh_gate_w, const void* residual, void* out,
+                                     float* weights, int64_t* ids, int dtype, void* ws, int* err, void* stream) {
+  if (!x || !router_w || !weights || !ids || !ws || top <= 0) return LMOE_ERR_INVALID;
+  if (!router_gemm_ok(tokens, hidden, experts, top)) return LMOE_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  const MoeWs W(tokens, top, experts, hidden, inter);
+  const MetaLayout ML(tokens, top, experts);
+  // a 128-token tile is one metadata chunk when top * 128 == kMetaChunk: the router kernel
+  // then writes the chunk's expert counts itself
+  const bool fused_counts = top * 128 == kMetaChunk;
+  int32_t* cc = fused_counts ? (int32_t*)((char*)ws + W.off_meta + ML.off_scratch) : nullptr;
+  // the router's fp32 partial sums go to the down rows' region, which the down GEMM only
+  // writes later in the call
+  if (router_gemm_workspace(tokens, experts) > W.bytes - W.off_down) return LMOE_ERR_UNSUPPORTED;
+  int rc = launch_router_gemm_topk(x, router_w, tokens, hidden, experts, top, weights, ids, nullptr, nullptr, cc,
+                                   (char*)ws + W.off_down, dtype, err, st);
+  if (rc) return rc;
+  return moe_block_body(x, weights, ids, tokens, top, qg, sg, qd, sd, experts, hidden, inter, sh_qg, sh_sg, sh_qu,
+                        sh_su, sh_qd, sh_sd, sh_gate_w, residual, out, dtype, ws, err, nullptr, st, fused_counts);
+}
+
+static int moe_block_body(const void* x, const float* weights, const int64_t* ids, int64_t tokens, int64_t top,
+                          const int8_t* qg, const float* sg, const int8_t* qd, const float* sd, int64_t experts,
+                          int64_t hidden, int64_t inter, const int8_t* sh_qg, const float* sh_sg, const int8_t* sh_qu,
+                          const float* sh_su, const int8_t* sh_qd, const float* sh_sd, const void* sh_gate_w,
+                          const void* residual, void* out, int dtype, void* ws, int* err, void** stage_events,
+                          cudaStream_t st, bool router_counts) {
   // top == 0 (no routed experts, the gated shared expert alone) is accepted when a shared
   // expert is given: expert-parallel callers compute their own tokens' shared expert this way
   const bool shared_only = top == 0 && sh_qg != nullptr;
@@ -142,7 +197,6 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_ERR_INVALID;
   const bool with_shared = sh_qg != nullptr;
   if (with_shared && (!sh_sg || !sh_qu || !sh_su || !sh_qd || !sh_sd)) return LMOE_ERR_INVALID;
-  cudaStream_t st = (cudaStream_t)stream;
   const MoeWs W(tokens, top, experts, hidden, inter);
   const MetaLayout ML(tokens, top, experts);
   char* w = (char*)ws;
@@ -159,7 +213,11 @@ extern "C" int lmoe_routed_moe(const void* x, const float* weights, const int64_
   };
   int rc = mark(0);
   if (rc) return rc;
-  if ((rc = lmoe_route_meta_impl(ids, weights, tokens, top, experts, with_shared ? 1 : 0, meta, err, st))) return rc;
+  if ((rc = router_counts ? lmoe_route_meta_after_counts(ids, weights, tokens, top, experts, with_shared ? 1 : 0, meta,
+                                                         err, st)
+                          : lmoe_route_meta_impl(ids, weights, tokens, top, experts, with_shared ? 1 : 0, meta, err,
+                                                 st)))
+    return rc;
   if ((rc = mark(1))) return rc;
 
   const int64_t rows = R + (with_shared ? tokens : 0);

@@ -369,8 +369,10 @@ extern "C" int64_t lmoe_route_meta_size(int64_t tokens, int64_t top, int64_t exp
   return MetaLayout(tokens, top, experts).bytes;
 }
 
-int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
-                         int with_shared, void* meta, int* err, cudaStream_t st) {
+// counts_ready: the per-chunk expert counts are already in the metadata's scratch (the
+// fused router kernel wrote them), so the count kernel is skipped
+static int route_meta_launch(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
+                             int with_shared, void* meta, int* err, cudaStream_t st, bool counts_ready) {
   // top == 0 with the shared expert: no routes, only the shared expert's tiles
   const bool shared_only = top == 0 && with_shared;
   if ((!ids && !shared_only) || !meta) return LMOE_ERR_INVALID;
@@ -397,7 +399,7 @@ int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t token
   const int nchunks = (R + kMetaChunk - 1) / kMetaChunk;
   const size_t hsm = (size_t)(experts + 1) * sizeof(int);
   const size_t wsm = (size_t)(kMetaChunk / 32) * (experts + 1) * sizeof(int);
-  if (nchunks > 0) {
+  if (nchunks > 0 && !counts_ready) {
     LMOE_CUDA_CHECK(launch_pdl(meta_count_kernel, dim3(nchunks), dim3(kMetaChunk), hsm, st, ids, R, (int)experts, cc,
                                err));
   }
@@ -408,6 +410,16 @@ int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t token
     LMOE_CUDA_CHECK(launch_pdl(meta_place_kernel, dim3(nchunks), dim3(kMetaChunk), wsm, st, a, cc));
   }
   return LMOE_OK;
+}
+
+int lmoe_route_meta_impl(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,
+                         int with_shared, void* meta, int* err, cudaStream_t st) {
+  return route_meta_launch(ids, weights, tokens, top, experts, with_shared, meta, err, st, false);
+}
+
+int lmoe_route_meta_after_counts(const int64_t* ids, const float* weights, int64_t tokens, int64_t top,
+                                 int64_t experts, int with_shared, void* meta, int* err, cudaStream_t st) {
+  return route_meta_launch(ids, weights, tokens, top, experts, with_shared, meta, err, st, true);
 }
 
 extern "C" int lmoe_route_meta(const int64_t* ids, const float* weights, int64_t tokens, int64_t top, int64_t experts,

@@ -12,15 +12,18 @@ host synchronisation per layer in ``Int8Experts.forward`` (int8.py:160).
 ``F.linear`` (a plain library GEMM), the fp32 softmax / top-k / renormalise tail
 is one library kernel (``lmoe_router_topk``).  ``SparseMoeBlock`` mirrors the HF
 block's ``forward(hidden_states) -> hidden_states``: one token goes through the
-graph-capturable decode chain, more tokens through the fused prefill block; the
-shared expert is folded into the same library call as the routed experts.
+graph-capturable decode chain, more tokens through the fused prefill block --
+with 64, 128 or 256 experts its router too (``lmoe_moe_block_router``: the
+logits on tensor cores, the tail and the metadata's route counts in the same
+kernel); the shared expert is folded into the same library call as the routed
+experts.
 """
 import torch
 import torch.nn.functional as F
 
 from .. import _native as N
 from .decode import decode_block
-from .gpu_routes import moe_block
+from .gpu_routes import moe_block, moe_block_router, router_gemm_ok
 
 
 def topk_from_logits(logits, top_k, return_probs=False):
@@ -101,8 +104,13 @@ class SparseMoeBlock(torch.nn.Module):
         x = hidden_states.reshape(-1, shape[-1])
         if x.shape[0] == 0:
             return hidden_states.clone()
-        w, ids = route(x, self.gate.weight, self.gate.top_k)
         res = residual.reshape(-1, shape[-1]) if residual is not None else None
+        if x.shape[0] > 1 and router_gemm_ok(x, self.gate.weight, self.gate.top_k):
+            # prefill: router (tensor-core logits + tail + route counts) and experts in one call
+            y, _, _ = moe_block_router(x, self.gate.weight, self.gate.top_k, self.banks, shared=self.shared,
+                                       shared_gate_weight=self.shared_gate_weight, residual=res)
+            return y.reshape(shape)
+        w, ids = route(x, self.gate.weight, self.gate.top_k)
         if x.shape[0] == 1:
             y = decode_block(x, w, ids, self.banks, shared=self.shared, shared_gate_weight=self.shared_gate_weight,
                              residual=res, activation=self.activation)

@@ -8,7 +8,10 @@ qwen35_deploy/runtime/gpu_routes.py).
   routing weight fused, ordered combine), no host synchronisation;
 * ``moe_block(...)`` -- the same launches with the shared expert folded in as
   one more expert segment and the HF gate/add fused into the combine
-  (transformers qwen3_5_moe/modeling_qwen3_5_moe.py:781-792).
+  (transformers qwen3_5_moe/modeling_qwen3_5_moe.py:781-792);
+* ``moe_block_router(...)`` -- the same block from the hidden states, its router
+  (logits GEMM + softmax/top-k + the metadata's route counts) one more kernel
+  (modeling_qwen3_5_moe.py:762-770).
 """
 import ctypes
 
@@ -90,6 +93,70 @@ def moe_block(x, weights, ids, banks, shared=None, shared_gate_weight=None, resi
            e, h, inter, *[N.ptr(v) for v in sh], N.ptr(gate), N.ptr(residual), N.ptr(out), N.dtype_code(x.dtype),
            N.ptr(ws), N.ptr(N.error_word(dev)), evs, N.stream(dev))
     return out
+
+
+ROUTER_EXPERTS = (64, 128, 256)  # expert counts the fused router kernel takes
+
+
+def router_gemm_ok(x, router_weight, top_k):
+    """Whether ``moe_block_router`` / ``router_topk_fused`` take this geometry."""
+    t, h = x.shape
+    return (router_weight.shape[0] in ROUTER_EXPERTS and router_weight.shape[1] == h and h % 64 == 0 and
+            1 <= top_k <= min(32, router_weight.shape[0]) and t > 0)
+
+
+def router_topk_fused(x, router_weight, top_k, return_probs=False, return_logits=False):
+    """The router on tensor cores (``lmoe_router_gemm_topk``): the logits
+    ``x . router_weight^T`` (K split over 4 CTAs per 128-token tile, the splits added in
+    order), rounded to ``x.dtype``, and the fp32 softmax / top-k / renormalise tail.  Returns ``(weights, ids)`` and, as asked,
+    the fp32 softmax and the logits."""
+    x = x.contiguous()
+    w_r = router_weight.to(x.dtype).contiguous()
+    t, e = x.shape[0], w_r.shape[0]
+    dev = x.device
+    w = torch.empty((t, top_k), dtype=torch.float32, device=dev)
+    ids = torch.empty((t, top_k), dtype=torch.int64, device=dev)
+    probs = torch.empty((t, e), dtype=torch.float32, device=dev) if return_probs else None
+    logits = torch.empty((t, e), dtype=x.dtype, device=dev) if return_logits else None
+    ws = N.workspace(dev, N.lib().lmoe_router_gemm_workspace_size(t, e), 'router')
+    N.call('lmoe_router_gemm_topk', N.ptr(x), N.ptr(w_r), t, x.shape[1], e, top_k, N.ptr(w), N.ptr(ids), N.ptr(probs),
+           N.ptr(logits), N.ptr(ws), N.dtype_code(x.dtype), N.ptr(N.error_word(dev)), N.stream(dev))
+    out = (w, ids)
+    if return_probs:
+        out = out + (probs,)
+    if return_logits:
+        out = out + (logits,)
+    return out
+
+
+def moe_block_router(x, router_weight, top_k, banks, shared=None, shared_gate_weight=None, residual=None):
+    """The whole sparse-MoE block from the hidden states (``lmoe_moe_block_router``):
+    the fused router kernel (which also counts the routes per expert of each 128-token
+    tile for the metadata when ``top_k == 8``) and then ``moe_block``'s launches on the
+    routing it produced.  Returns ``(out, weights, ids)``."""
+    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16) or x.ndim != 2:
+        raise ValueError('Expected CUDA FP16/BF16 activations')
+    x = x.contiguous()
+    e, h, inter = _check_banks(x, banks)
+    w_r = router_weight.to(x.dtype).contiguous()
+    if w_r.shape[0] != e:
+        raise ValueError('Router weight must be [experts, hidden]')
+    t = x.shape[0]
+    dev = x.device
+    out = torch.empty_like(x)
+    w = torch.empty((t, top_k), dtype=torch.float32, device=dev)
+    ids = torch.empty((t, top_k), dtype=torch.int64, device=dev)
+    ws = N.workspace(dev, N.lib().lmoe_moe_workspace_size(t, top_k, e, h, inter), 'moe')
+    sh = [None] * 6
+    if shared is not None:
+        (qsg, ssg), (qsu, ssu), (qsd, ssd) = shared
+        sh = [qsg, ssg, qsu, ssu, qsd, ssd]
+    gate = shared_gate_weight.to(x.dtype).contiguous() if shared_gate_weight is not None else None
+    qg, sg, qd, sd = banks
+    N.call('lmoe_moe_block_router', N.ptr(x), N.ptr(w_r), t, top_k, N.ptr(qg), N.ptr(sg), N.ptr(qd), N.ptr(sd), e, h,
+           inter, *[N.ptr(v) for v in sh], N.ptr(gate), N.ptr(residual), N.ptr(out), N.ptr(w), N.ptr(ids),
+           N.dtype_code(x.dtype), N.ptr(ws), N.ptr(N.error_word(dev)), N.stream(dev))
+    return out, w, ids
 
 
 def routed_moe(x, weights, ids, banks, large_tile=False, ready_event=None):

@@ -88,6 +88,35 @@ def test_router_many_ties():
     _check_against_torch(torch.from_numpy(lg).to(torch.bfloat16).cuda(), top)
 
 
+@pytest.mark.parametrize('dtype', [BF16, F16])
+@pytest.mark.parametrize('T,E,top', [(2048, 256, 8), (300, 128, 4), (1000, 64, 8), (5, 256, 8)])
+def test_router_gemm_topk_matches_linear_and_tail(dtype, T, E, top):
+    """The fused router kernel (tensor-core logits + the tail on chip): its logits are
+    F.linear's within one unit in the last place of the activation dtype (only the fp32
+    summation order differs), its routing is lmoe_router_topk's on those logits bit for
+    bit, and the expert sets are torch.topk's on them."""
+    from localmoe35ba3b_b200.runtime import gpu_routes
+    from localmoe35ba3b_b200.runtime.block import topk_from_logits
+    r = rng(T + E + top)
+    H = 2048
+    x = to_dev(act(r, (T, H), dtype), dtype)
+    wgt = to_dev(act(r, (E, H), dtype, 0.05), dtype)
+    w, ids, probs, logits = gpu_routes.router_topk_fused(x, wgt, top, return_probs=True, return_logits=True)
+    ref = F.linear(x, wgt)
+    torch.cuda.synchronize()
+    # one unit in the last place of the value, or of the fp32 sums' rounding noise for
+    # logits that cancel to near zero (2^-13 of the row's largest logit)
+    ulp = 2.0 ** (-7 if dtype == BF16 else -10)
+    lf, rf = logits.float(), ref.float()
+    noise = rf.abs().amax(-1, keepdim=True) * 2.0 ** -13
+    assert bool(((lf - rf).abs() <= rf.abs() * ulp + noise).all()), 'logits beyond one ulp of F.linear'
+    assert (lf == rf).float().mean().item() > 0.9
+    probs2, w2, ids2 = topk_from_logits(logits, top, return_probs=True)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, ids2) and torch.equal(w, w2) and torch.equal(probs, probs2)
+    _check_against_torch(logits, top)
+
+
 def _block_case(seed, T, E, H, I, top, dtype):
     r = rng(seed)
     qg, sg = rand_q(r, (E, 2 * I, H))
@@ -112,7 +141,12 @@ def test_sparse_moe_block_vs_oracle(T, activation):
     out = blk(xd)
     torch.cuda.synchronize()
     assert out.shape == (1, T, H)
-    logits = to_np(F.linear(xd.reshape(T, H), blk.gate.weight))
+    if T > 1:
+        # prefill routes with the fused router kernel: the oracle takes its logits
+        from localmoe35ba3b_b200.runtime import gpu_routes
+        logits = to_np(gpu_routes.router_topk_fused(xd.reshape(T, H), blk.gate.weight, top, return_logits=True)[2])
+    else:
+        logits = to_np(F.linear(xd.reshape(T, H), blk.gate.weight))
     ids, w = O.route(logits, top)
     if T == 1:
         ref = O.decode_block(x, ids, w, bank, shared, gate_w, activation, dtype)
@@ -157,3 +191,29 @@ def test_blocks_from_converted_checkpoint(tmp_path):
         bank = (t['gate_up'][0], t['gate_up'][1], t['down'][0], t['down'][1])
         ref = O.moe_block(x, w, ids, bank, t['shared'], t['shared_gate'], BF16)
         assert rel_maxabs(to_np(out), ref) < 1e-2
+
+
+@pytest.mark.parametrize('T,E,top', [(2048, 256, 8), (300, 256, 8), (257, 64, 4)])
+def test_moe_block_router_vs_oracle(T, E, top):
+    """The whole block from the hidden states in one library call (router kernel with the
+    metadata's route counts when top == 8, then the expert block): the returned routing
+    is the router kernel's own, and the output is within 1e-2 of the oracle block on that
+    routing, most of it in the reference's exact rounding sequence."""
+    from localmoe35ba3b_b200.runtime import gpu_routes
+    dtype, H, I = BF16, 2048, 512
+    x, router_w, bank, shared, gate_w = _block_case(40 + T, T, E, H, I, top, dtype)
+    xd, rw = to_dev(x, dtype), to_dev(router_w, dtype)
+    dev = [torch.from_numpy(b).cuda() for b in bank]
+    sh = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()) for q, s in shared]
+    out, w, ids = gpu_routes.moe_block_router(xd, rw, top, dev, shared=sh, shared_gate_weight=to_dev(gate_w, dtype))
+    w1, ids1 = gpu_routes.router_topk_fused(xd, rw, top)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, ids1) and torch.equal(w, w1)
+    ref = O.moe_block(x, to_np(w), to_np(ids), bank, shared, gate_w, dtype)
+    got = to_np(out)
+    assert rel_maxabs(got, ref) < 1e-2
+    assert (got == ref).mean() > 0.5
+    # the same routing through the block that takes it as input gives the same bits
+    again = gpu_routes.moe_block(xd, w, ids, dev, shared=sh, shared_gate_weight=to_dev(gate_w, dtype))
+    torch.cuda.synchronize()
+    assert torch.equal(again, out)

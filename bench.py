@@ -537,9 +537,9 @@ def _graph_time(fn, iters, dev):
 
 
 def dense_leg(dev, peaks, iters=20):
-    """C4: W8A16 dense linear sweep K=2048, N in {512,2048,4096,8192}, M in {1,16,256,2048}
-    (and the W8A8 table GEMV at M=1).  Weight copies rotate so each iteration reads
-    weights from HBM (the pool of copies exceeds L2)."""
+    """C4: dense linear sweep K=2048, N in {512,2048,4096,8192}, M in {1,16,256,2048}, W8A16
+    and W8A8 (the table GEMV at M=1, the int8 tensor-core GEMM above).  Weight copies rotate
+    so each iteration reads weights from HBM (the pool of copies exceeds L2)."""
     from localmoe35ba3b_b200.operators import int8 as I8
     from localmoe35ba3b_b200.operators import w8a8 as W8
     K = 2048
@@ -567,6 +567,20 @@ def dense_leg(dev, peaks, iters=20):
         gbs = (wb + 2 * K + 2 * n) / (us * 1e-6) / 1e9
         out.append({'op': 'w8a8', 'M': 1, 'N': n, 'K': K, 'us': round(us, 2), 'gbs': round(gbs, 1), 'bound': 'hbm',
                     'frac': round(gbs / peaks['hbm'], 4)})
+        # W8A8 at M > 1: activation quantisation + the int8 tensor-core GEMM (int32 group dots);
+        # the tensor peak is taken as twice the measured bf16 one (int8 runs at twice the rate)
+        for m in (16, 256, 2048):
+            x = torch.randn((m, K), device=dev).bfloat16()
+            us = _graph_time(lambda i: W8.linear(x, qs[i % copies], ss[i % copies]), iters, dev)
+            flops = 2.0 * m * n * K
+            bytes_ = wb + 2 * m * K + 2 * m * n
+            tops, gbs = flops / (us * 1e-6) / 1e12, bytes_ / (us * 1e-6) / 1e9
+            pk_i8 = 2 * peaks['tc']
+            bound = 'tensor' if flops / (pk_i8 * 1e12) > bytes_ / (peaks['hbm'] * 1e9) else 'hbm'
+            frac = tops / pk_i8 if bound == 'tensor' else gbs / peaks['hbm']
+            out.append({'op': 'w8a8', 'M': m, 'N': n, 'K': K, 'us': round(us, 2), 'tops': round(tops, 2),
+                        'gbs': round(gbs, 1), 'bound': bound, 'frac': round(frac, 4),
+                        'peak': 'int8 = 2 x measured bf16' if bound == 'tensor' else 'measured HBM'})
         del qs, ss, tabs
     return out
 

@@ -72,6 +72,17 @@ LMOE_API int64_t lmoe_linear_w8a16_workspace_size(int64_t m, int64_t n, int64_t 
 LMOE_API int lmoe_linear_w8a16_ws(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n,
                                   int64_t k, int dtype, void* ws, int64_t ws_bytes, int* err, void* stream);
 
+/* Dense W8A8 linear for any number of rows m (BASELINE's dense sweep; the reference has the
+ * same arithmetic only as its one-row decode GEMV, qwen35_deploy/operators/w8a8.py:8-48):
+ * x [m, k] quantised per (row, 128-group) as w8a8.quantize, then on int8 tensor cores
+ * y[r, n] = round_dtype(acc), acc = acc + (float(dot_g) * xs[r, g]) * ws[n, g] over the
+ * groups g in order, dot_g the exact int32 group dot.  n % 128 == 0, k % 128 == 0,
+ * k <= 8192; ws: lmoe_linear_w8a8_workspace_size(m, k) bytes, 256-byte aligned (the
+ * quantised rows and their scales). */
+LMOE_API int64_t lmoe_linear_w8a8_workspace_size(int64_t m, int64_t k);
+LMOE_API int lmoe_linear_w8a8(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n,
+                              int64_t k, int dtype, void* ws, int* err, void* stream);
+
 /* Replaces int8.grouped_linear / int8._grouped_linear (qwen35_deploy/operators/int8.py:213-237).
  * table is a device int64 [experts, 5] of (gate_up.q, gate_up.scale, down.q, down.scale, slot);
  * field 0 selects the gate_up pair, field 2 the down pair.  Row e uses x row 0 when

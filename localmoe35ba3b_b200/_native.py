@@ -28,6 +28,8 @@ SIGNATURES = {
     'lmoe_linear_w8a16': (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _P]),
     'lmoe_linear_w8a16_workspace_size': (_I64, [_I64, _I64, _I64]),
     'lmoe_linear_w8a16_ws': (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _I64, _P, _P]),
+    'lmoe_linear_w8a8_workspace_size': (_I64, [_I64, _I64]),
+    'lmoe_linear_w8a8': (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _P, _P]),
     'lmoe_grouped_linear_w8a16': (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P]),
     'lmoe_grouped_linear_w8a8': (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P]),
     'lmoe_ordered_reduce': (_I, [_P, _P, _P, _P, _I64, _I64, _I, _P]),

@@ -55,6 +55,7 @@ int launch_dense_ts(const void* x, const int8_t* q, const float* scale, void* y,
 int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K);
 int make_int8_pair_map(CUtensorMap* m, const int8_t* base, int64_t experts, int64_t inter, int64_t K);
 int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int dtype, int box_rows);
+int make_i8_tile_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K);
 int sm_count();
 
 // out[r] = x[pos[r]] for r < rows; rows of k 16-bit elements (permute.cu)

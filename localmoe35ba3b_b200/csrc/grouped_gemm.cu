@@ -539,6 +539,21 @@ int make_int8_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K) {
   return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
 }
 
+// int8 [rows, K] with a 128-row x 128-byte, 128B-swizzled box (the W8A8 GEMM's tiles)
+int make_i8_tile_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t K) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LMOE_ERR_CUDA;
+  if (((uintptr_t)base & 15) || (K % 128) || rows <= 0) return LMOE_ERR_INVALID;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K};
+  cuuint32_t box[2] = {128, 128};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)base, dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LMOE_OK : LMOE_ERR_CUDA;
+}
+
 // gate_up bank [E, 2I, K] int8 viewed as [2E][I][K]: box 2 x 64 rows x 128 bytes, 128-byte
 // swizzle -- the 64 gate rows and the matching 64 up rows of one output block in one copy
 int make_int8_pair_map(CUtensorMap* m, const int8_t* base, int64_t experts, int64_t inter, int64_t K) {

@@ -2,7 +2,10 @@
 
 ``quantize`` -- per-(row, 128-group) absmax int8 activations (w8a8.py:17-22);
 ``grouped_linear`` -- the table-driven int8 GEMV with per-group rescale
-(w8a8.py:44-48); it quantises inside the GEMV launch.
+(w8a8.py:44-48); it quantises inside the GEMV launch;
+``linear`` -- the same arithmetic for a dense linear of any number of rows on int8
+tensor cores (the dense sweep's W8A8 half; the reference has it only as the one-row
+GEMV).
 """
 import torch
 
@@ -32,3 +35,27 @@ def grouped_linear(x, table, experts, n, field, shared, return_quantized=False):
     N.call('lmoe_grouped_linear_w8a8', N.ptr(x), N.ptr(table), N.ptr(out), experts, n, k, field,
            1 if shared else 0, N.dtype_code(x.dtype), N.ptr(xq), N.ptr(xs), N.stream(x.device))
     return (out, xq, xs) if return_quantized else out
+
+
+def linear(x, q, scale):
+    """``y = W8A8(x) . W^T`` for ``x [..., K]`` (FP16/BF16, CUDA), ``q [N, K]`` int8 and
+    ``scale [N, K/128]`` fp32: each row of x quantised as ``quantize``, exact int32 dots
+    per 128-group on tensor cores, ``acc = acc + (float(dot) * xs) * ws`` in group order
+    (w8a8.py:37-40), rounded once to ``x.dtype``.  N must be a multiple of 128."""
+    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError('W8A8 requires CUDA FP16/BF16 activations')
+    n, k = q.shape
+    if k % 128 or x.shape[-1] != k or tuple(scale.shape) != (n, k // 128) or n % 128:
+        raise ValueError('Invalid INT8 group geometry')
+    if not (q.is_cuda and scale.is_cuda and q.dtype == torch.int8 and scale.dtype == torch.float32
+            and q.is_contiguous() and scale.is_contiguous()):
+        raise ValueError('Expected contiguous CUDA int8 weights with float32 group scales')
+    x = x.contiguous()
+    m = x.numel() // k
+    out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=x.dtype)
+    if m == 0:
+        return out
+    ws = N.workspace(x.device, N.lib().lmoe_linear_w8a8_workspace_size(m, k), 'w8a8')
+    N.call('lmoe_linear_w8a8', N.ptr(x), N.ptr(q), N.ptr(scale), N.ptr(out), m, n, k, N.dtype_code(x.dtype),
+           N.ptr(ws), N.ptr(N.error_word(x.device)), N.stream(x.device))
+    return out

@@ -407,3 +407,23 @@ def test_swiglu_silu_matches_exact_division_for_every_input(dtype):
     cnt = torch.zeros(1, dtype=torch.int32, device='cuda')
     N.call('lmoe_selftest_silu', N.dtype_code(TORCH_DT[dtype]), N.ptr(cnt), N.stream(cnt.device))
     assert int(cnt.item()) == 0
+
+
+@pytest.mark.parametrize('dtype', [BF16, F16])
+@pytest.mark.parametrize('M,N,K', [(1, 512, 2048), (16, 2048, 2048), (130, 1024, 1024), (256, 512, 4096),
+                                   (2048, 1024, 2048)])
+def test_linear_w8a8_tensor_core_bit_exact(dtype, M, N, K):
+    """The dense W8A8 linear on int8 tensor cores: the activation quantisation and the
+    int32 group dots are exact, the rescale (float(dot) * xs) * ws is added in group order,
+    so the output equals the oracle's restatement of the reference's W8A8 arithmetic bit
+    for bit (and stays within the W8A8 error class of an fp32 dequantise-then-matmul)."""
+    from localmoe35ba3b_b200.operators import w8a8
+    r = rng(90 + M + K)
+    q, s = rand_q(r, (N, K))
+    x = act(r, (M, K), dtype)
+    y = w8a8.linear(to_dev(x, dtype), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda())
+    torch.cuda.synchronize()
+    xq, xs = O.quantize_act(x)
+    ref = O.linear_w8a8(xq, xs, q, s, dtype)
+    assert np.array_equal(to_np(y), ref)
+    assert rel_maxabs(to_np(y), O.linear_fp32_reference(x, q, s)) < 3e-2

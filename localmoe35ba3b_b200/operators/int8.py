@@ -13,10 +13,14 @@ import torch
 from .. import _native as N
 
 
-def _check_weight(q, scale):
-    if not (q.is_cuda and scale.is_cuda and q.dtype == torch.int8 and scale.dtype == torch.float32
-            and q.is_contiguous() and scale.is_contiguous()):
-        raise ValueError('Expected contiguous CUDA int8 weights with float32 group scales')
+def _weights(q, scale):
+    """The weight and its group scales as the library reads them.  The reference's kernel
+    indexes both as contiguous row-major tensors without checking, so a strided view is
+    made contiguous here rather than refused; only a weight the library cannot read at all
+    (not CUDA int8 with float32 scales) raises."""
+    if not (q.is_cuda and scale.is_cuda and q.dtype == torch.int8 and scale.dtype == torch.float32):
+        raise ValueError('Expected CUDA int8 weights with float32 group scales')
+    return q.contiguous(), scale.contiguous()
 
 
 def linear(x, q, scale, large_tile=False):
@@ -27,7 +31,7 @@ def linear(x, q, scale, large_tile=False):
     n, k = q.shape
     if k % 128 or x.shape[-1] != k or tuple(scale.shape) != (n, k // 128):
         raise ValueError('Invalid INT8 group geometry')
-    _check_weight(q, scale)
+    q, scale = _weights(q, scale)
     x = x.contiguous()
     m = x.numel() // k
     out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=x.dtype)

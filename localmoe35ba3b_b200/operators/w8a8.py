@@ -47,10 +47,9 @@ def linear(x, q, scale):
     n, k = q.shape
     if k % 128 or x.shape[-1] != k or tuple(scale.shape) != (n, k // 128) or n % 128:
         raise ValueError('Invalid INT8 group geometry')
-    if not (q.is_cuda and scale.is_cuda and q.dtype == torch.int8 and scale.dtype == torch.float32
-            and q.is_contiguous() and scale.is_contiguous()):
-        raise ValueError('Expected contiguous CUDA int8 weights with float32 group scales')
-    x = x.contiguous()
+    if not (q.is_cuda and scale.is_cuda and q.dtype == torch.int8 and scale.dtype == torch.float32):
+        raise ValueError('Expected CUDA int8 weights with float32 group scales')
+    q, scale, x = q.contiguous(), scale.contiguous(), x.contiguous()
     m = x.numel() // k
     out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=x.dtype)
     if m == 0:

@@ -244,6 +244,24 @@ def test_linear_w8a16(dtype, M, N, K):
     assert rel_maxabs(to_np(y), O.linear_fp32_reference(x, q, s)) < 1e-2
 
 
+def test_linear_strided_weight_views():
+    """Strided views of the weight and its scales (columns of wider tensors) are read as
+    the reference's kernel reads its arguments, row-major: the result equals the call on
+    contiguous copies, for the W8A16 and the W8A8 linear."""
+    from localmoe35ba3b_b200.operators import int8, w8a8
+    r = rng(71)
+    N, K = 512, 1024
+    q, s = rand_q(r, (N, 2 * K))
+    x = to_dev(act(r, (20, K), BF16), BF16)
+    qw, sw = torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    qv, sv = qw[:, K:], sw[:, K // 128:]
+    assert not qv.is_contiguous() and not sv.is_contiguous()
+    for op in (int8.linear, w8a8.linear):
+        assert torch.equal(op(x, qv, sv), op(x, qv.contiguous(), sv.contiguous()))
+    with pytest.raises(ValueError, match='Expected CUDA int8 weights with float32 group scales'):
+        int8.linear(x, qv.cpu(), sv)
+
+
 @pytest.mark.parametrize('M,N,K', [(3, 1024, 2048), (64, 512, 1024)])
 def test_linear_w8a16_without_workspace_matches_split_k(M, N, K):
     """lmoe_linear_w8a16 (no workspace: K not split) and lmoe_linear_w8a16_ws (K split over

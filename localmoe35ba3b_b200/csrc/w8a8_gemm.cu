@@ -189,6 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     typename A::T* y = (typename A::T*)p.y;
     int gi = 0, ui = 0;
     bool ok = true;
+    // the activation scales read below are the previous kernel's (the quantiser's) output
+    grid_dep_wait();
     // every epilogue warp walks every unit and reaches both named barriers of each, also
     // after an abort (then skipping the work), so that none can wait at a barrier for good
     for (int64_t u = blockIdx.x; u < units; u += stride, ++ui) {
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 64; ++j) acc[j] = 0.f;
       for (int g = 0; g < G && ok; ++g, ++gi) {
         const int b = gi & 1;
-        const float xsg = __ldg(xsr + g);
+        const float xsg = xsr[g];
         if (lane == 0) have = mbar_wait(tfull(b), (gi >> 1) & 1, sAbort, p.err) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, have, 0)) {
           ok = false;

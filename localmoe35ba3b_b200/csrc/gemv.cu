@@ -40,6 +40,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) grouped_gemv_kernel(
     int64_t experts, int64_t n, int64_t k, int field, int shared, int8_t* __restrict__ xq_out,
     float* __restrict__ xs_out) {
   extern __shared__ __align__(16) uint8_t smem[];
+  // launched as a programmatic dependent: x and the descriptor table may be the previous
+  // kernel's output, so nothing is read before it completes; the next kernel may launch at
+  // once (it waits for this one before reading y)
+  grid_dep_launch();
+  grid_dep_wait();
   const int groups = (int)(k / kGroup);
   const int64_t row0 = (int64_t)blockIdx.x * kGemvWarps;  // flat (expert, n) row of warp 0
   const int lane = lane_id(), warp = warp_id();
@@ -94,29 +99,45 @@ __global__ void __launch_bounds__(kGemvWarps * 32) grouped_gemv_kernel(
 
 // ----------------------------------------------------------------------------
 // Dense W8A16 GEMV for m <= kDenseMaxM rows: one warp per weight row, the
-// dequantised weights are reused for all m activation rows.
+// dequantised weights are reused for all m activation rows.  Launched as a
+// programmatic dependent: the weight rows do not depend on the previous kernel, so
+// each warp requests its first chunks before waiting for it; the m activation rows
+// (which may be that kernel's output) are read after the wait with ordinary loads,
+// never through the read-only path.  The next kernel may launch at once: it waits for
+// this one before reading y.
 constexpr int kDenseMaxM = 16;
 
 template <int DT, int MM>
 __global__ void __launch_bounds__(kGemvWarps * 32) dense_gemv_w8a16_kernel(
     const typename Act<DT>::T* __restrict__ x, const int8_t* __restrict__ q, const float* __restrict__ scale,
     typename Act<DT>::T* __restrict__ y, int m, int64_t n, int64_t k) {
+  using T = typename Act<DT>::T;
   const int lane = lane_id();
   const int64_t nn = (int64_t)blockIdx.x * kGemvWarps + warp_id();
-  if (nn >= n) return;
+  const bool live = nn < n;
   const int groups = (int)(k / kGroup);
   const int chunks = (int)(k / 16);
-  const int8_t* wrow = q + nn * k;
-  const float* srow = scale + nn * groups;
+  const int8_t* wrow = q + (live ? nn : 0) * k;
+  const float* srow = scale + (live ? nn : 0) * groups;
+  grid_dep_launch();
+  uint4 w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = lane + 32 * i;
+    if (live && c < chunks) w[i] = ldg_stream(wrow + c * 16);
+  }
+  grid_dep_wait();
+  if (!live) return;
   float acc[MM];
 #pragma unroll
   for (int r = 0; r < MM; ++r) acc[r] = 0.f;
   for (int c0 = 0; c0 < chunks; c0 += 32 * 4) {
-    uint4 w[4];
+    if (c0 > 0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int c = c0 + lane + 32 * i;
-      if (c < chunks) w[i] = ldg_stream(wrow + c * 16);
+      for (int i = 0; i < 4; ++i) {
+        const int c = c0 + lane + 32 * i;
+        if (c < chunks) w[i] = ldg_stream(wrow + c * 16);
+      }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -137,9 +158,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) dense_gemv_w8a16_kernel(
 #pragma unroll
       for (int r = 0; r < MM; ++r) {
         if (r >= m) break;
-        const typename Act<DT>::T* xv = x + (int64_t)r * k + c * 16;
-        const uint4 xa = __ldg(reinterpret_cast<const uint4*>(xv));
-        const uint4 xb = __ldg(reinterpret_cast<const uint4*>(xv + 8));
+        const uint4* xv = reinterpret_cast<const uint4*>(x + (int64_t)r * k + c * 16);
+        const uint4 xa = xv[0], xb = xv[1];
         const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -244,13 +264,13 @@ static int launch_grouped(const void* x, const int64_t* table, void* y, int64_t 
   if (dtype == LMOE_BF16) {
     auto kern = grouped_gemv_kernel<LMOE_BF16, W8A8>;
     if (smem > 48 * 1024) LMOE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<blocks, kGemvWarps * 32, smem, st>>>((const __nv_bfloat16*)x, table, (__nv_bfloat16*)y, experts, n, k, field,
-                                                shared, xq, xs);
+    LMOE_CUDA_CHECK(launch_pdl(kern, dim3(blocks), dim3(kGemvWarps * 32), smem, st, (const __nv_bfloat16*)x, table,
+                               (__nv_bfloat16*)y, experts, n, k, field, shared, xq, xs));
   } else if (dtype == LMOE_F16) {
     auto kern = grouped_gemv_kernel<LMOE_F16, W8A8>;
     if (smem > 48 * 1024) LMOE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<blocks, kGemvWarps * 32, smem, st>>>((const __half*)x, table, (__half*)y, experts, n, k, field, shared, xq,
-                                                xs);
+    LMOE_CUDA_CHECK(launch_pdl(kern, dim3(blocks), dim3(kGemvWarps * 32), smem, st, (const __half*)x, table,
+                               (__half*)y, experts, n, k, field, shared, xq, xs));
   } else {
     return LMOE_ERR_INVALID;
   }
@@ -282,14 +302,19 @@ extern "C" int lmoe_grouped_linear_w8a8(const void* x, const int64_t* table, voi
 int lmoe_dense_gemv_w8a16(const void* x, const int8_t* q, const float* scale, void* y, int64_t m, int64_t n,
                           int64_t k, int dtype, cudaStream_t st) {
   if (m <= 0 || m > kDenseMaxM) return LMOE_ERR_INVALID;
+  const size_t smem = 0;
+  if ((uintptr_t)x & 15) return LMOE_ERR_INVALID;
   const unsigned blocks = (unsigned)((n + kGemvWarps - 1) / kGemvWarps);
 #define LMOE_DENSE_CASE(MM)                                                                                      \
-  if (dtype == LMOE_BF16)                                                                                        \
-    dense_gemv_w8a16_kernel<LMOE_BF16, MM><<<blocks, kGemvWarps * 32, 0, st>>>(                                  \
-        (const __nv_bfloat16*)x, q, scale, (__nv_bfloat16*)y, (int)m, n, k);                                     \
-  else                                                                                                           \
-    dense_gemv_w8a16_kernel<LMOE_F16, MM><<<blocks, kGemvWarps * 32, 0, st>>>((const __half*)x, q, scale,        \
-                                                                              (__half*)y, (int)m, n, k);
+  if (dtype == LMOE_BF16) {                                                                                      \
+    auto kern = dense_gemv_w8a16_kernel<LMOE_BF16, MM>;                                                          \
+    LMOE_CUDA_CHECK(launch_pdl(kern, dim3(blocks), dim3(kGemvWarps * 32), smem, st, (const __nv_bfloat16*)x, q,  \
+                               scale, (__nv_bfloat16*)y, (int)m, n, k));                                         \
+  } else {                                                                                                       \
+    auto kern = dense_gemv_w8a16_kernel<LMOE_F16, MM>;                                                           \
+    LMOE_CUDA_CHECK(launch_pdl(kern, dim3(blocks), dim3(kGemvWarps * 32), smem, st, (const __half*)x, q, scale,  \
+                               (__half*)y, (int)m, n, k));                                                       \
+  }
   if (m == 1) {
     LMOE_DENSE_CASE(1)
   } else if (m <= 4) {

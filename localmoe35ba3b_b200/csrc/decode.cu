@@ -223,8 +223,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
   auto expect_gu = [&](int blk) {
     const uint32_t wbytes = (uint32_t)(8 * H), sbytes = (uint32_t)(8 * GH * 4);
     if (lane < npieces) mbar_arrive_expect_tx(bars + 8u * lane, 2 * (wbytes + sbytes));
+    // (the first block's shared slice is armed and requested before the dependency wait)
     const int ns = sh_cols(blk);
-    if (lane == 0 && ns > 0) mbar_arrive_expect_tx(bar_sh, (uint32_t)(2 * ns * (H + GH * 4)));
+    if (lane == 0 && ns > 0 && blk != (int)blockIdx.x) mbar_arrive_expect_tx(bar_sh, (uint32_t)(2 * ns * (H + GH * 4)));
   };
   auto copy_gu = [&](int blk, int k) {
     const int r = blk / nblk;
@@ -291,13 +292,26 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
     for (int k = lane; k < n_dn_copies; k += 32) copy_dn(blk, k);
   };
 
+  const bool has_gu = (int)blockIdx.x < a.n_gu, has_dn = (int)blockIdx.x < a.n_dn;
+  // the shared expert's rows depend on nothing the previous kernel writes: this CTA's first
+  // slice of them is requested, and its shared down rows pulled towards L2, before waiting
+  const int ns0 = has_gu ? sh_cols(blockIdx.x) : 0;
+  if (threadIdx.x == 0) {
+    if (ns0 > 0) {
+      mbar_arrive_expect_tx(bar_sh, (uint32_t)(2 * ns0 * (H + GH * 4)));
+      for (int k = 4 * npieces; k < n_gu_copies; ++k) copy_gu(blockIdx.x, k);
+    }
+    if (has_dn && with_shared) {
+      prefetch_dn(blockIdx.x, 2 * top);
+      prefetch_dn(blockIdx.x, 2 * top + 1);
+    }
+  }
   // launched so that it may start before the previous kernel ends: the ids, the
   // routing weights, x and the hidden buffer (which the previous call reads) all
   // wait for it
   grid_dep_wait();
   int8_t* xq = reinterpret_cast<int8_t*>(smem + G.xq);
   float* xs = reinterpret_cast<float*>(smem + G.xs);
-  const bool has_gu = (int)blockIdx.x < a.n_gu, has_dn = (int)blockIdx.x < a.n_dn;
   if (warp == 0) {
     // the experts' order and their routing weights; arm the first block's barriers
     expert_ranks_w(a.ids, a.weights, top, a.E, s_eid, s_w, a.err, blockIdx.x == 0);
@@ -311,16 +325,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const Laye
     }
   }
   __syncthreads();
-  // the first block's copies, one warp each
+  // the first block's routed copies, one warp each
   if (lane == 0 && has_gu)
-    for (int k = warp; k < n_gu_copies; k += kDecWarps) copy_gu(blockIdx.x, k);
+    for (int k = warp; k < 4 * npieces; k += kDecWarps) copy_gu(blockIdx.x, k);
   __syncwarp();
   // every warp quantises groups of x (W8A8) and forms part of the shared gate's logit;
   // then the first down block's L2 prefetches (needed only after the grid barrier)
   if (W8A8)
     for (int g = warp; g < GH; g += kDecWarps) quant_group<DT>(x + g * kGroup, xq + g * kGroup, xs + g, lane);
   if (lane == 0 && has_dn)
-    for (int k = warp; k < n_dn_copies; k += kDecWarps) prefetch_dn(blockIdx.x, k);
+    for (int k = warp; k < 2 * top; k += kDecWarps) prefetch_dn(blockIdx.x, k);
   __syncwarp();
   if (gated && warp > 0) {
     const T* gw = (const T*)a.gate_w;

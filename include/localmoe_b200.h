@@ -14,6 +14,13 @@
  *  - no entry point allocates device memory: scratch ("workspace") buffers are
  *    passed in by the caller, sized by the *_workspace_size functions
  *    (lmoe_routed_moe_noalloc uses a fixed array inside the library instead);
+ *  - most kernels are launched as programmatic dependents of the work before
+ *    them on the stream and let the next kernel launch early: a library kernel
+ *    reads its inputs only after that work has completed, and a caller's own
+ *    kernel launched with programmatic stream serialization after a library
+ *    call must wait (griddepcontrol.wait / cudaGridDependencySynchronize)
+ *    before reading the call's outputs, as for any programmatic dependent;
+ *    ordinary launches, copies and events need nothing;
  *  - the return value is LMOE_OK or a negative LMOE_ERR_* code (invalid
  *    geometry or a CUDA launch error); nothing aborts or traps.  Device-side
  *    bounded waits that give up set LMOE_DEVERR_* bits in the caller's
